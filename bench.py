@@ -1,0 +1,450 @@
+#!/usr/bin/env python
+"""Benchmark of the causal attention hot path (flashAttentionForward ->
+computeD -> flashAttentionBackward) on B200, one process per GPU.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2]
+    python bench.py --impl reference ...     # the CPU implementation of the path
+
+A step is one pass of the path over one batch of the workload: forward,
+computeD and backward of every (batch, head) shard the rank owns.  At N GPUs
+each rank owns a full config-2 batch of shards (B=64, T=1024, H=12, d=64), so
+the global job is N x config 2 ("weak" scaling) and no data-path collective
+exists: the ranks only meet in the timing barrier and the max-over-ranks
+reduction.  Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import signal
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from metalllm_b200.inputs import CONFIGS, attention_inputs, causal_flops  # noqa: E402
+
+METRIC = "causal bf16 FlashAttn fwd+bwd TFLOP/s per GPU, % tensor peak, at 1/2/4/8 GPUs"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def env_int(name, default):
+    v = os.environ.get(name)
+    return int(v) if v not in (None, "") else default
+
+
+def workload_desc(cfg):
+    c = CONFIGS[cfg]
+    return f"{cfg}: causal attention fwd+bwd B={c['B']} T={c['T']} H={c['H']} d={c['D']} bf16"
+
+
+# --------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling during the timed region."""
+
+    FIELDS = ("index,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, bus_id: str):
+        self.bus_id = bus_id.upper()
+        self.proc = None
+        self.tmp = None
+
+    def start(self):
+        try:
+            self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.tmp, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.send_signal(signal.SIGTERM)
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.tmp.flush()
+        rows = []
+        for line in Path(self.tmp.name).read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 10:
+                continue
+            if not parts[1].upper().endswith(self.bus_id[-12:]):
+                continue
+            rows.append(parts)
+        os.unlink(self.tmp.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        mx = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
+        reasons = set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for r in rows:
+            for name, val in zip(names, r[6:10]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+# ------------------------------------------------------------ GPU arm
+def run_gpu(args):
+    import torch
+    import torch.distributed as dist
+
+    from metalllm_b200 import _lib
+    from metalllm_b200 import attention as A
+
+    world = env_int("WORLD_SIZE", 1)
+    rank = env_int("RANK", 0)
+    local = env_int("LOCAL_RANK", 0)
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    lib = _lib.load()
+
+    c = CONFIGS[args.config]
+    B, T, H, D = c["B"], c["T"], c["H"], c["D"]
+    p = A.make_params(T, H, D)
+    # this rank's shards: batch rows [rank*B, (rank+1)*B) of the global N*B batch
+    host = attention_inputs(B, T, H, D, seed=args.seed + rank, qkv_scale=c["qkv_scale"],
+                            do_scale=c["do_scale"])
+
+    def pinned(bits):
+        t = torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16)
+        return t.pin_memory()
+
+    h_q, h_k, h_v, h_do = (pinned(host[n]) for n in ("q", "k", "v", "do"))
+    act = (B, T, H * D)
+    q, k, v, do = (t.to(dev) for t in (h_q, h_k, h_v, h_do))
+    out = torch.empty(act, dtype=torch.bfloat16, device=dev)
+    l = torch.empty((B, T, H), dtype=torch.float32, device=dev)
+    Dv = torch.empty((B, T, H), dtype=torch.bfloat16, device=dev)
+    dQ = torch.empty(act, dtype=torch.float32, device=dev)
+    dK = torch.empty(act, dtype=torch.bfloat16, device=dev)
+    dV = torch.empty(act, dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    fwd_flops, bwd_flops = causal_flops(B, T, H, D)
+    step_flops = fwd_flops + bwd_flops
+
+    def step(ev=None):
+        if ev is not None:
+            ev[0].record(stream)
+        A.flashAttentionForward(q, k, v, p, B, out=out, l=l, stream=stream)
+        if ev is not None:
+            ev[1].record(stream)
+        A.computeD(do, out, p, B, D=Dv, stream=stream)
+        if ev is not None:
+            ev[2].record(stream)
+        A.flashAttentionBackward(do, Dv, l, q, k, v, p, B, dQ=dQ, dK=dK, dV=dV, stream=stream)
+        if ev is not None:
+            ev[3].record(stream)
+
+    def barrier():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- warm-up
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    if A.device_status(stream) != 0:
+        raise RuntimeError("a kernel reported a timeout during warm-up")
+
+    # ---- timed region (device time, CUDA events on the launching stream)
+    props = torch.cuda.get_device_properties(dev)
+    bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+    sampler = ClockSampler(bus)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    sampler.start()
+    time.sleep(0.3)
+    launches0 = lib.ma_kernel_launch_count()
+    barrier()
+    start.record(stream)
+    for i in range(args.steps):
+        step(evs[i])
+    stop.record(stream)
+    barrier()
+    launches = lib.ma_kernel_launch_count() - launches0
+    clocks = sampler.stop()
+    elapsed_ms = start.elapsed_time(stop)
+    fwd_ms = [e[0].elapsed_time(e[1]) for e in evs]
+    d_ms = [e[1].elapsed_time(e[2]) for e in evs]
+    bwd_ms = [e[2].elapsed_time(e[3]) for e in evs]
+    if A.device_status(stream) != 0:
+        raise RuntimeError("a kernel reported a timeout during the timed region")
+    elapsed_ms = max_over_ranks(elapsed_ms)
+    ms_per_step = elapsed_ms / args.steps
+    total_flops = step_flops * world * args.steps
+    value = total_flops / (elapsed_ms * 1e-3) / 1e12
+
+    # ---- end to end through the public API with host buffers (pinned)
+    h_out = torch.empty(act, dtype=torch.bfloat16).pin_memory()
+    h_l = torch.empty((B, T, H), dtype=torch.float32).pin_memory()
+    h_dQ = torch.empty(act, dtype=torch.float32).pin_memory()
+    h_dK = torch.empty(act, dtype=torch.bfloat16).pin_memory()
+    h_dV = torch.empty(act, dtype=torch.bfloat16).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in (h_q, h_k, h_v, h_do))
+    d2h = sum(t.numel() * t.element_size() for t in (h_out, h_l, h_dQ, h_dK, h_dV))
+
+    def e2e_step():
+        with torch.cuda.stream(stream):
+            for dst, src in ((q, h_q), (k, h_k), (v, h_v), (do, h_do)):
+                dst.copy_(src, non_blocking=True)
+        step()
+        with torch.cuda.stream(stream):
+            for dst, src in ((h_out, out), (h_l, l), (h_dQ, dQ), (h_dK, dK), (h_dV, dV)):
+                dst.copy_(src, non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 10))
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    e2e_value = step_flops * world * e2e_steps / (e2e_ms * 1e-3) / 1e12
+
+    # ---- roofline of the dominant kernel (backward: 5/7 of the FLOPs)
+    peaks, peak_src = load_peaks()
+    timed_s = elapsed_ms * 1e-3
+    peak_kind = "sustained" if timed_s >= 1.0 else "burst"
+    peak = peaks["bf16_tflops_sustained"] if peak_kind == "sustained" else peaks["bf16_tflops"]
+    bwd_avg = statistics.mean(bwd_ms)
+    fwd_avg = statistics.mean(fwd_ms)
+    d_avg = statistics.mean(d_ms)
+    bwd_tflops = bwd_flops / (bwd_avg * 1e-3) / 1e12
+    fwd_tflops = fwd_flops / (fwd_avg * 1e-3) / 1e12
+    d_bytes = 2 * (B * T * H * D) * 2 + B * T * H * 2
+    d_gbs = d_bytes / (d_avg * 1e-3) / 1e9
+    traffic = None
+    tfile = ROOT / "profiles" / "traffic.json"
+    if tfile.exists():
+        tr = json.loads(tfile.read_text())
+        ent = tr.get(f"{args.config}/flash_bwd")
+        if ent:
+            traffic = ent.get("bytes_per_launch")
+    roofline = {
+        "kernel": "flashAttentionBackward",
+        "bound": "tensor", "achieved": round(bwd_tflops, 2), "peak": peak, "unit": "TFLOP/s",
+        "frac": round(bwd_tflops / peak, 4), "traffic": traffic,
+        "peak_source": f"{peak_src} {peak_kind} bf16 (MEASURED_PEAKS.json)" if peak_src == "measured"
+        else f"fallback {peak_kind}",
+        "algorithmic_flops_per_launch": bwd_flops,
+    }
+    extra_kernels = {
+        "flashAttentionForward": {"ms": round(fwd_avg, 4), "tflops": round(fwd_tflops, 2),
+                                  "frac": round(fwd_tflops / peak, 4)},
+        "computeD": {"ms": round(d_avg, 4), "gbs": round(d_gbs, 1),
+                     "frac_hbm": round(d_gbs / peaks["hbm_gbs"], 4), "bytes": d_bytes},
+        "flashAttentionBackward": {"ms": round(bwd_avg, 4), "tflops": round(bwd_tflops, 2),
+                                   "frac": round(bwd_tflops / peak, 4)},
+    }
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args.config, args.seed, budget_s=args.cpu_seconds)
+
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC,
+        "value": round(value, 3),
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: Q,K,V,dO i.i.d. normal (splitmix64 + Box-Muller, seed %d), bf16" % args.seed,
+        "config": {
+            "workload": workload_desc(args.config),
+            "B_per_gpu": B, "T": T, "H": H, "d": D, "causal": True,
+            "global_batch": B * world,
+            "parallelism": f"(batch x head) shards, {B * H} per GPU, no collective",
+            "l2": "inputs larger than L2 (Q,K,V,dO = %.1f MB per step > 126 MB)" % (4 * B * T * H * D * 2 / 1e6),
+            "flops_convention": "fwd 2*B*H*T^2*d + bwd 5*B*H*T^2*d (causal T^2/2 pairs)",
+        },
+        "per_gpu_tflops": round(value / world, 3),
+        "frac_of_peak": round(value / world / peak, 4),
+        "clocks": clocks,
+        "e2e": {"value": round(e2e_value, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h,
+                "note": "pinned host Q,K,V,dO -> device, fwd+computeD+bwd, O,l,dQ,dK,dV -> host"},
+        "gpu_launches": int(launches),
+        "roofline": roofline,
+        "kernels": extra_kernels,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------- CPU (reference) arm
+def _cpu_sample(cfg, seed, nshards):
+    """Inputs of the first `nshards` (batch, head) shards of the config as
+    single-head arrays [nshards, T, d] (bit-identical to the GPU's shards)."""
+    c = CONFIGS[cfg]
+    B, T, H, D = c["B"], c["T"], c["H"], c["D"]
+    nb = min(B, (nshards + H - 1) // H)
+    x = attention_inputs(nb, T, H, D, seed=seed, qkv_scale=c["qkv_scale"], do_scale=c["do_scale"])
+    out = {}
+    for name, arr in x.items():
+        heads = arr.reshape(nb, T, H, D).transpose(0, 2, 1, 3).reshape(nb * H, T, D)[:nshards]
+        out[name] = np.ascontiguousarray(heads).reshape(nshards, T, D)
+    return out
+
+
+def cpu_step(o, x, nthreads):
+    """One pass of the path on the CPU oracle over single-head shards."""
+    out, lse = o.flash_forward(x["q"], x["k"], x["v"], 1, nthreads=nthreads)
+    Dv = o.compute_d(x["do"], out, 1, nthreads=nthreads)
+    o.flash_backward(x["do"], Dv, lse, x["q"], x["k"], x["v"], 1, nthreads=nthreads)
+
+
+def cpu_baseline(cfg, seed, budget_s=15.0, nthreads=0):
+    """Times the oracle port (the CPU restatement of attention.metal:56-299) on
+    a bounded sample of the config's shards, all host threads."""
+    from oracle import oracle as o
+    o.load()
+    nthreads = nthreads or (os.cpu_count() or 1)
+    c = CONFIGS[cfg]
+    T, D = c["T"], c["D"]
+    per_shard = sum(causal_flops(1, T, 1, D))
+    # calibrate on one shard per thread, then size the sample to the budget
+    n = max(1, nthreads)
+    x = _cpu_sample(cfg, seed, n)
+    t0 = time.perf_counter()
+    cpu_step(o, x, nthreads)
+    t1 = time.perf_counter() - t0
+    n2 = max(n, int(n * max(1.0, budget_s / max(t1, 1e-3))))
+    n2 = min(n2, c["B"] * c["H"])
+    x = _cpu_sample(cfg, seed, n2)
+    t0 = time.perf_counter()
+    cpu_step(o, x, nthreads)
+    t2 = time.perf_counter() - t0
+    val = per_shard * n2 / t2 / 1e12
+    return {"value": round(val, 6), "unit": "TFLOP/s", "cores": nthreads, "kind": "port",
+            "sample": f"{n2} of {c['B'] * c['H']} (batch, head) shards of {cfg} "
+                      f"(T={T}, d={D}), fwd+computeD+bwd, {t2:.2f} s"}
+
+
+def run_reference(args):
+    rank = env_int("RANK", 0)
+    if rank != 0:
+        return
+    from oracle import oracle as o
+    o.load()
+    nthreads = os.cpu_count() or 1
+    c = CONFIGS[args.config]
+    T, D = c["T"], c["D"]
+    per_shard = sum(causal_flops(1, T, 1, D))
+    # size one step to ~target seconds
+    target = max(0.5, min(6.0, 150.0 / max(1, args.steps + args.warmup)))
+    x = _cpu_sample(args.config, args.seed, nthreads)
+    t0 = time.perf_counter()
+    cpu_step(o, x, nthreads)
+    t1 = time.perf_counter() - t0
+    n = max(nthreads, int(nthreads * target / max(t1, 1e-3)))
+    n = min(n, c["B"] * c["H"])
+    x = _cpu_sample(args.config, args.seed, n)
+    for _ in range(max(0, args.warmup - 1)):
+        cpu_step(o, x, nthreads)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        cpu_step(o, x, nthreads)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    val = per_shard * n * args.steps / total / 1e12
+    sample = (f"each step: {n} of {c['B'] * c['H']} (batch, head) shards of {args.config} "
+              f"(T={T}, d={D}), fwd+computeD+bwd")
+    line = {
+        "impl": "reference",
+        "metric": METRIC, "value": round(val, 6), "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(total / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16 in/out, fp32 math",
+        "data": "synthetic (same generator and seed as the GPU arm)",
+        "config": {"workload": workload_desc(args.config), "B_per_gpu": c["B"], "T": T, "H": c["H"],
+                   "d": D, "causal": True},
+        "cpu_baseline": {"value": round(val, 6), "unit": "TFLOP/s", "cores": nthreads,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(val, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": ("The reference runs only on Apple Metal (unavailable on this box); this arm "
+                 "times its scalar multithreaded C++ restatement (oracle/attn_oracle.cpp)."),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--impl", default="native", choices=["native", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    # at least 3 untimed warm-up steps, whatever the caller asks for
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

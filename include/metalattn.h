@@ -1,0 +1,143 @@
+/*
+ * metalattn.h -- C ABI of the B200 (sm_100a) causal attention hot path of
+ * metalLLM.  Each entry point replaces one Metal kernel dispatch of the
+ * reference and keeps that kernel's buffer order, buffer layouts and dtypes.
+ *
+ * Layouts (row-major, a batch of B sequences stacked along the row axis):
+ *   X, Q, K, V, O (attnOut), dO (dZAttn), dK, dV : bf16 [B][M][N]
+ *   dQ                                           : fp32 [B][M][N]
+ *   l (row logsumexp)                            : fp32 [B][M][NH]
+ *   D (rowsum(dO*O))                             : bf16 [B][M][NH]
+ *   Wq, Wk, Wv                                   : bf16 [N][N], row = input feature
+ * where M = sequence length, N = NH*D, and head h owns columns h*D .. h*D+D-1.
+ *
+ * Conventions shared by every entry point:
+ *   - Pointers are device pointers on the current CUDA device, 16-byte aligned.
+ *   - Work is enqueued on `stream` (NULL = legacy default stream); nothing
+ *     synchronises the host.  Results are ready when the stream is.
+ *   - The return value is MA_OK or an MA_ERR_* code; ma_last_error_string()
+ *     describes the last failure of the calling host thread.  No entry point
+ *     exits, traps or prints.
+ *   - Outputs are written, never accumulated: callers need not pre-zero
+ *     dQ/dK/dV or Q/K/V (a caller that does, as model.h:418-424 and
+ *     model.h:549-551 do, gets identical results).
+ *   - Supported shapes: D in {64, 128}; M a multiple of 64 (the reference's
+ *     own requirement, attention.metal:74); N == NH*D; B >= 1.  Anything else
+ *     returns MA_ERR_SHAPE and computes nothing.
+ *   - The library allocates nothing per call on the device except a cached
+ *     4-byte error word per device.
+ */
+#ifndef METALATTN_H_
+#define METALATTN_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MA_API __attribute__((visibility("default")))
+#else
+#define MA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Shape carrier, laid out exactly as the reference's AttentionParams
+ * (attention.metal:7-12, host twin main.cpp:114-119, filled model.h:178):
+ * M = sequence length (BLOCK_SIZE), N = n_embed = NH*D, D = head size,
+ * NH = number of heads.  Four uint32, 16 bytes. */
+typedef struct AttentionParams {
+  uint32_t M;
+  uint32_t N;
+  uint32_t D;
+  uint32_t NH;
+} AttentionParams;
+
+/* A CUDA stream; binary-compatible with cudaStream_t / CUstream. */
+typedef struct CUstream_st* ma_stream_t;
+
+/* Raw bf16 bits (1 sign, 8 exponent, 7 mantissa), as the reference's bfloat. */
+typedef uint16_t ma_bf16;
+
+enum {
+  MA_OK = 0,
+  MA_ERR_SHAPE = 1,          /* unsupported or inconsistent AttentionParams / batch */
+  MA_ERR_NULL = 2,           /* a required pointer is NULL */
+  MA_ERR_ALIGN = 3,          /* a pointer is not 16-byte aligned */
+  MA_ERR_CUDA = 4,           /* a CUDA runtime/driver call or launch failed */
+  MA_ERR_DEVICE_TIMEOUT = 5, /* a kernel gave up on a bounded wait (see ma_device_status) */
+  MA_ERR_RANGE = 6,          /* bh_begin/bh_end outside [0, B*NH] or reversed */
+  MA_ERR_NO_DEVICE = 7,      /* no usable sm_100 device is current */
+  MA_ERR_LIMIT = 8           /* a size exceeds a documented fixed limit */
+};
+
+/* computeQKV: Q = X*Wq, K = X*Wk, V = X*Wv, fp32 accumulation, bf16 outputs.
+ * Replaces attention.metal:19-27 (buffers 0..7) dispatched at model.h:446-458.
+ * X has B*p->M rows. */
+MA_API int ma_computeQKV(const ma_bf16* X, ma_bf16* q, ma_bf16* k, ma_bf16* v,
+                  const ma_bf16* q_w, const ma_bf16* k_w, const ma_bf16* v_w,
+                  const AttentionParams* p, uint32_t B, ma_stream_t stream);
+
+/* flashAttentionForward: causal softmax(Q K^T / sqrt(D)) V per (batch, head);
+ * writes O (bf16) and l = rowmax + ln(rowsum) (fp32, natural log).
+ * Replaces attention.metal:56-66 (buffers 0..5; the threadgroup buffers are
+ * internal) dispatched at model.h:459-473. */
+MA_API int ma_flashAttentionForward(const ma_bf16* q, const ma_bf16* k, const ma_bf16* v,
+                             ma_bf16* out, float* l, const AttentionParams* p,
+                             uint32_t B, ma_stream_t stream);
+
+/* computeD: D[row, h] = bf16(sum_c dO[row, h*D+c] * O[row, h*D+c]), fp32 sum.
+ * Replaces attention.metal:166-171 (buffers 0..3) dispatched at model.h:639-647. */
+MA_API int ma_computeD(const ma_bf16* dO, const ma_bf16* O, ma_bf16* D,
+                const AttentionParams* p, uint32_t B, ma_stream_t stream);
+
+/* flashAttentionBackward: recomputes P = exp(Q K^T / sqrt(D) - l) and writes
+ * dQ (fp32), dK and dV (bf16) for causal attention, given dZ = dO and d = D
+ * from ma_computeD.  Replaces attention.metal:198-211 (buffers 0..9)
+ * dispatched at model.h:648-665. */
+MA_API int ma_flashAttentionBackward(const ma_bf16* dZ, const ma_bf16* d, const float* l,
+                              const ma_bf16* q, const ma_bf16* k, const ma_bf16* v,
+                              float* dQ, ma_bf16* dK, ma_bf16* dV,
+                              const AttentionParams* p, uint32_t B, ma_stream_t stream);
+
+/* Shard variants: the same computation restricted to the flat (batch, head)
+ * indices bh = b*NH + h in [bh_begin, bh_end) of the B-batch tensors the
+ * pointers describe.  Rows and columns outside the range are not touched.
+ * Used to split the independent (batch, head) shards over several GPUs; they
+ * have no counterpart in the single-device reference (model.h:459-473,
+ * model.h:639-665 always dispatch every head). */
+MA_API int ma_flashAttentionForward_shard(const ma_bf16* q, const ma_bf16* k, const ma_bf16* v,
+                                   ma_bf16* out, float* l, const AttentionParams* p,
+                                   uint32_t B, uint32_t bh_begin, uint32_t bh_end,
+                                   ma_stream_t stream);
+MA_API int ma_computeD_shard(const ma_bf16* dO, const ma_bf16* O, ma_bf16* D,
+                      const AttentionParams* p, uint32_t B, uint32_t bh_begin,
+                      uint32_t bh_end, ma_stream_t stream);
+MA_API int ma_flashAttentionBackward_shard(const ma_bf16* dZ, const ma_bf16* d, const float* l,
+                                    const ma_bf16* q, const ma_bf16* k, const ma_bf16* v,
+                                    float* dQ, ma_bf16* dK, ma_bf16* dV,
+                                    const AttentionParams* p, uint32_t B, uint32_t bh_begin,
+                                    uint32_t bh_end, ma_stream_t stream);
+
+/* Text for the last MA_ERR_* returned on the calling host thread ("" if none).
+ * Replaces the reference's printed command-buffer error (model.h:361-365). */
+MA_API const char* ma_last_error_string(void);
+
+/* Reads and clears the current device's kernel status word: 0 = no kernel
+ * gave up; otherwise a bit mask of the kernels whose bounded waits ran out.
+ * Synchronises `stream` first.  Returns MA_OK or an MA_ERR_* code. */
+MA_API int ma_device_status(uint32_t* status, ma_stream_t stream);
+
+/* Number of kernels this library has launched in this process (all devices,
+ * all threads), for accounting of launches in timed regions.  Diagnostic;
+ * no counterpart in the reference. */
+MA_API uint64_t ma_kernel_launch_count(void);
+
+/* Library version as major*10000 + minor*100 + patch. */
+MA_API int ma_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* METALATTN_H_ */

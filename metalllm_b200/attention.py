@@ -1,0 +1,184 @@
+"""Operator interface of the attention hot path on torch CUDA tensors.
+
+The four functions mirror the reference's four kernels (attention.metal:19-299)
+with the same buffer roles, order and dtypes, as its host code binds them
+(model.h:446-473 forward, model.h:639-665 backward).  Each call goes through the
+C ABI of libmetalattn (include/metalattn.h); PyTorch only provides the device
+memory and the stream.  Outputs may be passed in (as the reference's
+preallocated buffers) or are allocated here.
+
+Shapes (B sequences of length T = params.M, N = params.N = NH*D):
+    X, q, k, v, out, dO, dK, dV : bf16 [B, T, N]
+    dQ                          : fp32 [B, T, N]
+    l                           : fp32 [B, T, NH]
+    D                           : bf16 [B, T, NH]
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import torch
+
+from . import _lib
+from ._lib import AttentionParams, MetalAttnError  # noqa: F401  (re-exported)
+
+
+def make_params(T: int, NH: int, D: int) -> AttentionParams:
+    """AttentionParams{M=T, N=NH*D, D, NH} as model.h:178 fills it."""
+    return AttentionParams(T, NH * D, D, NH)
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(stream: Optional[torch.cuda.Stream]) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def _check(t: torch.Tensor, name: str, dtype: torch.dtype, shape: tuple) -> None:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (no CPU path exists)")
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if tuple(t.shape) != tuple(shape) and t.numel() != _numel(shape):
+        raise ValueError(f"{name} has shape {tuple(t.shape)}, expected {tuple(shape)}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def _numel(shape: tuple) -> int:
+    n = 1
+    for s in shape:
+        n *= s
+    return n
+
+
+def _out(t: Optional[torch.Tensor], like: torch.Tensor, shape: tuple, dtype: torch.dtype,
+         name: str) -> torch.Tensor:
+    if t is None:
+        return torch.empty(shape, dtype=dtype, device=like.device)
+    _check(t, name, dtype, shape)
+    return t
+
+
+def computeQKV(X: torch.Tensor, q_w: torch.Tensor, k_w: torch.Tensor, v_w: torch.Tensor,
+               p: AttentionParams, B: int, q: Optional[torch.Tensor] = None,
+               k: Optional[torch.Tensor] = None, v: Optional[torch.Tensor] = None,
+               stream: Optional[torch.cuda.Stream] = None):
+    """q, k, v = X Wq, X Wk, X Wv (attention.metal:19-53)."""
+    act = (B, p.M, p.N)
+    _check(X, "X", torch.bfloat16, act)
+    for w, n in ((q_w, "q_w"), (k_w, "k_w"), (v_w, "v_w")):
+        _check(w, n, torch.bfloat16, (p.N, p.N))
+    q = _out(q, X, act, torch.bfloat16, "q")
+    k = _out(k, X, act, torch.bfloat16, "k")
+    v = _out(v, X, act, torch.bfloat16, "v")
+    _lib.call("ma_computeQKV", _ptr(X), _ptr(q), _ptr(k), _ptr(v), _ptr(q_w), _ptr(k_w),
+              _ptr(v_w), ctypes.byref(p), B, _stream(stream))
+    return q, k, v
+
+
+def flashAttentionForward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, p: AttentionParams,
+                          B: int, out: Optional[torch.Tensor] = None,
+                          l: Optional[torch.Tensor] = None, shard: Optional[tuple] = None,
+                          stream: Optional[torch.cuda.Stream] = None):
+    """out, l = causal attention of (q, k, v) (attention.metal:56-164).
+
+    ``shard=(bh_begin, bh_end)`` restricts the work to flat (batch, head) indices
+    in that range (ma_flashAttentionForward_shard)."""
+    act = (B, p.M, p.N)
+    for t, n in ((q, "q"), (k, "k"), (v, "v")):
+        _check(t, n, torch.bfloat16, act)
+    out = _out(out, q, act, torch.bfloat16, "out")
+    l = _out(l, q, (B, p.M, p.NH), torch.float32, "l")
+    if shard is None:
+        _lib.call("ma_flashAttentionForward", _ptr(q), _ptr(k), _ptr(v), _ptr(out), _ptr(l),
+                  ctypes.byref(p), B, _stream(stream))
+    else:
+        _lib.call("ma_flashAttentionForward_shard", _ptr(q), _ptr(k), _ptr(v), _ptr(out), _ptr(l),
+                  ctypes.byref(p), B, shard[0], shard[1], _stream(stream))
+    return out, l
+
+
+def computeD(dO: torch.Tensor, O: torch.Tensor, p: AttentionParams, B: int,
+             D: Optional[torch.Tensor] = None, shard: Optional[tuple] = None,
+             stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """D = rowsum(dO * O) per head, bf16 (attention.metal:166-195)."""
+    act = (B, p.M, p.N)
+    _check(dO, "dO", torch.bfloat16, act)
+    _check(O, "O", torch.bfloat16, act)
+    D = _out(D, dO, (B, p.M, p.NH), torch.bfloat16, "D")
+    if shard is None:
+        _lib.call("ma_computeD", _ptr(dO), _ptr(O), _ptr(D), ctypes.byref(p), B, _stream(stream))
+    else:
+        _lib.call("ma_computeD_shard", _ptr(dO), _ptr(O), _ptr(D), ctypes.byref(p), B, shard[0],
+                  shard[1], _stream(stream))
+    return D
+
+
+def flashAttentionBackward(dZ: torch.Tensor, d: torch.Tensor, l: torch.Tensor, q: torch.Tensor,
+                           k: torch.Tensor, v: torch.Tensor, p: AttentionParams, B: int,
+                           dQ: Optional[torch.Tensor] = None, dK: Optional[torch.Tensor] = None,
+                           dV: Optional[torch.Tensor] = None, shard: Optional[tuple] = None,
+                           stream: Optional[torch.cuda.Stream] = None):
+    """dQ (fp32), dK, dV (bf16) of causal attention (attention.metal:198-299)."""
+    act = (B, p.M, p.N)
+    for t, n in ((dZ, "dZ"), (q, "q"), (k, "k"), (v, "v")):
+        _check(t, n, torch.bfloat16, act)
+    _check(d, "d", torch.bfloat16, (B, p.M, p.NH))
+    _check(l, "l", torch.float32, (B, p.M, p.NH))
+    dQ = _out(dQ, q, act, torch.float32, "dQ")
+    dK = _out(dK, q, act, torch.bfloat16, "dK")
+    dV = _out(dV, q, act, torch.bfloat16, "dV")
+    args = (_ptr(dZ), _ptr(d), _ptr(l), _ptr(q), _ptr(k), _ptr(v), _ptr(dQ), _ptr(dK), _ptr(dV),
+            ctypes.byref(p), B)
+    if shard is None:
+        _lib.call("ma_flashAttentionBackward", *args, _stream(stream))
+    else:
+        _lib.call("ma_flashAttentionBackward_shard", *args, shard[0], shard[1], _stream(stream))
+    return dQ, dK, dV
+
+
+def device_status(stream: Optional[torch.cuda.Stream] = None) -> int:
+    """Reads and clears the device's kernel status word (0 = no bounded wait ran out)."""
+    st = ctypes.c_uint32(0)
+    _lib.call("ma_device_status", ctypes.byref(st), _stream(stream))
+    return st.value
+
+
+class CudaAttention:
+    """Attention core of one transformer block with reference-style buffers.
+
+    Mirrors the attention part of the reference's MetalAttention harness
+    (main.cpp:955-1284) and Model::forward/backward (model.h:446-473,
+    639-665): buffers are allocated once for (B, T, NH, D) and reused, forward
+    runs flashAttentionForward, backward runs computeD then
+    flashAttentionBackward.  The projections around attention are not part of
+    this path."""
+
+    def __init__(self, B: int, T: int, NH: int, D: int, device="cuda"):
+        self.B, self.T, self.NH, self.D = B, T, NH, D
+        self.p = make_params(T, NH, D)
+        act = (B, T, NH * D)
+        dev = torch.device(device)
+        self.out = torch.empty(act, dtype=torch.bfloat16, device=dev)
+        self.l = torch.empty((B, T, NH), dtype=torch.float32, device=dev)
+        self.Dvec = torch.empty((B, T, NH), dtype=torch.bfloat16, device=dev)
+        self.dQ = torch.empty(act, dtype=torch.float32, device=dev)
+        self.dK = torch.empty(act, dtype=torch.bfloat16, device=dev)
+        self.dV = torch.empty(act, dtype=torch.bfloat16, device=dev)
+
+    def forward(self, q, k, v, stream=None):
+        self.q, self.k, self.v = q, k, v
+        return flashAttentionForward(q, k, v, self.p, self.B, out=self.out, l=self.l,
+                                     stream=stream)
+
+    def backward(self, dO, stream=None):
+        computeD(dO, self.out, self.p, self.B, D=self.Dvec, stream=stream)
+        return flashAttentionBackward(dO, self.Dvec, self.l, self.q, self.k, self.v, self.p,
+                                      self.B, dQ=self.dQ, dK=self.dK, dV=self.dV, stream=stream)

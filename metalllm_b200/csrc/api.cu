@@ -1,0 +1,279 @@
+// api.cu -- the extern "C" boundary of libmetalattn (include/metalattn.h).
+//
+// Each entry point replaces one Metal dispatch of the reference's host code
+// (model.h:446-473 forward, model.h:639-665 backward): it validates the
+// AttentionParams and pointers, then enqueues the kernel on the caller's
+// stream.  Errors are returned as MA_ERR_* codes with a per-thread message
+// instead of the reference's exit(1) (model.h:333-336) or printed-and-ignored
+// command-buffer error (model.h:361-365).
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "common.cuh"
+
+namespace {
+std::atomic<unsigned long long> g_launches{0};
+}  // namespace
+
+void ma::count_launches(unsigned n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int ok() {
+  g_last_error.clear();
+  return MA_OK;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(MA_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+// One 4-byte status word per device (bit mask of kernels whose bounded waits
+// ran out), allocated on first use and kept for the life of the process.
+constexpr int kMaxDevices = 64;
+uint32_t* g_status[kMaxDevices] = {};
+std::mutex g_status_mu;
+
+int device_status_word(uint32_t** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(MA_ERR_NO_DEVICE, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_status_mu);
+  if (!g_status[dev]) {
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    if (major != 10 || minor != 0)
+      return fail(MA_ERR_NO_DEVICE, "device %d is sm_%d%d; libmetalattn is built for sm_100a only", dev,
+                  major, minor);
+    void* p = nullptr;
+    e = cudaMalloc(&p, sizeof(uint32_t));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(status word)");
+    e = cudaMemset(p, 0, sizeof(uint32_t));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(status word)");
+    g_status[dev] = static_cast<uint32_t*>(p);
+  }
+  *out = g_status[dev];
+  return MA_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Validates AttentionParams + batch + shard range; fills the kernel shape.
+int check_shape(const AttentionParams* p, uint32_t B, uint32_t bh_begin, uint32_t bh_end,
+                bool is_range, ma::AttnShape* s) {
+  if (!p) return fail(MA_ERR_NULL, "AttentionParams pointer is NULL");
+  if (p->D != 64 && p->D != 128)
+    return fail(MA_ERR_SHAPE, "head size D=%u unsupported (supported: 64, 128)", p->D);
+  if (p->NH == 0 || p->M == 0 || B == 0)
+    return fail(MA_ERR_SHAPE, "empty shape: M=%u NH=%u B=%u", p->M, p->NH, B);
+  if ((uint64_t)p->NH * p->D != p->N)
+    return fail(MA_ERR_SHAPE, "N=%u must equal NH*D=%u*%u", p->N, p->NH, p->D);
+  if (p->M % 64 != 0)
+    return fail(MA_ERR_SHAPE, "sequence length M=%u must be a multiple of 64", p->M);
+  const uint64_t nbh = (uint64_t)B * p->NH;
+  if ((uint64_t)B * p->M * p->N >= (1ull << 40) || nbh >= (1ull << 30) || p->M > (1u << 24))
+    return fail(MA_ERR_LIMIT, "problem too large: B=%u M=%u N=%u", B, p->M, p->N);
+  if (is_range && (bh_begin > bh_end || bh_end > nbh))
+    return fail(MA_ERR_RANGE, "shard range [%u, %u) outside [0, %llu]", bh_begin, bh_end,
+                (unsigned long long)nbh);
+  s->T = (int)p->M;
+  s->N = (int)p->N;
+  s->D = (int)p->D;
+  s->NH = (int)p->NH;
+  s->B = (int)B;
+  s->bh_begin = is_range ? (int)bh_begin : 0;
+  s->bh_end = is_range ? (int)bh_end : (int)nbh;
+  return MA_OK;
+}
+
+#define MA_REQUIRE_PTR(ptr)                                                          \
+  do {                                                                               \
+    if (!(ptr)) return fail(MA_ERR_NULL, "pointer '%s' is NULL", #ptr);              \
+    if (!aligned16(ptr)) return fail(MA_ERR_ALIGN, "pointer '%s' is not 16-byte aligned", #ptr); \
+  } while (0)
+
+using bf16p = const __nv_bfloat16*;
+using bf16m = __nv_bfloat16*;
+
+int forward_impl(const ma_bf16* q, const ma_bf16* k, const ma_bf16* v, ma_bf16* out, float* l,
+                 const AttentionParams* p, uint32_t B, uint32_t b0, uint32_t b1, bool range,
+                 ma_stream_t stream) {
+  ma::AttnShape s;
+  int rc = check_shape(p, B, b0, b1, range, &s);
+  if (rc) return rc;
+  MA_REQUIRE_PTR(q);
+  MA_REQUIRE_PTR(k);
+  MA_REQUIRE_PTR(v);
+  MA_REQUIRE_PTR(out);
+  MA_REQUIRE_PTR(l);
+  uint32_t* status = nullptr;
+  rc = device_status_word(&status);
+  if (rc) return rc;
+  if (s.bh_end == s.bh_begin) return ok();
+  cudaError_t e = ma::launch_flash_fwd(reinterpret_cast<bf16p>(q), reinterpret_cast<bf16p>(k),
+                                       reinterpret_cast<bf16p>(v), reinterpret_cast<bf16m>(out), l, s,
+                                       status, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "flashAttentionForward launch");
+  return ok();
+}
+
+int compute_d_impl(const ma_bf16* dO, const ma_bf16* O, ma_bf16* D, const AttentionParams* p,
+                   uint32_t B, uint32_t b0, uint32_t b1, bool range, ma_stream_t stream) {
+  ma::AttnShape s;
+  int rc = check_shape(p, B, b0, b1, range, &s);
+  if (rc) return rc;
+  MA_REQUIRE_PTR(dO);
+  MA_REQUIRE_PTR(O);
+  if (!D) return fail(MA_ERR_NULL, "pointer 'D' is NULL");
+  if (reinterpret_cast<uintptr_t>(D) & 1u) return fail(MA_ERR_ALIGN, "pointer 'D' is not 2-byte aligned");
+  uint32_t* status = nullptr;
+  rc = device_status_word(&status);
+  if (rc) return rc;
+  if (s.bh_end == s.bh_begin) return ok();
+  cudaError_t e = ma::launch_compute_d(reinterpret_cast<bf16p>(dO), reinterpret_cast<bf16p>(O),
+                                       reinterpret_cast<bf16m>(D), s,
+                                       reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "computeD launch");
+  return ok();
+}
+
+int backward_impl(const ma_bf16* dZ, const ma_bf16* d, const float* l, const ma_bf16* q,
+                  const ma_bf16* k, const ma_bf16* v, float* dQ, ma_bf16* dK, ma_bf16* dV,
+                  const AttentionParams* p, uint32_t B, uint32_t b0, uint32_t b1, bool range,
+                  ma_stream_t stream) {
+  ma::AttnShape s;
+  int rc = check_shape(p, B, b0, b1, range, &s);
+  if (rc) return rc;
+  MA_REQUIRE_PTR(dZ);
+  if (!d) return fail(MA_ERR_NULL, "pointer 'd' is NULL");
+  if (reinterpret_cast<uintptr_t>(d) & 1u) return fail(MA_ERR_ALIGN, "pointer 'd' is not 2-byte aligned");
+  MA_REQUIRE_PTR(l);
+  MA_REQUIRE_PTR(q);
+  MA_REQUIRE_PTR(k);
+  MA_REQUIRE_PTR(v);
+  MA_REQUIRE_PTR(dQ);
+  MA_REQUIRE_PTR(dK);
+  MA_REQUIRE_PTR(dV);
+  uint32_t* status = nullptr;
+  rc = device_status_word(&status);
+  if (rc) return rc;
+  if (s.bh_end == s.bh_begin) return ok();
+  cudaError_t e = ma::launch_flash_bwd(
+      reinterpret_cast<bf16p>(dZ), reinterpret_cast<bf16p>(d), l, reinterpret_cast<bf16p>(q),
+      reinterpret_cast<bf16p>(k), reinterpret_cast<bf16p>(v), dQ, reinterpret_cast<bf16m>(dK),
+      reinterpret_cast<bf16m>(dV), s, status, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "flashAttentionBackward launch");
+  return ok();
+}
+
+}  // namespace
+
+extern "C" {
+
+int ma_computeQKV(const ma_bf16* X, ma_bf16* q, ma_bf16* k, ma_bf16* v, const ma_bf16* q_w,
+                  const ma_bf16* k_w, const ma_bf16* v_w, const AttentionParams* p, uint32_t B,
+                  ma_stream_t stream) {
+  if (!p) return fail(MA_ERR_NULL, "AttentionParams pointer is NULL");
+  if (p->N == 0 || p->M == 0 || B == 0) return fail(MA_ERR_SHAPE, "empty shape: M=%u N=%u B=%u", p->M, p->N, B);
+  if (p->N % 64 != 0) return fail(MA_ERR_SHAPE, "N=%u must be a multiple of 64", p->N);
+  if (p->M % 64 != 0) return fail(MA_ERR_SHAPE, "M=%u must be a multiple of 64", p->M);
+  if ((uint64_t)B * p->M >= (1ull << 31) || p->N > 16384)
+    return fail(MA_ERR_LIMIT, "problem too large: B*M=%llu N=%u", (unsigned long long)B * p->M, p->N);
+  MA_REQUIRE_PTR(X);
+  MA_REQUIRE_PTR(q);
+  MA_REQUIRE_PTR(k);
+  MA_REQUIRE_PTR(v);
+  MA_REQUIRE_PTR(q_w);
+  MA_REQUIRE_PTR(k_w);
+  MA_REQUIRE_PTR(v_w);
+  uint32_t* status = nullptr;
+  int rc = device_status_word(&status);
+  if (rc) return rc;
+  cudaError_t e = ma::launch_qkv(
+      reinterpret_cast<bf16p>(X), reinterpret_cast<bf16m>(q), reinterpret_cast<bf16m>(k),
+      reinterpret_cast<bf16m>(v), reinterpret_cast<bf16p>(q_w), reinterpret_cast<bf16p>(k_w),
+      reinterpret_cast<bf16p>(v_w), (int)(B * p->M), (int)p->N, status,
+      reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "computeQKV launch");
+  return ok();
+}
+
+int ma_flashAttentionForward(const ma_bf16* q, const ma_bf16* k, const ma_bf16* v, ma_bf16* out,
+                             float* l, const AttentionParams* p, uint32_t B, ma_stream_t stream) {
+  return forward_impl(q, k, v, out, l, p, B, 0, 0, false, stream);
+}
+
+int ma_flashAttentionForward_shard(const ma_bf16* q, const ma_bf16* k, const ma_bf16* v,
+                                   ma_bf16* out, float* l, const AttentionParams* p, uint32_t B,
+                                   uint32_t bh_begin, uint32_t bh_end, ma_stream_t stream) {
+  return forward_impl(q, k, v, out, l, p, B, bh_begin, bh_end, true, stream);
+}
+
+int ma_computeD(const ma_bf16* dO, const ma_bf16* O, ma_bf16* D, const AttentionParams* p,
+                uint32_t B, ma_stream_t stream) {
+  return compute_d_impl(dO, O, D, p, B, 0, 0, false, stream);
+}
+
+int ma_computeD_shard(const ma_bf16* dO, const ma_bf16* O, ma_bf16* D, const AttentionParams* p,
+                      uint32_t B, uint32_t bh_begin, uint32_t bh_end, ma_stream_t stream) {
+  return compute_d_impl(dO, O, D, p, B, bh_begin, bh_end, true, stream);
+}
+
+int ma_flashAttentionBackward(const ma_bf16* dZ, const ma_bf16* d, const float* l,
+                              const ma_bf16* q, const ma_bf16* k, const ma_bf16* v, float* dQ,
+                              ma_bf16* dK, ma_bf16* dV, const AttentionParams* p, uint32_t B,
+                              ma_stream_t stream) {
+  return backward_impl(dZ, d, l, q, k, v, dQ, dK, dV, p, B, 0, 0, false, stream);
+}
+
+int ma_flashAttentionBackward_shard(const ma_bf16* dZ, const ma_bf16* d, const float* l,
+                                    const ma_bf16* q, const ma_bf16* k, const ma_bf16* v,
+                                    float* dQ, ma_bf16* dK, ma_bf16* dV,
+                                    const AttentionParams* p, uint32_t B, uint32_t bh_begin,
+                                    uint32_t bh_end, ma_stream_t stream) {
+  return backward_impl(dZ, d, l, q, k, v, dQ, dK, dV, p, B, bh_begin, bh_end, true, stream);
+}
+
+const char* ma_last_error_string(void) { return g_last_error.c_str(); }
+
+int ma_device_status(uint32_t* status, ma_stream_t stream) {
+  if (!status) return fail(MA_ERR_NULL, "status pointer is NULL");
+  uint32_t* word = nullptr;
+  int rc = device_status_word(&word);
+  if (rc) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+  uint32_t host = 0;
+  e = cudaMemcpy(&host, word, sizeof(uint32_t), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy(status word)");
+  e = cudaMemset(word, 0, sizeof(uint32_t));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(status word)");
+  *status = host;
+  return ok();
+}
+
+uint64_t ma_kernel_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int ma_version(void) { return 100; }
+
+}  // extern "C"

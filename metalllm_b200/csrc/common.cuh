@@ -1,0 +1,51 @@
+// common.cuh -- helpers shared by the kernels of libmetalattn (sm_100a only).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/metalattn.h"
+
+namespace ma {
+
+// Per-kernel bits of the device status word (ma_device_status).
+enum : uint32_t {
+  STATUS_FWD_TIMEOUT = 1u << 0,
+  STATUS_BWD_TIMEOUT = 1u << 1,
+  STATUS_QKV_TIMEOUT = 1u << 2,
+};
+
+// Problem description shared by the attention kernels.  Row strides are in
+// elements: a (batch, position) row of Q/K/V/O/dO/dK/dV/dQ holds N = NH*D
+// values; l and D hold NH values per row.
+struct AttnShape {
+  int T;         // sequence length (AttentionParams.M)
+  int N;         // NH*D
+  int D;         // head size
+  int NH;        // heads
+  int B;         // batch
+  int bh_begin;  // flat (b*NH + h) shard range
+  int bh_end;
+};
+
+// Adds n to the process-wide kernel launch counter (ma_kernel_launch_count).
+void count_launches(unsigned n);
+
+// Launchers (each returns the cudaError_t of its launch).
+cudaError_t launch_compute_d(const __nv_bfloat16* dO, const __nv_bfloat16* O,
+                             __nv_bfloat16* Dv, const AttnShape& s, cudaStream_t st);
+cudaError_t launch_flash_fwd(const __nv_bfloat16* q, const __nv_bfloat16* k,
+                             const __nv_bfloat16* v, __nv_bfloat16* out, float* lse,
+                             const AttnShape& s, uint32_t* status, cudaStream_t st);
+cudaError_t launch_flash_bwd(const __nv_bfloat16* dO, const __nv_bfloat16* Dv,
+                             const float* lse, const __nv_bfloat16* q,
+                             const __nv_bfloat16* k, const __nv_bfloat16* v, float* dQ,
+                             __nv_bfloat16* dK, __nv_bfloat16* dV, const AttnShape& s,
+                             uint32_t* status, cudaStream_t st);
+cudaError_t launch_qkv(const __nv_bfloat16* X, __nv_bfloat16* q, __nv_bfloat16* k,
+                       __nv_bfloat16* v, const __nv_bfloat16* qw, const __nv_bfloat16* kw,
+                       const __nv_bfloat16* vw, int rows, int N, uint32_t* status,
+                       cudaStream_t st);
+
+}  // namespace ma

@@ -1,0 +1,251 @@
+"""GPU parity tests: every entry point of libmetalattn, called through the C
+ABI, against the CPU oracle (exact-interface mode) and the golden fixtures.
+
+Tolerances: O, dQ, dK, dV within max-abs 2e-2 and
+relative-L2 1e-2 of the oracle's fp32 values; lse within 1e-3 absolute.
+computeD is compared with the oracle's fp32 sum to 1 bf16 rounding step.
+Large configs are checked on sampled (batch, head) shards against the oracle
+and, over the whole tensor, through size-independent identities."""
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from metalllm_b200.inputs import CONFIGS, bf16_bits_to_f32, normal_bf16  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS, REL_L2, LSE_ABS = 2e-2, 1e-2, 1e-3
+GOLDEN = Path(__file__).resolve().parent / "golden" / "attn_golden.npz"
+
+
+@pytest.fixture(scope="module")
+def A():
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    from metalllm_b200.build import build_cuda
+    build_cuda()
+    from metalllm_b200 import attention
+    return attention
+
+
+def up(bits: np.ndarray) -> "torch.Tensor":
+    return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).view(torch.bfloat16).cuda()
+
+
+def down(t: "torch.Tensor") -> np.ndarray:
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def f32(t: "torch.Tensor") -> np.ndarray:
+    return t.detach().cpu().float().numpy()
+
+
+def bf(t) -> np.ndarray:
+    return bf16_bits_to_f32(down(t)) if isinstance(t, torch.Tensor) else bf16_bits_to_f32(t)
+
+
+def check(name, got, want, max_abs=MAX_ABS, rel_l2=REL_L2):
+    from oracle.oracle import compare
+    ok, mae, rl2 = compare(got, want, max_abs, rel_l2)
+    assert ok, f"{name}: max_abs={mae:.3e} rel_l2={rl2:.3e}"
+
+
+def inputs(B, T, H, D, seed=0, qkv_scale=1.0, do_scale=1.0):
+    n = B * T * H * D
+    shp = (B, T, H * D)
+    return [normal_bf16(n, seed, s, sc).reshape(shp)
+            for s, sc in ((1, qkv_scale), (2, qkv_scale), (3, qkv_scale), (4, do_scale))]
+
+
+def gpu_chain(A, q, k, v, do, B, T, H, D):
+    p = A.make_params(T, H, D)
+    tq, tk, tv, tdo = up(q), up(k), up(v), up(do)
+    out, l = A.flashAttentionForward(tq, tk, tv, p, B)
+    Dv = A.computeD(tdo, out, p, B)
+    dQ, dK, dV = A.flashAttentionBackward(tdo, Dv, l, tq, tk, tv, p, B)
+    torch.cuda.synchronize()
+    return out, l, Dv, dQ, dK, dV
+
+
+# ------------------------------------------------------------------ golden
+def _golden():
+    z = np.load(GOLDEN)
+    names = sorted({k.split("/")[0] for k in z.files})
+    return [(n, {k.split("/")[1]: z[k] for k in z.files if k.startswith(n + "/")}) for n in names]
+
+
+@pytest.mark.parametrize("name,case", _golden(), ids=[n for n, _ in _golden()])
+def test_golden_vectors(A, name, case):
+    B, T, H, D = (int(x) for x in case["shape"])
+    p = A.make_params(T, H, D)
+    tq, tk, tv, tdo = up(case["q"]), up(case["k"]), up(case["v"]), up(case["do"])
+    out, l = A.flashAttentionForward(tq, tk, tv, p, B)
+    check("O", bf(out), bf(case["o"]))
+    assert np.abs(f32(l) - case["lse"]).max() <= LSE_ABS
+    Dv = A.computeD(tdo, up(case["o"]), p, B)
+    assert np.abs(bf(Dv) - case["d32"]).max() <= 2 ** -7 * max(1.0, np.abs(case["d32"]).max())
+    dQ, dK, dV = A.flashAttentionBackward(tdo, up(case["d"]), torch.from_numpy(case["lse"]).cuda(),
+                                          tq, tk, tv, p, B)
+    check("dQ", f32(dQ), case["dq"])
+    check("dK", bf(dK), case["dk32"])
+    check("dV", bf(dV), case["dv32"])
+
+
+# --------------------------------------------------- small and medium shapes
+SHAPES = [
+    (1, 64, 1, 64), (2, 128, 3, 64), (1, 192, 2, 128), (2, 256, 2, 64), (1, 320, 1, 128),
+    (1, 1024, 2, 64), (1, 1024, 2, 128), (16, 256, 6, 64),  # the last one is config 1
+]
+
+
+@pytest.mark.parametrize("B,T,H,D", SHAPES)
+def test_parity_vs_oracle(A, oracle_mod, B, T, H, D):
+    o = oracle_mod
+    q, k, v, do = inputs(B, T, H, D, seed=T + D)
+    out, l, Dv, dQ, dK, dV = gpu_chain(A, q, k, v, do, B, T, H, D)
+    # forward against the oracle from the same inputs
+    oo, ol, o32 = o.flash_forward(q, k, v, H, want_f32=True)
+    check("O", bf(out), o32)
+    assert np.abs(f32(l) - ol).max() <= LSE_ABS
+    # computeD against the oracle from the GPU's O
+    od, od32 = o.compute_d(do, down(out), H, want_f32=True)
+    assert np.abs(bf(Dv) - od32).max() <= 2 ** -8 * max(1.0, np.abs(od32).max())
+    # backward against the oracle fed the same l and D as the GPU
+    rq, rk, rv, rk32, rv32 = o.flash_backward(do, down(Dv), f32(l), q, k, v, H, want_f32=True)
+    check("dQ", f32(dQ), rq)
+    check("dK", bf(dK), rk32)
+    check("dV", bf(dV), rv32)
+
+
+def test_row0_equals_v_row0(A):
+    """README.md:132: row 0 of a causal head equals V row 0 (bit-exact)."""
+    B, T, H, D = 3, 256, 4, 128
+    q, k, v, _ = inputs(B, T, H, D, seed=3)
+    p = A.make_params(T, H, D)
+    out, l = A.flashAttentionForward(up(q), up(k), up(v), p, B)
+    assert np.array_equal(down(out)[:, 0, :], v[:, 0, :])
+
+
+def test_shard_entry_points(A):
+    """Shard variants write exactly their (batch, head) slabs, bit-identical to
+    the full call, and leave the rest untouched."""
+    B, T, H, D = 2, 256, 3, 64
+    q, k, v, do = inputs(B, T, H, D, seed=9)
+    full = gpu_chain(A, q, k, v, do, B, T, H, D)
+    p = A.make_params(T, H, D)
+    tq, tk, tv, tdo = up(q), up(k), up(v), up(do)
+    b0, b1 = 2, 5
+    act = (B, T, H * D)
+    out = torch.full(act, float("nan"), dtype=torch.bfloat16, device="cuda")
+    l = torch.full((B, T, H), float("nan"), dtype=torch.float32, device="cuda")
+    Dv = torch.full((B, T, H), float("nan"), dtype=torch.bfloat16, device="cuda")
+    dQ = torch.full(act, float("nan"), dtype=torch.float32, device="cuda")
+    dK = torch.full(act, float("nan"), dtype=torch.bfloat16, device="cuda")
+    dV = torch.full(act, float("nan"), dtype=torch.bfloat16, device="cuda")
+    A.flashAttentionForward(tq, tk, tv, p, B, out=out, l=l, shard=(b0, b1))
+    A.computeD(tdo, full[0], p, B, D=Dv, shard=(b0, b1))
+    A.flashAttentionBackward(tdo, full[2], full[1], tq, tk, tv, p, B, dQ=dQ, dK=dK, dV=dV,
+                             shard=(b0, b1))
+    torch.cuda.synchronize()
+    for bh in range(B * H):
+        b, h = divmod(bh, H)
+        cols = slice(h * D, (h + 1) * D)
+        inside = b0 <= bh < b1
+        for got, ref in ((out, full[0]), (dK, full[4]), (dV, full[5])):
+            g = down(got[b, :, cols])
+            if inside:
+                assert np.array_equal(g, down(ref[b, :, cols]))
+            else:
+                assert np.isnan(bf16_bits_to_f32(g)).all()
+        for got, ref in ((l, full[1]), (Dv, full[2])):
+            g = got[b, :, h].float().cpu().numpy()
+            if inside:
+                assert np.array_equal(g, ref[b, :, h].float().cpu().numpy())
+            else:
+                assert np.isnan(g).all()
+        g = f32(dQ[b, :, cols])
+        if inside:
+            check("dQ shard", g, f32(full[3][b, :, cols]), 1e-5, 1e-6)
+        else:
+            assert np.isnan(g).all()
+
+
+def test_determinism(A):
+    B, T, H, D = 2, 512, 2, 64
+    q, k, v, do = inputs(B, T, H, D, seed=21)
+    r1 = gpu_chain(A, q, k, v, do, B, T, H, D)
+    r2 = gpu_chain(A, q, k, v, do, B, T, H, D)
+    for i in (0, 1, 2, 4, 5):
+        assert torch.equal(r1[i], r2[i]), i
+    check("dQ rerun", f32(r1[3]), f32(r2[3]), 1e-5, 1e-6)
+
+
+def test_compute_qkv(A, oracle_mod):
+    B, M, H, D = 2, 256, 6, 64
+    N = H * D
+    X = normal_bf16(B * M * N, 31, 5).reshape(B, M, N)
+    W = [normal_bf16(N * N, 31, 6 + i, 0.02).reshape(N, N) for i in range(3)]
+    p = A.make_params(M, H, D)
+    q, k, v = A.computeQKV(up(X), up(W[0]), up(W[1]), up(W[2]), p, B)
+    torch.cuda.synchronize()
+    rq, rk, rv, rq32, rk32, rv32 = oracle_mod.compute_qkv(X, *W, want_f32=True)
+    check("Q", bf(q), rq32, 1e-2, 5e-3)
+    check("K", bf(k), rk32, 1e-2, 5e-3)
+    check("V", bf(v), rv32, 1e-2, 5e-3)
+
+
+def test_cuda_attention_class_and_stream(A, oracle_mod):
+    B, T, H, D = 2, 256, 2, 128
+    q, k, v, do = inputs(B, T, H, D, seed=41)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        att = A.CudaAttention(B, T, H, D)
+        out, l = att.forward(up(q), up(k), up(v), stream=s)
+        dQ, dK, dV = att.backward(up(do), stream=s)
+    s.synchronize()
+    ref = gpu_chain(A, q, k, v, do, B, T, H, D)
+    assert torch.equal(out, ref[0]) and torch.equal(dK, ref[4])
+    assert A.device_status() == 0
+
+
+def test_bad_call_on_gpu_raises(A):
+    p = A.make_params(96, 1, 64)  # M not a multiple of 64
+    x = torch.zeros(1, 96, 64, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(A.MetalAttnError, match="MA_ERR_SHAPE"):
+        A.flashAttentionForward(x, x, x, p, 1)
+
+
+# ------------------------------------------------ BASELINE configs 2, 3, 4
+@pytest.mark.parametrize("cfg", ["c2", "c3", "c4"])
+def test_full_config_sampled_shards_and_identities(A, oracle_mod, cfg):
+    c = CONFIGS[cfg]
+    B, T, H, D = c["B"], c["T"], c["H"], c["D"]
+    q, k, v, do = inputs(B, T, H, D, seed=0, qkv_scale=c["qkv_scale"], do_scale=c["do_scale"])
+    out, l, Dv, dQ, dK, dV = gpu_chain(A, q, k, v, do, B, T, H, D)
+    assert A.device_status() == 0
+    # README.md:132 on every head of the full tensor
+    assert np.array_equal(down(out[:, 0, :]), v[:, 0, :])
+    assert torch.isfinite(l).all() and torch.isfinite(dQ).all()
+    # sum over keys of dV equals the sum over queries of dO (softmax rows sum
+    # to 1), per head, over the whole tensor
+    sdv = dV.double().sum(1)
+    sdo = torch.from_numpy(bf16_bits_to_f32(do)).cuda().double().sum(1)
+    rel = ((sdv - sdo).norm() / sdo.norm()).item()
+    assert rel < 1e-2, rel
+    # sampled shards: first and last (batch, head) against the oracle
+    for bh in (0, B * H - 1):
+        b, h = divmod(bh, H)
+        cols = slice(h * D, (h + 1) * D)
+        sl = lambda a: np.ascontiguousarray(a[b:b + 1, :, cols])
+        oo, ol, o32 = oracle_mod.flash_forward(sl(q), sl(k), sl(v), 1, want_f32=True)
+        check(f"O[{bh}]", bf(out[b:b + 1, :, cols]), o32)
+        assert np.abs(f32(l[b:b + 1, :, h:h + 1]) - ol).max() <= LSE_ABS
+        rq, rk, rv, rk32, rv32 = oracle_mod.flash_backward(
+            sl(do), np.ascontiguousarray(down(Dv[b:b + 1, :, h:h + 1])),
+            np.ascontiguousarray(f32(l[b:b + 1, :, h:h + 1])), sl(q), sl(k), sl(v), 1, want_f32=True)
+        check(f"dQ[{bh}]", f32(dQ[b:b + 1, :, cols]), rq)
+        check(f"dK[{bh}]", bf(dK[b:b + 1, :, cols]), rk32)
+        check(f"dV[{bh}]", bf(dV[b:b + 1, :, cols]), rv32)
