@@ -132,6 +132,8 @@ def run_gpu(args):
 
     c = CONFIGS[args.config]
     B, T, H, D = c["B"], c["T"], c["H"], c["D"]
+    if args.batch:
+        B = args.batch  # smaller case of the same shape (profiling); not a bench line
     p = A.make_params(T, H, D)
     # this rank's shards: batch rows [rank*B, (rank+1)*B) of the global N*B batch
     host = attention_inputs(B, T, H, D, seed=args.seed + rank, qkv_scale=c["qkv_scale"],
@@ -236,18 +238,20 @@ def run_gpu(args):
                 dst.copy_(src, non_blocking=True)
 
     e2e_steps = max(3, min(args.steps, 10))
-    for _ in range(2):
-        e2e_step()
-    barrier()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
-    e1.record(stream)
-    barrier()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
-    e2e_value = step_flops * world * e2e_steps / (e2e_ms * 1e-3) / 1e12
+    e2e_value = None
+    if not args.no_e2e:
+        for _ in range(2):
+            e2e_step()
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        barrier()
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+        e2e_value = round(step_flops * world * e2e_steps / (e2e_ms * 1e-3) / 1e12, 3)
 
     # ---- roofline of the dominant kernel (backward: 5/7 of the FLOPs)
     peaks, peak_src = load_peaks()
@@ -318,7 +322,7 @@ def run_gpu(args):
         "per_gpu_tflops": round(value / world, 3),
         "frac_of_peak": round(value / world / peak, 4),
         "clocks": clocks,
-        "e2e": {"value": round(e2e_value, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+        "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
                 "note": "pinned host Q,K,V,dO -> device, fwd+computeD+bwd, O,l,dQ,dK,dV -> host"},
         "gpu_launches": int(launches),
@@ -437,6 +441,9 @@ def main():
     ap.add_argument("--impl", default="native", choices=["native", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) leg")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="override the config's batch (smaller profiling case)")
     args = ap.parse_args()
     # at least 3 untimed warm-up steps, whatever the caller asks for
     args.warmup = max(args.warmup, 3)

@@ -1,0 +1,508 @@
+// flash_bwd_sm100.cu -- flashAttentionBackward (attention.metal:198-299) on
+// sm_100a with tcgen05 UMMA, TMEM accumulators and TMA.
+//
+// Work unit, as in the reference (attention.metal:219-223): one CTA owns one
+// 128-key tile of one (batch, head) and walks the query tiles i from the
+// diagonal to the end (causal: earlier queries never see these keys).  Per
+// query tile (128 queries):
+//   S^T  = K Q_i^T                 UMMA 128x128xD  -> TMEM
+//   dP^T = V dO_i^T                UMMA 128x128xD  -> TMEM
+//   P^T  = exp2(S^T c - l_i log2e), 0 where key > query   (compute warps)
+//   dS^T = P^T (dP^T - D_i) / sqrt(D)                       (compute warps)
+//   dV  += P^T dO_i                UMMA 128xDx128  (TMEM-resident)
+//   dK  += dS^T Q_i                UMMA 128xDx128  (TMEM-resident)
+//   dQ_i = dS K                    UMMA 128xDx128  -> TMEM -> smem -> TMA
+//                                  bulk reduce-add into fp32 dQ in global
+// P^T and dS^T are written once to shared memory (bf16, K-major 128-byte
+// swizzle); the dQ MMA reads the same dS^T buffer as an MN-major operand.
+// dK/dV are owned by the CTA and stored once (bf16); dQ is accumulated in
+// fp32 by the bulk reductions of every key tile, so the launcher zeroes it
+// first (the reference's host zeroes it, model.h:549).
+//
+// Roles (320 threads): warp 0 TMA producer, warp 1 TMEM owner + UMMA issuer,
+// warps 2-9 compute (thread = key row = TMEM lane; warps 2-5 take query
+// columns 0-63, warps 6-9 columns 64-127), dQ drain and dK/dV epilogue.
+// Conventions as the reference: P = exp(S/sqrt(D) - l) with l read as stored,
+// D read as stored (bf16), dS includes 1/sqrt(D).  The reference rounds S,
+// dP, P, dS and the dQ tile to bf16 and accumulates dK/dV in bf16 memory;
+// here S, dP, dQ and dK/dV stay fp32 until their single store, and P, dS are
+// bf16 (the UMMA operand type).
+//
+// All mbarrier waits are bounded (about 2 s); on time-out the CTA winds down,
+// frees its TMEM and sets STATUS_BWD_TIMEOUT.
+#include "common.cuh"
+#include "sm100.cuh"
+#include "tmap.h"
+
+namespace ma {
+namespace {
+
+using namespace sm100;
+
+constexpr int BK = 128;  // keys per CTA
+constexpr int BQ = 128;  // queries per step
+constexpr int NUM_THREADS = 320;
+constexpr int NCOMP = 256;  // compute threads
+constexpr float LOG2E = 1.4426950408889634f;
+
+template <int HD>
+struct BwdCfg {
+  static constexpr int KB = HD / 64;
+  static constexpr int STAGES = HD == 64 ? 2 : 1;
+  static constexpr bool DQ_ALIAS = HD != 64;  // dQ accumulator reuses the S^T columns
+  static constexpr uint32_t KV_BYTES = BK * HD * 2;
+  static constexpr uint32_t QD_BYTES = BQ * HD * 2;
+  static constexpr uint32_t PT_BYTES = BK * BQ * 2;
+  static constexpr uint32_t DQS_BYTES = BQ * HD * 4;
+  static constexpr uint32_t OFF_K = 0;
+  static constexpr uint32_t OFF_V = OFF_K + KV_BYTES;
+  static constexpr uint32_t OFF_Q = OFF_V + KV_BYTES;                // [STAGES]
+  static constexpr uint32_t OFF_DO = OFF_Q + STAGES * QD_BYTES;      // [STAGES]
+  static constexpr uint32_t OFF_PT = OFF_DO + STAGES * QD_BYTES;
+  static constexpr uint32_t OFF_DST = OFF_PT + PT_BYTES;
+  // dQ staging: own region for D=64, the P^T/dS^T region for D=128
+  static constexpr uint32_t OFF_DQS = HD == 64 ? OFF_DST + PT_BYTES : OFF_PT;
+  static constexpr uint32_t OFF_STAT = HD == 64 ? OFF_DQS + DQS_BYTES : OFF_DST + PT_BYTES;
+  static constexpr uint32_t STAT_BYTES = 8 * 2 * 64 * 4;  // per compute warp: 64 l, 64 D
+  static constexpr uint32_t OFF_BAR = OFF_STAT + STAT_BYTES;
+  // kv_full, qd_full[S], qd_empty[S], s_full, s_free, p_ready, p_free, dq_full, dq_free, done
+  static constexpr int NBAR = 1 + 2 * STAGES + 7;
+  static constexpr uint32_t OFF_TSLOT = OFF_BAR + NBAR * 8;
+  static constexpr uint32_t SMEM_BYTES = OFF_TSLOT + 16 + 1024;
+  static constexpr uint32_t TCOL_S = 0;
+  static constexpr uint32_t TCOL_DP = 128;
+  static constexpr uint32_t TCOL_DV = 256;
+  static constexpr uint32_t TCOL_DK = 256 + HD;
+  static constexpr uint32_t TCOL_DQ = DQ_ALIAS ? 0 : 256 + 2 * HD;
+};
+
+struct BwdParams {
+  int T, N, NH, bh_begin, nbh, nkt;
+  float scale, scale_log2;
+  const float* lse;
+  const __nv_bfloat16* Dv;
+  uint32_t* status;
+};
+
+__device__ __forceinline__ void compute_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+template <int HD>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    flash_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
+                     const __grid_constant__ CUtensorMap tmdQ, const __grid_constant__ CUtensorMap tmdK,
+                     const __grid_constant__ CUtensorMap tmdV, const BwdParams prm) {
+  using C = BwdCfg<HD>;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ int abort_flag;
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t sbase = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (sbase - raw);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  // key tiles with the most query tiles (the first ones) launch first
+  const int idx = blockIdx.x;
+  const int kt = idx / prm.nbh;
+  const int bh = prm.bh_begin + idx % prm.nbh;
+  const int b = bh / prm.NH, h = bh % prm.NH;
+  const int nq = prm.nkt - kt;  // query tiles kt .. nkt-1
+  const int col0 = h * HD;
+
+  const uint32_t bar0 = sbase + C::OFF_BAR;
+  const uint32_t BAR_KV = bar0;
+  auto BAR_QF = [&](int s) { return bar0 + 8u * (1 + s); };
+  auto BAR_QE = [&](int s) { return bar0 + 8u * (1 + C::STAGES + s); };
+  const uint32_t BAR_SF = bar0 + 8u * (1 + 2 * C::STAGES);
+  const uint32_t BAR_SE = BAR_SF + 8;
+  const uint32_t BAR_PR = BAR_SF + 16;
+  const uint32_t BAR_PE = BAR_SF + 24;
+  const uint32_t BAR_DQF = BAR_SF + 32;
+  const uint32_t BAR_DQE = BAR_SF + 40;
+  const uint32_t BAR_DONE = BAR_SF + 48;
+  const uint32_t tslot = sbase + C::OFF_TSLOT;
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    mbar_init(BAR_KV, 1);
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(BAR_QF(s), 1);
+      mbar_init(BAR_QE(s), 1);
+    }
+    mbar_init(BAR_SF, 1);
+    mbar_init(BAR_SE, NCOMP);
+    mbar_init(BAR_PR, NCOMP);
+    mbar_init(BAR_PE, 1);
+    mbar_init(BAR_DQF, 1);
+    mbar_init(BAR_DQE, NCOMP);
+    mbar_init(BAR_DONE, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tslot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(gbase + C::OFF_TSLOT);
+  volatile int* abort_p = &abort_flag;
+
+  if (warp == 0) {
+    // ------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmdO);
+      mbar_arrive_expect_tx(BAR_KV, 2 * C::KV_BYTES);
+      for (int kb = 0; kb < C::KB; ++kb) {
+        tma_load_3d(sbase + C::OFF_K + kb * BK * 128, &tmK, BAR_KV, col0 + kb * 64, kt * BK, b);
+        tma_load_3d(sbase + C::OFF_V + kb * BK * 128, &tmV, BAR_KV, col0 + kb * 64, kt * BK, b);
+      }
+      for (int i = 0; i < nq; ++i) {
+        const int st = i % C::STAGES;
+        if (i >= C::STAGES && !mbar_wait(BAR_QE(st), ((i - C::STAGES) / C::STAGES) & 1, abort_p))
+          break;
+        const int qrow = (kt + i) * BQ;
+        mbar_arrive_expect_tx(BAR_QF(st), 2 * C::QD_BYTES);
+        for (int kb = 0; kb < C::KB; ++kb) {
+          tma_load_3d(sbase + C::OFF_Q + st * C::QD_BYTES + kb * BQ * 128, &tmQ, BAR_QF(st),
+                      col0 + kb * 64, qrow, b);
+          tma_load_3d(sbase + C::OFF_DO + st * C::QD_BYTES + kb * BQ * 128, &tmdO, BAR_QF(st),
+                      col0 + kb * 64, qrow, b);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------- MMA
+    if (lane == 0) {
+      constexpr uint32_t IDESC_S = idesc_bf16_f32(BK, BQ, 0, 0);   // S^T, dP^T
+      constexpr uint32_t IDESC_KV = idesc_bf16_f32(BK, HD, 0, 1);  // dV, dK
+      constexpr uint32_t IDESC_Q = idesc_bf16_f32(BQ, HD, 1, 1);   // dQ
+      const uint32_t sk = sbase + C::OFF_K, sv = sbase + C::OFF_V;
+      const uint32_t spt = sbase + C::OFF_PT, sdst = sbase + C::OFF_DST;
+      bool ok = mbar_wait(BAR_KV, 0, abort_p);
+      // S^T_i and dP^T_i
+      auto issue_s = [&](int i) -> bool {
+        const int st = i % C::STAGES;
+        if (!mbar_wait(BAR_QF(st), (i / C::STAGES) & 1, abort_p)) return false;
+        if (i >= 1 && !mbar_wait(BAR_SE, (i - 1) & 1, abort_p)) return false;
+        if (C::DQ_ALIAS && i >= 1 && !mbar_wait(BAR_DQE, (i - 1) & 1, abort_p)) return false;
+        tc_fence_after();
+        const uint32_t sq = sbase + C::OFF_Q + st * C::QD_BYTES;
+        const uint32_t sdo = sbase + C::OFF_DO + st * C::QD_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * (BK * 128) + (kk & 3) * 32;
+          umma_bf16_ss(tmem + C::TCOL_S, smem_desc_sw128(sk + off, 16, 1024),
+                       smem_desc_sw128(sq + off, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * (BK * 128) + (kk & 3) * 32;
+          umma_bf16_ss(tmem + C::TCOL_DP, smem_desc_sw128(sv + off, 16, 1024),
+                       smem_desc_sw128(sdo + off, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(BAR_SF);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int i = 0; ok && i < nq; ++i) {
+        const int st = i % C::STAGES;
+        const uint32_t sq = sbase + C::OFF_Q + st * C::QD_BYTES;
+        const uint32_t sdo = sbase + C::OFF_DO + st * C::QD_BYTES;
+        if (!mbar_wait(BAR_PR, i & 1, abort_p)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BQ / 16; ++kk) {  // dV += P^T dO_i
+          const uint64_t ad = smem_desc_sw128(spt + (kk >> 2) * (BK * 128) + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = smem_desc_sw128(sdo + kk * 2048, BQ * 128, 1024);
+          umma_bf16_ss(tmem + C::TCOL_DV, ad, bd, IDESC_KV, (i > 0 || kk > 0) ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < BQ / 16; ++kk) {  // dK += dS^T Q_i
+          const uint64_t ad = smem_desc_sw128(sdst + (kk >> 2) * (BK * 128) + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = smem_desc_sw128(sq + kk * 2048, BQ * 128, 1024);
+          umma_bf16_ss(tmem + C::TCOL_DK, ad, bd, IDESC_KV, (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(BAR_QE(st));
+        if (!C::DQ_ALIAS && i >= 1 && !mbar_wait(BAR_DQE, (i - 1) & 1, abort_p)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) {  // dQ_i = dS K (A = dS^T as MN-major)
+          const uint64_t ad = smem_desc_sw128(sdst + kk * 2048, BK * 128, 1024);
+          const uint64_t bd = smem_desc_sw128(sk + kk * 2048, BK * 128, 1024);
+          umma_bf16_ss(tmem + C::TCOL_DQ, ad, bd, IDESC_Q, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(BAR_DQF);
+        umma_commit(BAR_PE);
+        if (i + 1 < nq) {
+          if (!issue_s(i + 1)) break;
+        } else {
+          umma_commit(BAR_DONE);
+        }
+      }
+    }
+  } else {
+    // ----------------------------------------------------------- compute
+    const int cw = warp - 2;                   // 0..7
+    const int quarter = warp & 3;              // TMEM lane quarter
+    const int krow = quarter * 32 + lane;      // key row within the tile
+    const int half = cw >> 2;                  // query columns half*64 .. +63
+    const uint32_t tl = tmem + ((uint32_t)(quarter * 32) << 16);
+    float* stat = reinterpret_cast<float*>(gbase + C::OFF_STAT) + cw * 128;  // [64 nl][64 ds]
+    const bool issuer = (cw == 0 && lane == 0);
+    // Failure handling: after a timed-out wait `ok` turns false and the work
+    // of the remaining tiles is skipped, but every thread still executes the
+    // same sequence of named barriers (compute_bar) so none can hang there.
+    bool ok = true;
+    for (int i = 0; i < nq; ++i) {
+      const int qt = kt + i;
+      if (ok) {
+        // per-query statistics of my 64 columns: -l*log2(e) and D/sqrt(D)
+        const long long rbase = (long long)b * prm.T;
+        for (int c = lane; c < 64; c += 32) {
+          const int q = qt * BQ + half * 64 + c;
+          float nl = 0.0f, dd = 0.0f;
+          if (q < prm.T) {
+            const long long si = (rbase + q) * prm.NH + h;
+            nl = -prm.lse[si] * LOG2E;
+            dd = __bfloat162float(prm.Dv[si]) * prm.scale;
+          }
+          stat[c] = nl;
+          stat[64 + c] = dd;
+        }
+        __syncwarp();
+        ok = mbar_wait_warp(BAR_SF, i & 1, abort_p);
+      }
+      if (ok) {
+        tc_fence_after();
+        float s[64], dp[64];
+        {
+          uint32_t r[32];
+          tmem_ld32(tl + C::TCOL_S + half * 64, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) s[j] = __uint_as_float(r[j]);
+          tmem_ld32(tl + C::TCOL_S + half * 64 + 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) s[32 + j] = __uint_as_float(r[j]);
+          tmem_ld32(tl + C::TCOL_DP + half * 64, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) dp[j] = __uint_as_float(r[j]);
+          tmem_ld32(tl + C::TCOL_DP + half * 64 + 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) dp[32 + j] = __uint_as_float(r[j]);
+        }
+        tc_fence_before();
+        mbar_arrive(BAR_SE);
+        const float c = prm.scale_log2, sc = prm.scale;
+        const bool diag = (i == 0);
+#pragma unroll
+        for (int j = 0; j < 64; j += 4) {
+          const float4 nl = *reinterpret_cast<const float4*>(stat + j);
+          const float4 dd = *reinterpret_cast<const float4*>(stat + 64 + j);
+          const float nla[4] = {nl.x, nl.y, nl.z, nl.w};
+          const float dda[4] = {dd.x, dd.y, dd.z, dd.w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            float p = ex2(fmaf(s[j + u], c, nla[u]));
+            if (diag && krow > half * 64 + j + u) p = 0.0f;  // key after query
+            s[j + u] = p;
+            dp[j + u] = p * fmaf(dp[j + u], sc, -dda[u]);
+          }
+        }
+        // P^T / dS^T buffers are free once the previous tile's MMAs are done
+        if (i >= 1) ok = mbar_wait_warp(BAR_PE, (i - 1) & 1, abort_p);
+        if (ok) {
+          uint8_t* pt = gbase + C::OFF_PT + half * (BK * 128) + krow * 128;
+          uint8_t* dst = gbase + C::OFF_DST + half * (BK * 128) + krow * 128;
+#pragma unroll
+          for (int ch = 0; ch < 8; ++ch) {
+            const int c0 = ch * 8;
+            uint4 v, w;
+            v.x = pack_bf16(s[c0 + 0], s[c0 + 1]);
+            v.y = pack_bf16(s[c0 + 2], s[c0 + 3]);
+            v.z = pack_bf16(s[c0 + 4], s[c0 + 5]);
+            v.w = pack_bf16(s[c0 + 6], s[c0 + 7]);
+            w.x = pack_bf16(dp[c0 + 0], dp[c0 + 1]);
+            w.y = pack_bf16(dp[c0 + 2], dp[c0 + 3]);
+            w.z = pack_bf16(dp[c0 + 4], dp[c0 + 5]);
+            w.w = pack_bf16(dp[c0 + 6], dp[c0 + 7]);
+            const int sw = (ch ^ (krow & 7)) * 16;
+            *reinterpret_cast<uint4*>(pt + sw) = v;
+            *reinterpret_cast<uint4*>(dst + sw) = w;
+          }
+          fence_proxy_async_smem();
+          tc_fence_before();
+          mbar_arrive(BAR_PR);
+          // ---- dQ_i: TMEM -> smem (fp32, 128-byte swizzle) -> bulk reduce-add
+          ok = mbar_wait_warp(BAR_DQF, i & 1, abort_p);
+        }
+      }
+      if (ok) {
+        tc_fence_after();
+        // thread = query row (TMEM lane); this half takes columns half*HD/2 ..
+        constexpr int CPH = HD / 2;  // columns per half
+        const int qrow = quarter * 32 + lane;
+        uint8_t* dqs = gbase + C::OFF_DQS;
+#pragma unroll
+        for (int cc = 0; cc < CPH; cc += 32) {
+          uint32_t r[32];
+          tmem_ld32(tl + C::TCOL_DQ + half * CPH + cc, r);
+          tmem_wait_ld();
+          // 32 fp32 = one 128-byte row of box (half*CPH + cc)/32
+          const int box = (half * CPH + cc) / 32;
+          uint8_t* rowp = dqs + box * (BQ * 128) + qrow * 128;
+#pragma unroll
+          for (int ch = 0; ch < 8; ++ch) {
+            uint4 v = make_uint4(r[ch * 4 + 0], r[ch * 4 + 1], r[ch * 4 + 2], r[ch * 4 + 3]);
+            *reinterpret_cast<uint4*>(rowp + ((ch ^ (qrow & 7)) * 16)) = v;
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(BAR_DQE);
+        fence_proxy_async_smem();
+      }
+      compute_bar();
+      if (issuer && ok && !*abort_p) {
+        for (int box = 0; box < HD / 32; ++box)
+          tma_reduce_add_3d(&tmdQ, sbase + C::OFF_DQS + box * (BQ * 128), col0 + box * 32, qt * BQ, b);
+        bulk_commit();
+        bulk_wait_read<0>();  // the staging buffer is rewritten by the next tile
+      }
+      compute_bar();
+    }
+    // --------------------------------------------- dK / dV epilogue
+    const bool epi = ok && mbar_wait_warp(BAR_DONE, 0, abort_p);
+    if (epi) {
+      tc_fence_after();
+      // stage dV then dK (bf16) in the P^T / dS^T regions, one row per thread-half
+      constexpr int CPH = HD / 2;
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
+        const uint32_t tcol = which == 0 ? C::TCOL_DV : C::TCOL_DK;
+        uint8_t* stage = gbase + (which == 0 ? C::OFF_PT : C::OFF_DST);
+#pragma unroll
+        for (int cc = 0; cc < CPH; cc += 16) {
+          uint32_t r[16];
+          tmem_ld16(tl + tcol + half * CPH + cc, r);
+          tmem_wait_ld();
+          const int col = half * CPH + cc;  // column within the head
+          const int kb = col / 64, ch = (col % 64) / 8;
+          uint8_t* rowp = stage + kb * (BK * 128) + krow * 128;
+          uint4 v0, v1;
+          v0.x = pack_bf16(__uint_as_float(r[0]), __uint_as_float(r[1]));
+          v0.y = pack_bf16(__uint_as_float(r[2]), __uint_as_float(r[3]));
+          v0.z = pack_bf16(__uint_as_float(r[4]), __uint_as_float(r[5]));
+          v0.w = pack_bf16(__uint_as_float(r[6]), __uint_as_float(r[7]));
+          v1.x = pack_bf16(__uint_as_float(r[8]), __uint_as_float(r[9]));
+          v1.y = pack_bf16(__uint_as_float(r[10]), __uint_as_float(r[11]));
+          v1.z = pack_bf16(__uint_as_float(r[12]), __uint_as_float(r[13]));
+          v1.w = pack_bf16(__uint_as_float(r[14]), __uint_as_float(r[15]));
+          *reinterpret_cast<uint4*>(rowp + ((ch ^ (krow & 7)) * 16)) = v0;
+          *reinterpret_cast<uint4*>(rowp + (((ch + 1) ^ (krow & 7)) * 16)) = v1;
+        }
+      }
+      fence_proxy_async_smem();
+    }
+    compute_bar();
+    if (epi && issuer) {
+      for (int kb = 0; kb < C::KB; ++kb) {
+        tma_store_3d(&tmdV, sbase + C::OFF_PT + kb * BK * 128, col0 + kb * 64, kt * BK, b);
+        tma_store_3d(&tmdK, sbase + C::OFF_DST + kb * BK * 128, col0 + kb * 64, kt * BK, b);
+      }
+      bulk_commit();
+      bulk_wait<0>();
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+  if (threadIdx.x == 0 && abort_flag) atomicOr(prm.status, STATUS_BWD_TIMEOUT);
+}
+
+// Zeroes the dQ columns of the (batch, head) shard range.
+__global__ void zero_dq_shard_kernel(float4* __restrict__ dQ, int T, int N, int D, int NH,
+                                     int bh_begin, int bh_end) {
+  const long long per_bh = (long long)T * (D / 4);
+  const long long total = (long long)(bh_end - bh_begin) * per_bh;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long bh = bh_begin + i / per_bh;
+    const long long rem = i % per_bh;
+    const long long t = rem / (D / 4), c4 = rem % (D / 4);
+    const long long bb = bh / NH, hh = bh % NH;
+    dQ[((bb * T + t) * N + hh * D) / 4 + c4] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+
+template <int HD>
+cudaError_t launch_bwd(const __nv_bfloat16* dO, const __nv_bfloat16* Dv, const float* lse,
+                       const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* v,
+                       float* dQ, __nv_bfloat16* dK, __nv_bfloat16* dV, const AttnShape& s,
+                       uint32_t* status, cudaStream_t st) {
+  using C = BwdCfg<HD>;
+  CUtensorMap tq, tk, tv, tdo, tdq, tdk, tdv;
+  const CUtensorMapDataType bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B;
+  if (!make_tmap_3d(&tq, q, bf, 2, s.N, s.T, s.B, 64, BQ, sw) ||
+      !make_tmap_3d(&tk, k, bf, 2, s.N, s.T, s.B, 64, BK, sw) ||
+      !make_tmap_3d(&tv, v, bf, 2, s.N, s.T, s.B, 64, BK, sw) ||
+      !make_tmap_3d(&tdo, dO, bf, 2, s.N, s.T, s.B, 64, BQ, sw) ||
+      !make_tmap_3d(&tdq, dQ, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, s.N, s.T, s.B, 32, BQ, sw) ||
+      !make_tmap_3d(&tdk, dK, bf, 2, s.N, s.T, s.B, 64, BK, sw) ||
+      !make_tmap_3d(&tdv, dV, bf, 2, s.N, s.T, s.B, 64, BK, sw))
+    return cudaErrorInvalidValue;
+  // dQ is accumulated by bulk reductions: zero the shard's columns first
+  const int nbh = s.bh_end - s.bh_begin;
+  cudaError_t e;
+  if (s.bh_begin == 0 && s.bh_end == s.B * s.NH) {
+    e = cudaMemsetAsync(dQ, 0, (size_t)s.B * s.T * s.N * sizeof(float), st);
+  } else {
+    zero_dq_shard_kernel<<<1184, 256, 0, st>>>(reinterpret_cast<float4*>(dQ), s.T, s.N, s.D, s.NH,
+                                              s.bh_begin, s.bh_end);
+    count_launches(1);
+    e = cudaGetLastError();
+  }
+  if (e != cudaSuccess) return e;
+  BwdParams prm;
+  prm.T = s.T;
+  prm.N = s.N;
+  prm.NH = s.NH;
+  prm.bh_begin = s.bh_begin;
+  prm.nbh = nbh;
+  prm.nkt = (s.T + BK - 1) / BK;
+  prm.scale = 1.0f / sqrtf((float)HD);
+  prm.scale_log2 = LOG2E / sqrtf((float)HD);
+  prm.lse = lse;
+  prm.Dv = Dv;
+  prm.status = status;
+  e = cudaFuncSetAttribute(flash_bwd_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           C::SMEM_BYTES);
+  if (e != cudaSuccess) return e;
+  const long long nblocks = (long long)prm.nkt * nbh;
+  flash_bwd_kernel<HD><<<(unsigned)nblocks, NUM_THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, tdo, tdq,
+                                                                            tdk, tdv, prm);
+  count_launches(1);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_flash_bwd(const __nv_bfloat16* dO, const __nv_bfloat16* Dv,
+                             const float* lse, const __nv_bfloat16* q,
+                             const __nv_bfloat16* k, const __nv_bfloat16* v, float* dQ,
+                             __nv_bfloat16* dK, __nv_bfloat16* dV, const AttnShape& s,
+                             uint32_t* status, cudaStream_t st) {
+  if (s.bh_end <= s.bh_begin) return cudaSuccess;
+  return s.D == 64 ? launch_bwd<64>(dO, Dv, lse, q, k, v, dQ, dK, dV, s, status, st)
+                   : launch_bwd<128>(dO, Dv, lse, q, k, v, dQ, dK, dV, s, status, st);
+}
+
+}  // namespace ma

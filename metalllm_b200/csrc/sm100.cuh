@@ -80,6 +80,14 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   }
 }
 
+// mbar_wait for roles that run whole warps: the result is made warp-uniform
+// (all lanes fail if any lane failed), so warp-collective instructions that
+// follow (tcgen05.ld/st, shuffles, votes) always see a converged warp.
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, volatile int* abort) {
+  const bool ok = mbar_wait(bar, parity, abort);
+  return __all_sync(0xffffffffu, ok);
+}
+
 // ------------------------------------------------------------------ TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -256,6 +264,13 @@ __device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t col, uin
   const uint32_t blk = col >> 6, c = col & 63u;
   const uint32_t chunk = (c >> 3) ^ (row & 7u);
   return blk * rows * 128u + row * 128u + chunk * 16u + (c & 7u) * 2u;
+}
+
+// 2^x with the MUFU.EX2 hardware approximation (PTX ex2.approx.ftz.f32).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
