@@ -31,6 +31,7 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 from metalllm_b200.inputs import CONFIGS, attention_inputs, causal_flops  # noqa: E402
+from metalllm_b200.shards import plan as plan_shards  # noqa: E402
 
 METRIC = "causal bf16 FlashAttn fwd+bwd TFLOP/s per GPU, % tensor peak, at 1/2/4/8 GPUs"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
@@ -135,38 +136,57 @@ def run_gpu(args):
     if args.batch:
         B = args.batch  # smaller case of the same shape (profiling); not a bench line
     p = A.make_params(T, H, D)
-    # this rank's shards: batch rows [rank*B, (rank+1)*B) of the global N*B batch
-    host = attention_inputs(B, T, H, D, seed=args.seed + rank, qkv_scale=c["qkv_scale"],
-                            do_scale=c["do_scale"])
+    if args.mode == "weak":
+        # every rank owns a whole batch of the config: global batch = world * B
+        seed = args.seed + rank
+        Bl, shard = B, None
+        nshards = B * H
+        global_shards = B * H * world
+        row_offset = 0
+    else:
+        # the config's B*H shards split evenly over the ranks (strong scaling)
+        sp = plan_shards(B, H, world, rank)
+        seed = args.seed
+        Bl, shard = sp.local_batch, (sp.local_bh_begin, sp.local_bh_end)
+        nshards = sp.shards
+        global_shards = B * H
+        row_offset = sp.b_begin
+    n_local = Bl * T * H * D
+    from metalllm_b200.inputs import STREAM_DO, STREAM_K, STREAM_Q, STREAM_V, normal_bf16
+    host = {name: normal_bf16(n_local, seed, stream, sc, offset=row_offset * T * H * D).reshape(Bl, T, H * D)
+            for name, stream, sc in (("q", STREAM_Q, c["qkv_scale"]), ("k", STREAM_K, c["qkv_scale"]),
+                                     ("v", STREAM_V, c["qkv_scale"]), ("do", STREAM_DO, c["do_scale"]))}
 
     def pinned(bits):
         t = torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16)
         return t.pin_memory()
 
     h_q, h_k, h_v, h_do = (pinned(host[n]) for n in ("q", "k", "v", "do"))
-    act = (B, T, H * D)
+    act = (Bl, T, H * D)
     q, k, v, do = (t.to(dev) for t in (h_q, h_k, h_v, h_do))
     out = torch.empty(act, dtype=torch.bfloat16, device=dev)
-    l = torch.empty((B, T, H), dtype=torch.float32, device=dev)
-    Dv = torch.empty((B, T, H), dtype=torch.bfloat16, device=dev)
+    l = torch.empty((Bl, T, H), dtype=torch.float32, device=dev)
+    Dv = torch.empty((Bl, T, H), dtype=torch.bfloat16, device=dev)
     dQ = torch.empty(act, dtype=torch.float32, device=dev)
     dK = torch.empty(act, dtype=torch.bfloat16, device=dev)
     dV = torch.empty(act, dtype=torch.bfloat16, device=dev)
     stream = torch.cuda.Stream(device=dev)
 
-    fwd_flops, bwd_flops = causal_flops(B, T, H, D)
+    fwd1, bwd1 = causal_flops(1, T, 1, D)           # per (batch, head) shard
+    fwd_flops, bwd_flops = fwd1 * nshards, bwd1 * nshards
     step_flops = fwd_flops + bwd_flops
 
     def step(ev=None):
         if ev is not None:
             ev[0].record(stream)
-        A.flashAttentionForward(q, k, v, p, B, out=out, l=l, stream=stream)
+        A.flashAttentionForward(q, k, v, p, Bl, out=out, l=l, shard=shard, stream=stream)
         if ev is not None:
             ev[1].record(stream)
-        A.computeD(do, out, p, B, D=Dv, stream=stream)
+        A.computeD(do, out, p, Bl, D=Dv, shard=shard, stream=stream)
         if ev is not None:
             ev[2].record(stream)
-        A.flashAttentionBackward(do, Dv, l, q, k, v, p, B, dQ=dQ, dK=dK, dV=dV, stream=stream)
+        A.flashAttentionBackward(do, Dv, l, q, k, v, p, Bl, dQ=dQ, dK=dK, dV=dV, shard=shard,
+                                 stream=stream)
         if ev is not None:
             ev[3].record(stream)
 
@@ -197,18 +217,29 @@ def run_gpu(args):
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
     start = torch.cuda.Event(enable_timing=True)
     stop = torch.cuda.Event(enable_timing=True)
+    # inputs smaller than L2 (126 MB): overwrite a 256 MB buffer before every
+    # step, outside the per-step events, and time the steps only
+    flush = None
+    if 4 * n_local * 2 <= 126e6:
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     sampler.start()
     time.sleep(0.3)
     launches0 = lib.ma_kernel_launch_count()
     barrier()
     start.record(stream)
     for i in range(args.steps):
+        if flush is not None:
+            with torch.cuda.stream(stream):
+                flush.fill_(i & 0xFF)
         step(evs[i])
     stop.record(stream)
     barrier()
     launches = lib.ma_kernel_launch_count() - launches0
     clocks = sampler.stop()
-    elapsed_ms = start.elapsed_time(stop)
+    if flush is None:
+        elapsed_ms = start.elapsed_time(stop)
+    else:
+        elapsed_ms = sum(e[0].elapsed_time(e[3]) for e in evs)
     fwd_ms = [e[0].elapsed_time(e[1]) for e in evs]
     d_ms = [e[1].elapsed_time(e[2]) for e in evs]
     bwd_ms = [e[2].elapsed_time(e[3]) for e in evs]
@@ -216,12 +247,12 @@ def run_gpu(args):
         raise RuntimeError("a kernel reported a timeout during the timed region")
     elapsed_ms = max_over_ranks(elapsed_ms)
     ms_per_step = elapsed_ms / args.steps
-    total_flops = step_flops * world * args.steps
+    total_flops = (fwd1 + bwd1) * global_shards * args.steps
     value = total_flops / (elapsed_ms * 1e-3) / 1e12
 
     # ---- end to end through the public API with host buffers (pinned)
     h_out = torch.empty(act, dtype=torch.bfloat16).pin_memory()
-    h_l = torch.empty((B, T, H), dtype=torch.float32).pin_memory()
+    h_l = torch.empty((Bl, T, H), dtype=torch.float32).pin_memory()
     h_dQ = torch.empty(act, dtype=torch.float32).pin_memory()
     h_dK = torch.empty(act, dtype=torch.bfloat16).pin_memory()
     h_dV = torch.empty(act, dtype=torch.bfloat16).pin_memory()
@@ -251,7 +282,7 @@ def run_gpu(args):
         e1.record(stream)
         barrier()
         e2e_ms = max_over_ranks(e0.elapsed_time(e1))
-        e2e_value = round(step_flops * world * e2e_steps / (e2e_ms * 1e-3) / 1e12, 3)
+        e2e_value = round((fwd1 + bwd1) * global_shards * e2e_steps / (e2e_ms * 1e-3) / 1e12, 3)
 
     # ---- roofline of the dominant kernel (backward: 5/7 of the FLOPs)
     peaks, peak_src = load_peaks()
@@ -263,7 +294,7 @@ def run_gpu(args):
     d_avg = statistics.mean(d_ms)
     bwd_tflops = bwd_flops / (bwd_avg * 1e-3) / 1e12
     fwd_tflops = fwd_flops / (fwd_avg * 1e-3) / 1e12
-    d_bytes = 2 * (B * T * H * D) * 2 + B * T * H * 2
+    d_bytes = (2 * T * D * 2 + T * 2) * nshards
     d_gbs = d_bytes / (d_avg * 1e-3) / 1e9
     traffic = None
     tfile = ROOT / "profiles" / "traffic.json"
@@ -307,16 +338,17 @@ def run_gpu(args):
         "warmup": args.warmup,
         "ms_per_step": round(ms_per_step, 4),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": args.mode,
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic: Q,K,V,dO i.i.d. normal (splitmix64 + Box-Muller, seed %d), bf16" % args.seed,
         "config": {
             "workload": workload_desc(args.config),
-            "B_per_gpu": B, "T": T, "H": H, "d": D, "causal": True,
-            "global_batch": B * world,
-            "parallelism": f"(batch x head) shards, {B * H} per GPU, no collective",
-            "l2": "inputs larger than L2 (Q,K,V,dO = %.1f MB per step > 126 MB)" % (4 * B * T * H * D * 2 / 1e6),
+            "B_per_gpu": Bl, "T": T, "H": H, "d": D, "causal": True,
+            "global_batch": B * world if args.mode == "weak" else B,
+            "parallelism": f"(batch x head) shards, {nshards} on rank 0 of {global_shards}, no collective",
+            "l2": ("inputs larger than L2 (Q,K,V,dO = %.1f MB per step per GPU > 126 MB)" % (4 * n_local * 2 / 1e6))
+                  if flush is None else "L2 flushed (256 MB write) before every step, outside the timed steps",
             "flops_convention": "fwd 2*B*H*T^2*d + bwd 5*B*H*T^2*d (causal T^2/2 pairs)",
         },
         "per_gpu_tflops": round(value / world, 3),
@@ -442,6 +474,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) leg")
+    ap.add_argument("--mode", default="weak", choices=["weak", "strong"],
+                    help="weak: each GPU runs a whole config batch; strong: the config's "
+                         "(batch, head) shards are split over the GPUs")
     ap.add_argument("--batch", type=int, default=0,
                     help="override the config's batch (smaller profiling case)")
     args = ap.parse_args()
