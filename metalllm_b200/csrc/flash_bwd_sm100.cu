@@ -19,9 +19,22 @@
 // fp32 by the bulk reductions of every key tile, so the launcher zeroes it
 // first (the reference's host zeroes it, model.h:549).
 //
-// Roles (320 threads): warp 0 TMA producer, warp 1 TMEM owner + UMMA issuer,
-// warps 2-9 compute (thread = key row = TMEM lane; warps 2-5 take query
-// columns 0-63, warps 6-9 columns 64-127), dQ drain and dK/dV epilogue.
+// Roles (320 threads):
+//   warp 0     producer: TMA for K/V once and Q_i/dO_i per stage; its 32 lanes
+//              also stage the per-query statistics -l_i*log2(e) and
+//              -D_i/sqrt(D) (strided in global memory) into shared memory
+//   warp 1     TMEM owner; lane 0 issues every UMMA and commit
+//   warps 2-9  compute: thread = key row = TMEM lane; warps 2-5 take query
+//              columns 0-63, warps 6-9 columns 64-127; dQ drain and dK/dV
+//              epilogue (thread = TMEM lane of the respective accumulator)
+// D=64 schedule ("early S"): S^T/dP^T of tile i+1 are issued as soon as the
+// compute warps have read tile i's, so they run on the tensor core while the
+// compute warps form P^T_i/dS^T_i; dV_i, dK_i and dQ_i follow P^T_i.  dQ_{i-1}
+// is drained after P^T_i is handed over, and its bulk reduction is left in
+// flight until the next drain.  D=128 has no TMEM room for that (S^T, dP^T, dV,
+// dK fill all 512 columns; dQ reuses the S^T columns) and runs the steps in
+// order, draining dQ_i before S^T_{i+1}.
+//
 // Conventions as the reference: P = exp(S/sqrt(D) - l) with l read as stored,
 // D read as stored (bf16), dS includes 1/sqrt(D).  The reference rounds S,
 // dP, P, dS and the dQ tile to bf16 and accumulates dK/dV in bf16 memory;
@@ -29,7 +42,8 @@
 // bf16 (the UMMA operand type).
 //
 // All mbarrier waits are bounded (about 2 s); on time-out the CTA winds down,
-// frees its TMEM and sets STATUS_BWD_TIMEOUT.
+// frees its TMEM and sets STATUS_BWD_TIMEOUT.  Compute warps execute the same
+// named-barrier sequence whether or not a wait failed.
 #include "common.cuh"
 #include "sm100.cuh"
 #include "tmap.h"
@@ -50,10 +64,12 @@ struct BwdCfg {
   static constexpr int KB = HD / 64;
   static constexpr int STAGES = HD == 64 ? 2 : 1;
   static constexpr bool DQ_ALIAS = HD != 64;  // dQ accumulator reuses the S^T columns
+  static constexpr bool EARLY_S = !DQ_ALIAS;
   static constexpr uint32_t KV_BYTES = BK * HD * 2;
   static constexpr uint32_t QD_BYTES = BQ * HD * 2;
   static constexpr uint32_t PT_BYTES = BK * BQ * 2;
   static constexpr uint32_t DQS_BYTES = BQ * HD * 4;
+  static constexpr uint32_t STAT_BYTES = 2 * BQ * 4;  // per stage: -l*log2e[128], -D/sqrt(D)[128]
   static constexpr uint32_t OFF_K = 0;
   static constexpr uint32_t OFF_V = OFF_K + KV_BYTES;
   static constexpr uint32_t OFF_Q = OFF_V + KV_BYTES;                // [STAGES]
@@ -63,8 +79,7 @@ struct BwdCfg {
   // dQ staging: own region for D=64, the P^T/dS^T region for D=128
   static constexpr uint32_t OFF_DQS = HD == 64 ? OFF_DST + PT_BYTES : OFF_PT;
   static constexpr uint32_t OFF_STAT = HD == 64 ? OFF_DQS + DQS_BYTES : OFF_DST + PT_BYTES;
-  static constexpr uint32_t STAT_BYTES = 8 * 2 * 64 * 4;  // per compute warp: 64 l, 64 D
-  static constexpr uint32_t OFF_BAR = OFF_STAT + STAT_BYTES;
+  static constexpr uint32_t OFF_BAR = OFF_STAT + STAGES * STAT_BYTES;
   // kv_full, qd_full[S], qd_empty[S], s_full, s_free, p_ready, p_free, dq_full, dq_free, done
   static constexpr int NBAR = 1 + 2 * STAGES + 7;
   static constexpr uint32_t OFF_TSLOT = OFF_BAR + NBAR * 8;
@@ -86,8 +101,44 @@ struct BwdParams {
 
 __device__ __forceinline__ void compute_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
+// P^T and dS^T for 64 query columns of one key row.  s[] holds S^T on entry
+// and P^T on exit; dp[] holds dP^T on entry and dS^T on exit.  nl = -l*log2e
+// and nd = -D/sqrt(D) per query column (shared memory, broadcast reads).
+template <bool DIAG>
+__device__ __forceinline__ void p_ds_row(float (&s)[64], float (&dp)[64], const float* nl,
+                                         const float* nd, float c, float sc, int krow, int qcol0) {
+  const float2 c2 = make_float2(c, c), sc2 = make_float2(sc, sc);
+#pragma unroll
+  for (int j = 0; j < 64; j += 4) {
+    const float4 L = *reinterpret_cast<const float4*>(nl + j);
+    const float4 Dn = *reinterpret_cast<const float4*>(nd + j);
+    const float2 t0 = __ffma2_rn(make_float2(s[j], s[j + 1]), c2, make_float2(L.x, L.y));
+    const float2 t1 = __ffma2_rn(make_float2(s[j + 2], s[j + 3]), c2, make_float2(L.z, L.w));
+    float p0 = ex2(t0.x), p1 = ex2(t0.y), p2 = ex2(t1.x), p3 = ex2(t1.y);
+    if (DIAG) {  // key after query: P = 0 (attention.metal:282)
+      const int q = qcol0 + j;
+      if (krow > q) p0 = 0.0f;
+      if (krow > q + 1) p1 = 0.0f;
+      if (krow > q + 2) p2 = 0.0f;
+      if (krow > q + 3) p3 = 0.0f;
+    }
+    const float2 d0 = __ffma2_rn(make_float2(dp[j], dp[j + 1]), sc2, make_float2(Dn.x, Dn.y));
+    const float2 d1 = __ffma2_rn(make_float2(dp[j + 2], dp[j + 3]), sc2, make_float2(Dn.z, Dn.w));
+    const float2 r0 = __fmul2_rn(make_float2(p0, p1), d0);
+    const float2 r1 = __fmul2_rn(make_float2(p2, p3), d1);
+    s[j] = p0;
+    s[j + 1] = p1;
+    s[j + 2] = p2;
+    s[j + 3] = p3;
+    dp[j] = r0.x;
+    dp[j + 1] = r0.y;
+    dp[j + 2] = r1.x;
+    dp[j + 3] = r1.y;
+  }
+}
+
 template <int HD>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+__global__ void __maxnreg__(200)
     flash_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
                      const __grid_constant__ CUtensorMap tmdQ, const __grid_constant__ CUtensorMap tmdK,
@@ -120,12 +171,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t BAR_DQE = BAR_SF + 40;
   const uint32_t BAR_DONE = BAR_SF + 48;
   const uint32_t tslot = sbase + C::OFF_TSLOT;
+  float* stat_base = reinterpret_cast<float*>(gbase + C::OFF_STAT);
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
     mbar_init(BAR_KV, 1);
     for (int s = 0; s < C::STAGES; ++s) {
-      mbar_init(BAR_QF(s), 1);
+      mbar_init(BAR_QF(s), 1 + 32);  // TMA expect_tx arrival + 32 statistics lanes
       mbar_init(BAR_QE(s), 1);
     }
     mbar_init(BAR_SF, 1);
@@ -148,7 +200,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   volatile int* abort_p = &abort_flag;
 
   if (warp == 0) {
-    // ------------------------------------------------------ TMA producer
+    // ------------------------------------------------------------ producer
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmdO);
@@ -157,22 +209,42 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tma_load_3d(sbase + C::OFF_K + kb * BK * 128, &tmK, BAR_KV, col0 + kb * 64, kt * BK, b);
         tma_load_3d(sbase + C::OFF_V + kb * BK * 128, &tmV, BAR_KV, col0 + kb * 64, kt * BK, b);
       }
-      for (int i = 0; i < nq; ++i) {
-        const int st = i % C::STAGES;
-        if (i >= C::STAGES && !mbar_wait(BAR_QE(st), ((i - C::STAGES) / C::STAGES) & 1, abort_p))
-          break;
-        const int qrow = (kt + i) * BQ;
+    }
+    const long long rbase = (long long)b * prm.T;
+    for (int i = 0; i < nq; ++i) {
+      const int st = i % C::STAGES;
+      if (i >= C::STAGES &&
+          !mbar_wait_warp(BAR_QE(st), ((i - C::STAGES) / C::STAGES) & 1, abort_p))
+        break;
+      const int qt = kt + i;
+      if (lane == 0) {
         mbar_arrive_expect_tx(BAR_QF(st), 2 * C::QD_BYTES);
         for (int kb = 0; kb < C::KB; ++kb) {
           tma_load_3d(sbase + C::OFF_Q + st * C::QD_BYTES + kb * BQ * 128, &tmQ, BAR_QF(st),
-                      col0 + kb * 64, qrow, b);
+                      col0 + kb * 64, qt * BQ, b);
           tma_load_3d(sbase + C::OFF_DO + st * C::QD_BYTES + kb * BQ * 128, &tmdO, BAR_QF(st),
-                      col0 + kb * 64, qrow, b);
+                      col0 + kb * 64, qt * BQ, b);
         }
       }
+      // per-query statistics of the tile: 4 queries per lane
+      float* stt = stat_base + st * (2 * BQ);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int qi = lane * 4 + u;
+        const int q = qt * BQ + qi;
+        float nl = 0.0f, nd = 0.0f;
+        if (q < prm.T) {
+          const long long si = (rbase + q) * prm.NH + h;
+          nl = -__ldg(prm.lse + si) * LOG2E;
+          nd = -__bfloat162float(prm.Dv[si]) * prm.scale;
+        }
+        stt[qi] = nl;
+        stt[BQ + qi] = nd;
+      }
+      mbar_arrive(BAR_QF(st));
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------- MMA
+    // ------------------------------------------------------------------ MMA
     if (lane == 0) {
       constexpr uint32_t IDESC_S = idesc_bf16_f32(BK, BQ, 0, 0);   // S^T, dP^T
       constexpr uint32_t IDESC_KV = idesc_bf16_f32(BK, HD, 0, 1);  // dV, dK
@@ -180,7 +252,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const uint32_t sk = sbase + C::OFF_K, sv = sbase + C::OFF_V;
       const uint32_t spt = sbase + C::OFF_PT, sdst = sbase + C::OFF_DST;
       bool ok = mbar_wait(BAR_KV, 0, abort_p);
-      // S^T_i and dP^T_i
+      // S^T_i and dP^T_i into their TMEM columns
       auto issue_s = [&](int i) -> bool {
         const int st = i % C::STAGES;
         if (!mbar_wait(BAR_QF(st), (i / C::STAGES) & 1, abort_p)) return false;
@@ -206,6 +278,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       };
       if (ok) ok = issue_s(0);
       for (int i = 0; ok && i < nq; ++i) {
+        if (C::EARLY_S && i + 1 < nq && !issue_s(i + 1)) break;
         const int st = i % C::STAGES;
         const uint32_t sq = sbase + C::OFF_Q + st * C::QD_BYTES;
         const uint32_t sdo = sbase + C::OFF_DO + st * C::QD_BYTES;
@@ -224,7 +297,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           umma_bf16_ss(tmem + C::TCOL_DK, ad, bd, IDESC_KV, (i > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(BAR_QE(st));
-        if (!C::DQ_ALIAS && i >= 1 && !mbar_wait(BAR_DQE, (i - 1) & 1, abort_p)) break;
+        // the dQ columns must have been drained (dQ_{i-1})
+        if (i >= 1 && !mbar_wait(BAR_DQE, (i - 1) & 1, abort_p)) break;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk) {  // dQ_i = dS K (A = dS^T as MN-major)
@@ -234,131 +308,49 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         umma_commit(BAR_DQF);
         umma_commit(BAR_PE);
-        if (i + 1 < nq) {
-          if (!issue_s(i + 1)) break;
-        } else {
-          umma_commit(BAR_DONE);
-        }
+        if (!C::EARLY_S && i + 1 < nq && !issue_s(i + 1)) break;
+        if (i + 1 == nq) umma_commit(BAR_DONE);
       }
     }
   } else {
-    // ----------------------------------------------------------- compute
+    // -------------------------------------------------------------- compute
     const int cw = warp - 2;                   // 0..7
     const int quarter = warp & 3;              // TMEM lane quarter
-    const int krow = quarter * 32 + lane;      // key row within the tile
+    const int krow = quarter * 32 + lane;      // key row (and dQ query row) within the tile
     const int half = cw >> 2;                  // query columns half*64 .. +63
     const uint32_t tl = tmem + ((uint32_t)(quarter * 32) << 16);
-    float* stat = reinterpret_cast<float*>(gbase + C::OFF_STAT) + cw * 128;  // [64 nl][64 ds]
     const bool issuer = (cw == 0 && lane == 0);
+    const float c = prm.scale_log2, sc = prm.scale;
     // Failure handling: after a timed-out wait `ok` turns false and the work
     // of the remaining tiles is skipped, but every thread still executes the
     // same sequence of named barriers (compute_bar) so none can hang there.
     bool ok = true;
-    for (int i = 0; i < nq; ++i) {
-      const int qt = kt + i;
-      if (ok) {
-        // per-query statistics of my 64 columns: -l*log2(e) and D/sqrt(D)
-        const long long rbase = (long long)b * prm.T;
-        for (int c = lane; c < 64; c += 32) {
-          const int q = qt * BQ + half * 64 + c;
-          float nl = 0.0f, dd = 0.0f;
-          if (q < prm.T) {
-            const long long si = (rbase + q) * prm.NH + h;
-            nl = -prm.lse[si] * LOG2E;
-            dd = __bfloat162float(prm.Dv[si]) * prm.scale;
-          }
-          stat[c] = nl;
-          stat[64 + c] = dd;
-        }
-        __syncwarp();
-        ok = mbar_wait_warp(BAR_SF, i & 1, abort_p);
+
+    // dQ_j: TMEM -> fp32 staging (128-byte swizzle, 32-column boxes) -> TMA
+    // bulk reduce-add.  D=64 leaves the reduction in flight (its staging
+    // buffer is private); D=128 stages in the P^T/dS^T buffers and waits for
+    // the reduction to have read them before they are rewritten.
+    auto drain_dq = [&](int j) {
+      if (ok) ok = mbar_wait_warp(BAR_DQF, j & 1, abort_p);
+      if (C::EARLY_S) {
+        if (issuer) bulk_wait_read<0>();  // the previous reduction has read the staging
+        compute_bar();
       }
       if (ok) {
         tc_fence_after();
-        float s[64], dp[64];
-        {
-          uint32_t r[32];
-          tmem_ld32(tl + C::TCOL_S + half * 64, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 32; ++j) s[j] = __uint_as_float(r[j]);
-          tmem_ld32(tl + C::TCOL_S + half * 64 + 32, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 32; ++j) s[32 + j] = __uint_as_float(r[j]);
-          tmem_ld32(tl + C::TCOL_DP + half * 64, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 32; ++j) dp[j] = __uint_as_float(r[j]);
-          tmem_ld32(tl + C::TCOL_DP + half * 64 + 32, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 32; ++j) dp[32 + j] = __uint_as_float(r[j]);
-        }
-        tc_fence_before();
-        mbar_arrive(BAR_SE);
-        const float c = prm.scale_log2, sc = prm.scale;
-        const bool diag = (i == 0);
-#pragma unroll
-        for (int j = 0; j < 64; j += 4) {
-          const float4 nl = *reinterpret_cast<const float4*>(stat + j);
-          const float4 dd = *reinterpret_cast<const float4*>(stat + 64 + j);
-          const float nla[4] = {nl.x, nl.y, nl.z, nl.w};
-          const float dda[4] = {dd.x, dd.y, dd.z, dd.w};
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            float p = ex2(fmaf(s[j + u], c, nla[u]));
-            if (diag && krow > half * 64 + j + u) p = 0.0f;  // key after query
-            s[j + u] = p;
-            dp[j + u] = p * fmaf(dp[j + u], sc, -dda[u]);
-          }
-        }
-        // P^T / dS^T buffers are free once the previous tile's MMAs are done
-        if (i >= 1) ok = mbar_wait_warp(BAR_PE, (i - 1) & 1, abort_p);
-        if (ok) {
-          uint8_t* pt = gbase + C::OFF_PT + half * (BK * 128) + krow * 128;
-          uint8_t* dst = gbase + C::OFF_DST + half * (BK * 128) + krow * 128;
-#pragma unroll
-          for (int ch = 0; ch < 8; ++ch) {
-            const int c0 = ch * 8;
-            uint4 v, w;
-            v.x = pack_bf16(s[c0 + 0], s[c0 + 1]);
-            v.y = pack_bf16(s[c0 + 2], s[c0 + 3]);
-            v.z = pack_bf16(s[c0 + 4], s[c0 + 5]);
-            v.w = pack_bf16(s[c0 + 6], s[c0 + 7]);
-            w.x = pack_bf16(dp[c0 + 0], dp[c0 + 1]);
-            w.y = pack_bf16(dp[c0 + 2], dp[c0 + 3]);
-            w.z = pack_bf16(dp[c0 + 4], dp[c0 + 5]);
-            w.w = pack_bf16(dp[c0 + 6], dp[c0 + 7]);
-            const int sw = (ch ^ (krow & 7)) * 16;
-            *reinterpret_cast<uint4*>(pt + sw) = v;
-            *reinterpret_cast<uint4*>(dst + sw) = w;
-          }
-          fence_proxy_async_smem();
-          tc_fence_before();
-          mbar_arrive(BAR_PR);
-          // ---- dQ_i: TMEM -> smem (fp32, 128-byte swizzle) -> bulk reduce-add
-          ok = mbar_wait_warp(BAR_DQF, i & 1, abort_p);
-        }
-      }
-      if (ok) {
-        tc_fence_after();
-        // thread = query row (TMEM lane); this half takes columns half*HD/2 ..
         constexpr int CPH = HD / 2;  // columns per half
-        const int qrow = quarter * 32 + lane;
         uint8_t* dqs = gbase + C::OFF_DQS;
 #pragma unroll
         for (int cc = 0; cc < CPH; cc += 32) {
           uint32_t r[32];
           tmem_ld32(tl + C::TCOL_DQ + half * CPH + cc, r);
-          tmem_wait_ld();
-          // 32 fp32 = one 128-byte row of box (half*CPH + cc)/32
+          tmem_wait_ld_dep(r);
           const int box = (half * CPH + cc) / 32;
-          uint8_t* rowp = dqs + box * (BQ * 128) + qrow * 128;
+          uint8_t* rowp = dqs + box * (BQ * 128) + krow * 128;
 #pragma unroll
           for (int ch = 0; ch < 8; ++ch) {
             uint4 v = make_uint4(r[ch * 4 + 0], r[ch * 4 + 1], r[ch * 4 + 2], r[ch * 4 + 3]);
-            *reinterpret_cast<uint4*>(rowp + ((ch ^ (qrow & 7)) * 16)) = v;
+            *reinterpret_cast<uint4*>(rowp + ((ch ^ (krow & 7)) * 16)) = v;
           }
         }
         tc_fence_before();
@@ -367,14 +359,80 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       compute_bar();
       if (issuer && ok && !*abort_p) {
+        const int qt = kt + j;
         for (int box = 0; box < HD / 32; ++box)
           tma_reduce_add_3d(&tmdQ, sbase + C::OFF_DQS + box * (BQ * 128), col0 + box * 32, qt * BQ, b);
         bulk_commit();
-        bulk_wait_read<0>();  // the staging buffer is rewritten by the next tile
+        if (!C::EARLY_S) bulk_wait_read<0>();
       }
-      compute_bar();
+      if (!C::EARLY_S) compute_bar();
+    };
+
+    for (int i = 0; i < nq; ++i) {
+      const int st = i % C::STAGES;
+      if (ok) ok = mbar_wait_warp(BAR_SF, i & 1, abort_p);
+      float s[64], dp[64];
+      if (ok) {
+        tc_fence_after();
+        uint32_t ra[32], rb[32];
+        tmem_ld32(tl + C::TCOL_S + half * 64, ra);
+        tmem_ld32(tl + C::TCOL_S + half * 64 + 32, rb);
+        tmem_wait_ld_dep(ra, rb);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          s[j] = __uint_as_float(ra[j]);
+          s[32 + j] = __uint_as_float(rb[j]);
+        }
+        tmem_ld32(tl + C::TCOL_DP + half * 64, ra);
+        tmem_ld32(tl + C::TCOL_DP + half * 64 + 32, rb);
+        tmem_wait_ld_dep(ra, rb);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          dp[j] = __uint_as_float(ra[j]);
+          dp[32 + j] = __uint_as_float(rb[j]);
+        }
+        tc_fence_before();
+        mbar_arrive(BAR_SE);
+        // statistics of this tile were staged with Q_i/dO_i (BAR_QF), which
+        // completed before S^T_i could be computed
+        const float* stt = stat_base + st * (2 * BQ) + half * 64;
+        if (i == 0) p_ds_row<true>(s, dp, stt, stt + BQ, c, sc, krow, half * 64);
+        else p_ds_row<false>(s, dp, stt, stt + BQ, c, sc, krow, half * 64);
+        // P^T / dS^T buffers are free once the previous tile's MMAs are done
+        if (i >= 1) ok = mbar_wait_warp(BAR_PE, (i - 1) & 1, abort_p);
+      }
+      if (ok) {
+        uint8_t* pt = gbase + C::OFF_PT + half * (BK * 128) + krow * 128;
+        uint8_t* dst = gbase + C::OFF_DST + half * (BK * 128) + krow * 128;
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch) {
+          const int c0 = ch * 8;
+          uint4 v, w;
+          v.x = pack_bf16(s[c0 + 0], s[c0 + 1]);
+          v.y = pack_bf16(s[c0 + 2], s[c0 + 3]);
+          v.z = pack_bf16(s[c0 + 4], s[c0 + 5]);
+          v.w = pack_bf16(s[c0 + 6], s[c0 + 7]);
+          w.x = pack_bf16(dp[c0 + 0], dp[c0 + 1]);
+          w.y = pack_bf16(dp[c0 + 2], dp[c0 + 3]);
+          w.z = pack_bf16(dp[c0 + 4], dp[c0 + 5]);
+          w.w = pack_bf16(dp[c0 + 6], dp[c0 + 7]);
+          const int sw = (ch ^ (krow & 7)) * 16;
+          *reinterpret_cast<uint4*>(pt + sw) = v;
+          *reinterpret_cast<uint4*>(dst + sw) = w;
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(BAR_PR);
+      }
+      if (C::EARLY_S) {
+        if (i >= 1) drain_dq(i - 1);
+      } else {
+        drain_dq(i);
+      }
     }
-    // --------------------------------------------- dK / dV epilogue
+    if (C::EARLY_S && nq >= 1) drain_dq(nq - 1);
+
+    // ------------------------------------------------ dK / dV epilogue
     const bool epi = ok && mbar_wait_warp(BAR_DONE, 0, abort_p);
     if (epi) {
       tc_fence_after();
@@ -388,7 +446,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int cc = 0; cc < CPH; cc += 16) {
           uint32_t r[16];
           tmem_ld16(tl + tcol + half * CPH + cc, r);
-          tmem_wait_ld();
+          tmem_wait_ld_dep(r);
           const int col = half * CPH + cc;  // column within the head
           const int kb = col / 64, ch = (col % 64) / 8;
           uint8_t* rowp = stage + kb * (BK * 128) + krow * 128;
@@ -408,13 +466,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       fence_proxy_async_smem();
     }
     compute_bar();
-    if (epi && issuer) {
-      for (int kb = 0; kb < C::KB; ++kb) {
-        tma_store_3d(&tmdV, sbase + C::OFF_PT + kb * BK * 128, col0 + kb * 64, kt * BK, b);
-        tma_store_3d(&tmdK, sbase + C::OFF_DST + kb * BK * 128, col0 + kb * 64, kt * BK, b);
+    if (issuer) {
+      if (epi) {
+        for (int kb = 0; kb < C::KB; ++kb) {
+          tma_store_3d(&tmdV, sbase + C::OFF_PT + kb * BK * 128, col0 + kb * 64, kt * BK, b);
+          tma_store_3d(&tmdK, sbase + C::OFF_DST + kb * BK * 128, col0 + kb * 64, kt * BK, b);
+        }
+        bulk_commit();
       }
-      bulk_commit();
-      bulk_wait<0>();
+      bulk_wait<0>();  // every bulk operation of this CTA has completed
     }
   }
 

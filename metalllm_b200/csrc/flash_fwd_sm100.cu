@@ -213,12 +213,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after();
       float s[BN];
 #pragma unroll
-      for (int cc = 0; cc < BN; cc += 32) {
-        uint32_t r[32];
-        tmem_ld32(trow + C::TCOL_S + sb * BN + cc, r);
-        tmem_wait_ld();
+      for (int cc = 0; cc < BN; cc += 64) {
+        uint32_t ra[32], rb[32];
+        tmem_ld32(trow + C::TCOL_S + sb * BN + cc, ra);
+        tmem_ld32(trow + C::TCOL_S + sb * BN + cc + 32, rb);
+        tmem_wait_ld_dep(ra, rb);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) s[cc + i] = __uint_as_float(r[i]);
+        for (int i = 0; i < 32; ++i) {
+          s[cc + i] = __uint_as_float(ra[i]);
+          s[cc + 32 + i] = __uint_as_float(rb[i]);
+        }
       }
       tc_fence_before();
       mbar_arrive(BAR_SE(sb));
@@ -227,9 +231,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int i = 0; i < BN; ++i)
           if (i > row) s[i] = -INFINITY;
       }
-      float mx = -INFINITY;
+      // row maximum with 8 independent partial maxima (short dependency chains)
+      float pm[8];
 #pragma unroll
-      for (int i = 0; i < BN; ++i) mx = fmaxf(mx, s[i]);
+      for (int u = 0; u < 8; ++u) pm[u] = s[u];
+#pragma unroll
+      for (int i = 8; i < BN; i += 8)
+#pragma unroll
+        for (int u = 0; u < 8; ++u) pm[u] = fmaxf(pm[u], s[i + u]);
+      const float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
+                             fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
       const float m_new = fmaxf(m_used, mx * c);
       if (j == 0) {
         m_used = m_new;
@@ -249,7 +260,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           for (int cc = 0; cc < HD; cc += 16) {
             uint32_t r[16];
             tmem_ld16(trow + C::TCOL_O + cc, r);
-            tmem_wait_ld();
+            tmem_wait_ld_dep(r);
 #pragma unroll
             for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
             tmem_st16(trow + C::TCOL_O + cc, r);
@@ -257,13 +268,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tmem_wait_st();
         }
       }
-      const float neg_m = -m_used;
-      float rs = 0.0f;
+      // P = 2^(S*c - m) with packed fp32x2 FMAs; row sum in 4 packed partials
+      const float2 c2 = make_float2(c, c), nm2 = make_float2(-m_used, -m_used);
+      float2 ps[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                      make_float2(0.f, 0.f)};
 #pragma unroll
-      for (int i = 0; i < BN; ++i) {
-        s[i] = ex2(fmaf(s[i], c, neg_m));
-        rs += s[i];
+      for (int i = 0; i < BN; i += 2) {
+        const float2 t = __ffma2_rn(make_float2(s[i], s[i + 1]), c2, nm2);
+        s[i] = ex2(t.x);
+        s[i + 1] = ex2(t.y);
+        ps[(i >> 1) & 3] = __fadd2_rn(ps[(i >> 1) & 3], make_float2(s[i], s[i + 1]));
       }
+      const float rs = (ps[0].x + ps[0].y) + (ps[1].x + ps[1].y) + (ps[2].x + ps[2].y) +
+                       (ps[3].x + ps[3].y);
       l_sum += rs;
       if (j >= C::PBUF && !mbar_wait_warp(BAR_PE(pb), ((j - C::PBUF) / C::PBUF) & 1, abort_p)) { ok = false; break; }
       uint8_t* prow = gbase + C::OFF_P + pb * C::P_BYTES;
@@ -295,7 +312,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int cc = 0; cc < HD; cc += 16) {
         uint32_t r[16];
         tmem_ld16(trow + C::TCOL_O + cc, r);
-        tmem_wait_ld();
+        tmem_wait_ld_dep(r);
         uint4 v0, v1;
         v0.x = pack_bf16(__uint_as_float(r[0]) * inv, __uint_as_float(r[1]) * inv);
         v0.y = pack_bf16(__uint_as_float(r[2]) * inv, __uint_as_float(r[3]) * inv);
