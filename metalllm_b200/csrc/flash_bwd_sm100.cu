@@ -138,7 +138,7 @@ __device__ __forceinline__ void p_ds_row(float (&s)[64], float (&dp)[64], const 
 }
 
 template <int HD>
-__global__ void __maxnreg__(200)
+__global__ void __launch_bounds__(NUM_THREADS, 1)
     flash_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
                      const __grid_constant__ CUtensorMap tmdQ, const __grid_constant__ CUtensorMap tmdK,
