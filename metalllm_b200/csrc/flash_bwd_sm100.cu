@@ -19,14 +19,16 @@
 // fp32 by the bulk reductions of every key tile, so the launcher zeroes it
 // first (the reference's host zeroes it, model.h:549).
 //
-// Roles (320 threads):
-//   warp 0     producer: TMA for K/V once and Q_i/dO_i per stage; its 32 lanes
+// Roles (384 threads, three warpgroups):
+//   warpgroup 0 (120 registers per thread after setmaxnreg):
+//     warp 0   producer: TMA for K/V once and Q_i/dO_i per stage; its 32 lanes
 //              also stage the per-query statistics -l_i*log2(e) and
 //              -D_i/sqrt(D) (strided in global memory) into shared memory
-//   warp 1     TMEM owner; lane 0 issues every UMMA and commit
-//   warps 2-9  compute: thread = key row = TMEM lane; warps 2-5 take query
-//              columns 0-63, warps 6-9 columns 64-127; dQ drain and dK/dV
-//              epilogue (thread = TMEM lane of the respective accumulator)
+//     warp 1   TMEM owner; lane 0 issues every UMMA and commit
+//   warpgroups 1, 2 (192 registers): compute, thread = key row = TMEM lane;
+//              warpgroup 1 takes query columns 0-63, warpgroup 2 columns
+//              64-127; dQ drain and dK/dV epilogue (thread = TMEM lane of the
+//              respective accumulator)
 // D=64 schedule ("early S"): S^T/dP^T of tile i+1 are issued as soon as the
 // compute warps have read tile i's, so they run on the tensor core while the
 // compute warps form P^T_i/dS^T_i; dV_i, dK_i and dQ_i follow P^T_i.  dQ_{i-1}
@@ -55,8 +57,13 @@ using namespace sm100;
 
 constexpr int BK = 128;  // keys per CTA
 constexpr int BQ = 128;  // queries per step
-constexpr int NUM_THREADS = 320;
-constexpr int NCOMP = 256;  // compute threads
+constexpr int NUM_THREADS = 384;
+constexpr int NCOMP = 256;  // compute threads (warpgroups 1 and 2)
+constexpr int LAUNCH_REGS = 168;    // 65536 / 384, rounded down to a multiple of 8
+constexpr int REGS_PRODUCER = 120;  // warpgroup 0 after setmaxnreg.dec
+constexpr int REGS_COMPUTE = 192;   // warpgroups 1, 2 after setmaxnreg.inc
+static_assert(128 * REGS_PRODUCER + 256 * REGS_COMPUTE == NUM_THREADS * LAUNCH_REGS,
+              "register split must equal the launch allocation");
 constexpr float LOG2E = 1.4426950408889634f;
 
 template <int HD>
@@ -199,122 +206,126 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(gbase + C::OFF_TSLOT);
   volatile int* abort_p = &abort_flag;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      tma_prefetch_desc(&tmQ);
-      tma_prefetch_desc(&tmdO);
-      mbar_arrive_expect_tx(BAR_KV, 2 * C::KV_BYTES);
-      for (int kb = 0; kb < C::KB; ++kb) {
-        tma_load_3d(sbase + C::OFF_K + kb * BK * 128, &tmK, BAR_KV, col0 + kb * 64, kt * BK, b);
-        tma_load_3d(sbase + C::OFF_V + kb * BK * 128, &tmV, BAR_KV, col0 + kb * 64, kt * BK, b);
-      }
-    }
-    const long long rbase = (long long)b * prm.T;
-    for (int i = 0; i < nq; ++i) {
-      const int st = i % C::STAGES;
-      if (i >= C::STAGES &&
-          !mbar_wait_warp(BAR_QE(st), ((i - C::STAGES) / C::STAGES) & 1, abort_p))
-        break;
-      const int qt = kt + i;
+  if (warp < 4) {
+    reg_dealloc<REGS_PRODUCER>();
+    if (warp == 0) {
+      // ------------------------------------------------------------ producer
       if (lane == 0) {
-        mbar_arrive_expect_tx(BAR_QF(st), 2 * C::QD_BYTES);
+        tma_prefetch_desc(&tmQ);
+        tma_prefetch_desc(&tmdO);
+        mbar_arrive_expect_tx(BAR_KV, 2 * C::KV_BYTES);
         for (int kb = 0; kb < C::KB; ++kb) {
-          tma_load_3d(sbase + C::OFF_Q + st * C::QD_BYTES + kb * BQ * 128, &tmQ, BAR_QF(st),
-                      col0 + kb * 64, qt * BQ, b);
-          tma_load_3d(sbase + C::OFF_DO + st * C::QD_BYTES + kb * BQ * 128, &tmdO, BAR_QF(st),
-                      col0 + kb * 64, qt * BQ, b);
+          tma_load_3d(sbase + C::OFF_K + kb * BK * 128, &tmK, BAR_KV, col0 + kb * 64, kt * BK, b);
+          tma_load_3d(sbase + C::OFF_V + kb * BK * 128, &tmV, BAR_KV, col0 + kb * 64, kt * BK, b);
         }
       }
-      // per-query statistics of the tile: 4 queries per lane
-      float* stt = stat_base + st * (2 * BQ);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int qi = lane * 4 + u;
-        const int q = qt * BQ + qi;
-        float nl = 0.0f, nd = 0.0f;
-        if (q < prm.T) {
-          const long long si = (rbase + q) * prm.NH + h;
-          nl = -__ldg(prm.lse + si) * LOG2E;
-          nd = -__bfloat162float(prm.Dv[si]) * prm.scale;
+      const long long rbase = (long long)b * prm.T;
+      for (int i = 0; i < nq; ++i) {
+        const int st = i % C::STAGES;
+        if (i >= C::STAGES &&
+            !mbar_wait_warp(BAR_QE(st), ((i - C::STAGES) / C::STAGES) & 1, abort_p))
+          break;
+        const int qt = kt + i;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(BAR_QF(st), 2 * C::QD_BYTES);
+          for (int kb = 0; kb < C::KB; ++kb) {
+            tma_load_3d(sbase + C::OFF_Q + st * C::QD_BYTES + kb * BQ * 128, &tmQ, BAR_QF(st),
+                        col0 + kb * 64, qt * BQ, b);
+            tma_load_3d(sbase + C::OFF_DO + st * C::QD_BYTES + kb * BQ * 128, &tmdO, BAR_QF(st),
+                        col0 + kb * 64, qt * BQ, b);
+          }
         }
-        stt[qi] = nl;
-        stt[BQ + qi] = nd;
+        // per-query statistics of the tile: 4 queries per lane
+        float* stt = stat_base + st * (2 * BQ);
+  #pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int qi = lane * 4 + u;
+          const int q = qt * BQ + qi;
+          float nl = 0.0f, nd = 0.0f;
+          if (q < prm.T) {
+            const long long si = (rbase + q) * prm.NH + h;
+            nl = -__ldg(prm.lse + si) * LOG2E;
+            nd = -__bfloat162float(prm.Dv[si]) * prm.scale;
+          }
+          stt[qi] = nl;
+          stt[BQ + qi] = nd;
+        }
+        mbar_arrive(BAR_QF(st));
       }
-      mbar_arrive(BAR_QF(st));
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA
-    if (lane == 0) {
-      constexpr uint32_t IDESC_S = idesc_bf16_f32(BK, BQ, 0, 0);   // S^T, dP^T
-      constexpr uint32_t IDESC_KV = idesc_bf16_f32(BK, HD, 0, 1);  // dV, dK
-      constexpr uint32_t IDESC_Q = idesc_bf16_f32(BQ, HD, 1, 1);   // dQ
-      const uint32_t sk = sbase + C::OFF_K, sv = sbase + C::OFF_V;
-      const uint32_t spt = sbase + C::OFF_PT, sdst = sbase + C::OFF_DST;
-      bool ok = mbar_wait(BAR_KV, 0, abort_p);
-      // S^T_i and dP^T_i into their TMEM columns
-      auto issue_s = [&](int i) -> bool {
-        const int st = i % C::STAGES;
-        if (!mbar_wait(BAR_QF(st), (i / C::STAGES) & 1, abort_p)) return false;
-        if (i >= 1 && !mbar_wait(BAR_SE, (i - 1) & 1, abort_p)) return false;
-        if (C::DQ_ALIAS && i >= 1 && !mbar_wait(BAR_DQE, (i - 1) & 1, abort_p)) return false;
-        tc_fence_after();
-        const uint32_t sq = sbase + C::OFF_Q + st * C::QD_BYTES;
-        const uint32_t sdo = sbase + C::OFF_DO + st * C::QD_BYTES;
-#pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * (BK * 128) + (kk & 3) * 32;
-          umma_bf16_ss(tmem + C::TCOL_S, smem_desc_sw128(sk + off, 16, 1024),
-                       smem_desc_sw128(sq + off, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
+    } else if (warp == 1) {
+      // ------------------------------------------------------------------ MMA
+      if (lane == 0) {
+        constexpr uint32_t IDESC_S = idesc_bf16_f32(BK, BQ, 0, 0);   // S^T, dP^T
+        constexpr uint32_t IDESC_KV = idesc_bf16_f32(BK, HD, 0, 1);  // dV, dK
+        constexpr uint32_t IDESC_Q = idesc_bf16_f32(BQ, HD, 1, 1);   // dQ
+        const uint32_t sk = sbase + C::OFF_K, sv = sbase + C::OFF_V;
+        const uint32_t spt = sbase + C::OFF_PT, sdst = sbase + C::OFF_DST;
+        bool ok = mbar_wait(BAR_KV, 0, abort_p);
+        // S^T_i and dP^T_i into their TMEM columns
+        auto issue_s = [&](int i) -> bool {
+          const int st = i % C::STAGES;
+          if (!mbar_wait(BAR_QF(st), (i / C::STAGES) & 1, abort_p)) return false;
+          if (i >= 1 && !mbar_wait(BAR_SE, (i - 1) & 1, abort_p)) return false;
+          if (C::DQ_ALIAS && i >= 1 && !mbar_wait(BAR_DQE, (i - 1) & 1, abort_p)) return false;
+          tc_fence_after();
+          const uint32_t sq = sbase + C::OFF_Q + st * C::QD_BYTES;
+          const uint32_t sdo = sbase + C::OFF_DO + st * C::QD_BYTES;
+  #pragma unroll
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * (BK * 128) + (kk & 3) * 32;
+            umma_bf16_ss(tmem + C::TCOL_S, smem_desc_sw128(sk + off, 16, 1024),
+                         smem_desc_sw128(sq + off, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
+          }
+  #pragma unroll
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * (BK * 128) + (kk & 3) * 32;
+            umma_bf16_ss(tmem + C::TCOL_DP, smem_desc_sw128(sv + off, 16, 1024),
+                         smem_desc_sw128(sdo + off, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(BAR_SF);
+          return true;
+        };
+        if (ok) ok = issue_s(0);
+        for (int i = 0; ok && i < nq; ++i) {
+          if (C::EARLY_S && i + 1 < nq && !issue_s(i + 1)) break;
+          const int st = i % C::STAGES;
+          const uint32_t sq = sbase + C::OFF_Q + st * C::QD_BYTES;
+          const uint32_t sdo = sbase + C::OFF_DO + st * C::QD_BYTES;
+          if (!mbar_wait(BAR_PR, i & 1, abort_p)) break;
+          tc_fence_after();
+  #pragma unroll
+          for (int kk = 0; kk < BQ / 16; ++kk) {  // dV += P^T dO_i
+            const uint64_t ad = smem_desc_sw128(spt + (kk >> 2) * (BK * 128) + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd = smem_desc_sw128(sdo + kk * 2048, BQ * 128, 1024);
+            umma_bf16_ss(tmem + C::TCOL_DV, ad, bd, IDESC_KV, (i > 0 || kk > 0) ? 1u : 0u);
+          }
+  #pragma unroll
+          for (int kk = 0; kk < BQ / 16; ++kk) {  // dK += dS^T Q_i
+            const uint64_t ad = smem_desc_sw128(sdst + (kk >> 2) * (BK * 128) + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd = smem_desc_sw128(sq + kk * 2048, BQ * 128, 1024);
+            umma_bf16_ss(tmem + C::TCOL_DK, ad, bd, IDESC_KV, (i > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(BAR_QE(st));
+          // the dQ columns must have been drained (dQ_{i-1})
+          if (i >= 1 && !mbar_wait(BAR_DQE, (i - 1) & 1, abort_p)) break;
+          tc_fence_after();
+  #pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {  // dQ_i = dS K (A = dS^T as MN-major)
+            const uint64_t ad = smem_desc_sw128(sdst + kk * 2048, BK * 128, 1024);
+            const uint64_t bd = smem_desc_sw128(sk + kk * 2048, BK * 128, 1024);
+            umma_bf16_ss(tmem + C::TCOL_DQ, ad, bd, IDESC_Q, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(BAR_DQF);
+          umma_commit(BAR_PE);
+          if (!C::EARLY_S && i + 1 < nq && !issue_s(i + 1)) break;
+          if (i + 1 == nq) umma_commit(BAR_DONE);
         }
-#pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * (BK * 128) + (kk & 3) * 32;
-          umma_bf16_ss(tmem + C::TCOL_DP, smem_desc_sw128(sv + off, 16, 1024),
-                       smem_desc_sw128(sdo + off, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
-        }
-        umma_commit(BAR_SF);
-        return true;
-      };
-      if (ok) ok = issue_s(0);
-      for (int i = 0; ok && i < nq; ++i) {
-        if (C::EARLY_S && i + 1 < nq && !issue_s(i + 1)) break;
-        const int st = i % C::STAGES;
-        const uint32_t sq = sbase + C::OFF_Q + st * C::QD_BYTES;
-        const uint32_t sdo = sbase + C::OFF_DO + st * C::QD_BYTES;
-        if (!mbar_wait(BAR_PR, i & 1, abort_p)) break;
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < BQ / 16; ++kk) {  // dV += P^T dO_i
-          const uint64_t ad = smem_desc_sw128(spt + (kk >> 2) * (BK * 128) + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = smem_desc_sw128(sdo + kk * 2048, BQ * 128, 1024);
-          umma_bf16_ss(tmem + C::TCOL_DV, ad, bd, IDESC_KV, (i > 0 || kk > 0) ? 1u : 0u);
-        }
-#pragma unroll
-        for (int kk = 0; kk < BQ / 16; ++kk) {  // dK += dS^T Q_i
-          const uint64_t ad = smem_desc_sw128(sdst + (kk >> 2) * (BK * 128) + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = smem_desc_sw128(sq + kk * 2048, BQ * 128, 1024);
-          umma_bf16_ss(tmem + C::TCOL_DK, ad, bd, IDESC_KV, (i > 0 || kk > 0) ? 1u : 0u);
-        }
-        umma_commit(BAR_QE(st));
-        // the dQ columns must have been drained (dQ_{i-1})
-        if (i >= 1 && !mbar_wait(BAR_DQE, (i - 1) & 1, abort_p)) break;
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk) {  // dQ_i = dS K (A = dS^T as MN-major)
-          const uint64_t ad = smem_desc_sw128(sdst + kk * 2048, BK * 128, 1024);
-          const uint64_t bd = smem_desc_sw128(sk + kk * 2048, BK * 128, 1024);
-          umma_bf16_ss(tmem + C::TCOL_DQ, ad, bd, IDESC_Q, kk > 0 ? 1u : 0u);
-        }
-        umma_commit(BAR_DQF);
-        umma_commit(BAR_PE);
-        if (!C::EARLY_S && i + 1 < nq && !issue_s(i + 1)) break;
-        if (i + 1 == nq) umma_commit(BAR_DONE);
       }
     }
   } else {
+    reg_alloc<REGS_COMPUTE>();
     // -------------------------------------------------------------- compute
-    const int cw = warp - 2;                   // 0..7
+    const int cw = warp - 4;                   // 0..7
     const int quarter = warp & 3;              // TMEM lane quarter
     const int krow = quarter * 32 + lane;      // key row (and dQ query row) within the tile
     const int half = cw >> 2;                  // query columns half*64 .. +63
@@ -508,6 +519,15 @@ cudaError_t launch_bwd(const __nv_bfloat16* dO, const __nv_bfloat16* Dv, const f
                        float* dQ, __nv_bfloat16* dK, __nv_bfloat16* dV, const AttnShape& s,
                        uint32_t* status, cudaStream_t st) {
   using C = BwdCfg<HD>;
+  // The setmaxnreg split assumes the kernel was compiled to exactly
+  // LAUNCH_REGS registers per thread; refuse to launch otherwise.
+  static const cudaError_t reg_check = [] {
+    cudaFuncAttributes a;
+    cudaError_t e = cudaFuncGetAttributes(&a, flash_bwd_kernel<HD>);
+    if (e != cudaSuccess) return e;
+    return a.numRegs == LAUNCH_REGS ? cudaSuccess : cudaErrorInvalidKernelImage;
+  }();
+  if (reg_check != cudaSuccess) return reg_check;
   CUtensorMap tq, tk, tv, tdo, tdq, tdk, tdv;
   const CUtensorMapDataType bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B;

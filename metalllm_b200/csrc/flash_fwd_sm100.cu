@@ -1,24 +1,32 @@
 // flash_fwd_sm100.cu -- flashAttentionForward (attention.metal:56-164) on
 // sm_100a: tcgen05 UMMA with TMEM accumulators, TMA-staged Q/K/V tiles in
 // 128-byte-swizzled shared memory, an mbarrier pipeline and warp-specialised
-// roles.
+// roles in a persistent kernel.
 //
-// Work unit: one CTA per (batch*head, 128-row query tile); tiles with the most
-// causal work are launched first.  Per key tile j (128 keys):
-//   S_j  = Q K_j^T            UMMA 128x128xD, fp32 in TMEM (double-buffered)
-//   P_j  = exp2(S_j*c - m)    softmax warps, c = log2(e)/sqrt(D), bf16 to smem
-//   O   += P_j V_j            UMMA 128xDx128, fp32 in TMEM
-// Roles (192 threads):
-//   warp 0     TMA producer: Q once, K/V tiles into a STAGES-deep ring
-//   warp 1     owns TMEM; lane 0 issues every UMMA and commit
-//   warps 2-5  softmax: thread = query row = TMEM lane; row max/sum in
-//              registers, lazy O rescaling (only when the running max grows by
-//              more than 2^8), epilogue O/l -> bf16 via smem + TMA store, and
-//              l = m + ln(rowsum) in fp32.
+// Work unit: one (batch*head, 256-row query pair) = two 128-row query tiles
+// A (rows 256p..256p+127) and B (the next 128 rows).  Units are ordered
+// heaviest first (causal work grows with p) and dealt round-robin to one CTA
+// per SM.  Per key tile j (128 keys) of a unit:
+//   S_X  = Q_X K_j^T          UMMA 128x128xD, fp32 in TMEM      (X = A, B)
+//   P_X  = exp2(S_X c - m_X)  softmax warpgroup X, c = log2(e)/sqrt(D), bf16
+//   O_X += P_X V_j            UMMA 128xDx128, fp32 in TMEM
+// Tile A needs key tiles 0..2p, tile B 0..2p+1 (causal).  The UMMA issue order
+// S_A(j) S_B(j) | PV_A(j) S_A(j+1) | PV_B(j) S_B(j+1) | ... keeps the tensor
+// core busy with one tile while the other tile's softmax runs (ping-pong), and
+// K_j/V_j are loaded once for both tiles.
+// Roles (384 threads, three warpgroups):
+//   warpgroup 0  warp 0 TMA producer (Q pair per unit, K/V tile rings);
+//                warp 1 owns TMEM (S_A, S_B, O_A, O_B) and issues every UMMA;
+//                runs on 120 registers per thread (setmaxnreg)
+//   warpgroups 1, 2  softmax of tile A resp. B on 192 registers: thread =
+//                query row = TMEM lane; row max/sum in registers, lazy O
+//                rescaling (only when the running max grows by more than 2^8),
+//                epilogue O/rowsum -> bf16 -> smem -> TMA store, and
+//                l = m + ln(rowsum) in fp32.
 // Conventions match the reference: scale 1/sqrt(D) applied to Q K^T, key >
-// query masked, l stored fp32 at [row*NH + head], O = (sum P V) / rowsum.
-// S stays fp32 (the reference rounds it to bf16); P is bf16 as in the
-// reference (attention.metal:139,153).
+// query masked, l stored fp32 at [row*NH + head], O = (sum P V) / rowsum.  S
+// stays fp32 (the reference rounds it to bf16); P is bf16 as in the reference
+// (attention.metal:139,153).
 //
 // Every mbarrier wait is bounded (about 2 s); on time-out the CTA sets an
 // abort flag that all roles poll, winds down, frees its TMEM and sets
@@ -32,43 +40,66 @@ namespace {
 
 using namespace sm100;
 
-constexpr int BM = 128;  // query rows per CTA
+constexpr int BM = 128;  // query rows per tile
 constexpr int BN = 128;  // keys per tile
-constexpr int NUM_THREADS = 192;
+constexpr int NUM_THREADS = 384;
+constexpr int LAUNCH_REGS = 168;    // 65536 / 384, rounded down to a multiple of 8
+constexpr int REGS_PRODUCER = 120;  // warpgroup 0 after setmaxnreg.dec
+constexpr int REGS_SOFTMAX = 192;  // warpgroups 1, 2 after setmaxnreg.inc
+static_assert(128 * REGS_PRODUCER + 256 * REGS_SOFTMAX == NUM_THREADS * LAUNCH_REGS,
+              "register split must equal the launch allocation");
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float LN2 = 0.6931471805599453f;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
 
 template <int HD>
 struct FwdCfg {
-  static constexpr int KB = HD / 64;                 // 64-column blocks per row
-  static constexpr int STAGES = 2;
-  static constexpr int PBUF = HD == 64 ? 2 : 1;
-  static constexpr uint32_t Q_BYTES = BM * HD * 2;
+  static constexpr int KB = HD / 64;  // 64-column blocks per row
+  static constexpr int QST = HD == 64 ? 2 : 1;  // Q-pair stages
+  static constexpr int KST = 2;                 // K tile stages
+  static constexpr int VST = HD == 64 ? 2 : 1;  // V tile stages
+  static constexpr uint32_t QT_BYTES = BM * HD * 2;  // one query tile
   static constexpr uint32_t KV_BYTES = BN * HD * 2;
   static constexpr uint32_t P_BYTES = BM * BN * 2;
   // shared memory map (offsets from a 1024-aligned base)
-  static constexpr uint32_t OFF_Q = 0;
-  static constexpr uint32_t OFF_K = OFF_Q + Q_BYTES;
-  static constexpr uint32_t OFF_V = OFF_K + STAGES * KV_BYTES;
-  static constexpr uint32_t OFF_P = OFF_V + STAGES * KV_BYTES;
-  static constexpr uint32_t OFF_BAR = OFF_P + PBUF * P_BYTES;
-  // barriers: q_full, k_full[S], v_full[S], kv_empty[S], s_full[2], s_free[2],
-  // p_full[PB], p_free[PB], o_full
-  static constexpr int NBAR = 1 + 3 * STAGES + 4 + 2 * PBUF + 1;
+  static constexpr uint32_t OFF_Q = 0;                          // [QST][2 tiles]
+  static constexpr uint32_t OFF_K = OFF_Q + QST * 2 * QT_BYTES;  // [KST]
+  static constexpr uint32_t OFF_V = OFF_K + KST * KV_BYTES;      // [VST]
+  static constexpr uint32_t OFF_P = OFF_V + VST * KV_BYTES;      // [2 tiles]
+  static constexpr uint32_t OFF_BAR = OFF_P + 2 * P_BYTES;
+  // q_full/empty[QST], k_full/empty[KST], v_full/empty[VST], per tile X:
+  // s_full, s_free, p_full, pv_done, o_free
+  static constexpr int NBAR = 2 * QST + 2 * KST + 2 * VST + 2 * 5;
   static constexpr uint32_t OFF_TSLOT = OFF_BAR + NBAR * 8;
   static constexpr uint32_t SMEM_BYTES = OFF_TSLOT + 16 + 1024;  // + alignment slack
-  static constexpr uint32_t TMEM_COLS = 512;
-  static constexpr uint32_t TCOL_S = 0;     // S buffers at columns 0, 128
-  static constexpr uint32_t TCOL_O = 256;   // O at 256 .. 256+HD
+  static constexpr uint32_t TCOL_S = 0;     // S_A, S_B at columns 0, 128
+  static constexpr uint32_t TCOL_O = 256;   // O_A, O_B at 256, 256+HD
 };
 
 struct FwdParams {
-  int T, N, NH, bh_begin, nbh, nqt;
+  int T, NH, bh_begin, nbh, npairs, nqt;
+  int nunits;
   float scale_log2;
   float* lse;
   uint32_t* status;
 };
+
+// Unit u (heaviest first) -> (pair, bh) and its tiles' key-tile counts.
+struct Unit {
+  int pair, b, h, nA, nB, nkv;
+};
+
+__device__ __forceinline__ Unit decode_unit(const FwdParams& prm, int u) {
+  Unit x;
+  x.pair = prm.npairs - 1 - u / prm.nbh;
+  const int bh = prm.bh_begin + u % prm.nbh;
+  x.b = bh / prm.NH;
+  x.h = bh % prm.NH;
+  x.nA = 2 * x.pair + 1;                                   // key tiles 0..2p
+  x.nB = (2 * x.pair + 1 < prm.nqt) ? 2 * x.pair + 2 : 0;  // tile B inside T?
+  x.nkv = x.nB > 0 ? x.nB : x.nA;
+  return x;
+}
 
 template <int HD>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
@@ -81,49 +112,49 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t sbase = (raw + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (sbase - raw);
-
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  // heaviest query tiles first
-  const int idx = blockIdx.x;
-  const int qt = prm.nqt - 1 - idx / prm.nbh;
-  const int bh = prm.bh_begin + idx % prm.nbh;
-  const int b = bh / prm.NH, h = bh % prm.NH;
-  const int ntiles = qt + 1;  // causal: key tiles 0..qt
-  const int col0 = h * HD;
 
   const uint32_t bar0 = sbase + C::OFF_BAR;
-  const uint32_t BAR_Q = bar0;
-  auto BAR_KF = [&](int s) { return bar0 + 8u * (1 + s); };
-  auto BAR_VF = [&](int s) { return bar0 + 8u * (1 + C::STAGES + s); };
-  auto BAR_KVE = [&](int s) { return bar0 + 8u * (1 + 2 * C::STAGES + s); };
-  auto BAR_SF = [&](int s) { return bar0 + 8u * (1 + 3 * C::STAGES + s); };
-  auto BAR_SE = [&](int s) { return bar0 + 8u * (3 + 3 * C::STAGES + s); };
-  auto BAR_PF = [&](int s) { return bar0 + 8u * (5 + 3 * C::STAGES + s); };
-  auto BAR_PE = [&](int s) { return bar0 + 8u * (5 + 3 * C::STAGES + C::PBUF + s); };
-  const uint32_t BAR_O = bar0 + 8u * (5 + 3 * C::STAGES + 2 * C::PBUF);
+  auto BAR_QF = [&](int s) { return bar0 + 8u * s; };
+  auto BAR_QE = [&](int s) { return bar0 + 8u * (C::QST + s); };
+  auto BAR_KF = [&](int s) { return bar0 + 8u * (2 * C::QST + s); };
+  auto BAR_KE = [&](int s) { return bar0 + 8u * (2 * C::QST + C::KST + s); };
+  auto BAR_VF = [&](int s) { return bar0 + 8u * (2 * C::QST + 2 * C::KST + s); };
+  auto BAR_VE = [&](int s) { return bar0 + 8u * (2 * C::QST + 2 * C::KST + C::VST + s); };
+  const uint32_t barX = bar0 + 8u * (2 * C::QST + 2 * C::KST + 2 * C::VST);
+  // per tile X in {0: A, 1: B}
+  auto BAR_SF = [&](int x) { return barX + 8u * (0 * 2 + x); };
+  auto BAR_SE = [&](int x) { return barX + 8u * (1 * 2 + x); };
+  auto BAR_PF = [&](int x) { return barX + 8u * (2 * 2 + x); };
+  auto BAR_PV = [&](int x) { return barX + 8u * (3 * 2 + x); };
+  auto BAR_OE = [&](int x) { return barX + 8u * (4 * 2 + x); };
   const uint32_t tslot = sbase + C::OFF_TSLOT;
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
-    mbar_init(BAR_Q, 1);
-    for (int s = 0; s < C::STAGES; ++s) {
+    for (int s = 0; s < C::QST; ++s) {
+      mbar_init(BAR_QF(s), 1);
+      mbar_init(BAR_QE(s), 1);
+    }
+    for (int s = 0; s < C::KST; ++s) {
       mbar_init(BAR_KF(s), 1);
+      mbar_init(BAR_KE(s), 1);
+    }
+    for (int s = 0; s < C::VST; ++s) {
       mbar_init(BAR_VF(s), 1);
-      mbar_init(BAR_KVE(s), 1);
+      mbar_init(BAR_VE(s), 1);
     }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(BAR_SF(s), 1);
-      mbar_init(BAR_SE(s), 128);
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(BAR_SF(x), 1);
+      mbar_init(BAR_SE(x), 128);
+      mbar_init(BAR_PF(x), 128);
+      mbar_init(BAR_PV(x), 1);
+      mbar_init(BAR_OE(x), 128);
     }
-    for (int s = 0; s < C::PBUF; ++s) {
-      mbar_init(BAR_PF(s), 128);
-      mbar_init(BAR_PE(s), 1);
-    }
-    mbar_init(BAR_O, 1);
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tslot, C::TMEM_COLS);
+    tmem_alloc(tslot, 512);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -132,220 +163,288 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(gbase + C::OFF_TSLOT);
   volatile int* abort_p = &abort_flag;
 
-  if (warp == 0) {
-    // ------------------------------------------------------ TMA producer
-    if (lane == 0) {
+  if (warp < 4) {
+    reg_dealloc<REGS_PRODUCER>();
+    if (warp == 0 && lane == 0) {
+      // ---------------------------------------------------- TMA producer
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      mbar_arrive_expect_tx(BAR_Q, C::Q_BYTES);
-      for (int kb = 0; kb < C::KB; ++kb)
-        tma_load_3d(sbase + C::OFF_Q + kb * BM * 128, &tmQ, BAR_Q, col0 + kb * 64, qt * BM, b);
-      for (int j = 0; j < ntiles; ++j) {
-        const int st = j % C::STAGES;
-        if (j >= C::STAGES && !mbar_wait(BAR_KVE(st), ((j - C::STAGES) / C::STAGES) & 1, abort_p))
-          break;
-        const uint32_t sk = sbase + C::OFF_K + st * C::KV_BYTES;
-        const uint32_t sv = sbase + C::OFF_V + st * C::KV_BYTES;
-        mbar_arrive_expect_tx(BAR_KF(st), C::KV_BYTES);
-        for (int kb = 0; kb < C::KB; ++kb)
-          tma_load_3d(sk + kb * BN * 128, &tmK, BAR_KF(st), col0 + kb * 64, j * BN, b);
-        mbar_arrive_expect_tx(BAR_VF(st), C::KV_BYTES);
-        for (int kb = 0; kb < C::KB; ++kb)
-          tma_load_3d(sv + kb * BN * 128, &tmV, BAR_VF(st), col0 + kb * 64, j * BN, b);
+      uint32_t qc = 0, kc = 0, vc = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < prm.nunits; u += gridDim.x) {
+        const Unit un = decode_unit(prm, u);
+        const int col0 = un.h * HD;
+        const int qs = qc % C::QST;
+        if (qc >= C::QST && !mbar_wait(BAR_QE(qs), ((qc / C::QST) - 1) & 1, abort_p)) break;
+        const int ntile = un.nB > 0 ? 2 : 1;
+        mbar_arrive_expect_tx(BAR_QF(qs), ntile * C::QT_BYTES);
+        for (int x = 0; x < ntile; ++x)
+          for (int kb = 0; kb < C::KB; ++kb)
+            tma_load_3d(sbase + C::OFF_Q + (qs * 2 + x) * C::QT_BYTES + kb * BM * 128, &tmQ,
+                        BAR_QF(qs), col0 + kb * 64, (2 * un.pair + x) * BM, un.b);
+        ++qc;
+        for (int j = 0; j < un.nkv; ++j) {
+          const int ks = kc % C::KST;
+          if (kc >= C::KST && !mbar_wait(BAR_KE(ks), ((kc / C::KST) - 1) & 1, abort_p)) { ok = false; break; }
+          mbar_arrive_expect_tx(BAR_KF(ks), C::KV_BYTES);
+          for (int kb = 0; kb < C::KB; ++kb)
+            tma_load_3d(sbase + C::OFF_K + ks * C::KV_BYTES + kb * BN * 128, &tmK, BAR_KF(ks),
+                        col0 + kb * 64, j * BN, un.b);
+          ++kc;
+          const int vs = vc % C::VST;
+          if (vc >= C::VST && !mbar_wait(BAR_VE(vs), ((vc / C::VST) - 1) & 1, abort_p)) { ok = false; break; }
+          mbar_arrive_expect_tx(BAR_VF(vs), C::KV_BYTES);
+          for (int kb = 0; kb < C::KB; ++kb)
+            tma_load_3d(sbase + C::OFF_V + vs * C::KV_BYTES + kb * BN * 128, &tmV, BAR_VF(vs),
+                        col0 + kb * 64, j * BN, un.b);
+          ++vc;
+        }
       }
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------- MMA
-    if (lane == 0) {
+    } else if (warp == 1 && lane == 0) {
+      // ----------------------------------------------------------- MMA
       constexpr uint32_t IDESC_S = idesc_bf16_f32(BM, BN, 0, 0);
       constexpr uint32_t IDESC_O = idesc_bf16_f32(BM, HD, 0, 1);
-      const uint32_t sq = sbase + C::OFF_Q;
-      bool ok = mbar_wait(BAR_Q, 0, abort_p);
-      auto issue_s = [&](int j) -> bool {
-        const int st = j % C::STAGES, sb = j & 1;
-        if (!mbar_wait(BAR_KF(st), (j / C::STAGES) & 1, abort_p)) return false;
-        if (j >= 2 && !mbar_wait(BAR_SE(sb), ((j - 2) >> 1) & 1, abort_p)) return false;
-        tc_fence_after();
-        const uint32_t sk = sbase + C::OFF_K + st * C::KV_BYTES;
+      uint32_t qc = 0, kc = 0, vc = 0;
+      uint32_t sc[2] = {0, 0};   // S_X issued so far
+      uint32_t pvc[2] = {0, 0};  // PV_X issued so far
+      uint32_t uc[2] = {0, 0};   // units in which tile X was active
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < prm.nunits; u += gridDim.x) {
+        const Unit un = decode_unit(prm, u);
+        const int n[2] = {un.nA, un.nB};
+        const int qs = qc % C::QST;
+        if (!mbar_wait(BAR_QF(qs), (qc / C::QST) & 1, abort_p)) break;
+        // S_X(j) = Q_X K_j^T
+        auto issue_s = [&](int x, int j) -> bool {
+          if (sc[x] >= 1 && !mbar_wait(BAR_SE(x), (sc[x] - 1) & 1, abort_p)) return false;
+          tc_fence_after();
+          const uint32_t sq = sbase + C::OFF_Q + (qs * 2 + x) * C::QT_BYTES;
+          const uint32_t sk = sbase + C::OFF_K + ((kc + j) % C::KST) * C::KV_BYTES;
 #pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t koff = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
-          const uint64_t ad = smem_desc_sw128(sq + koff, 16, 1024);
-          const uint64_t bd = smem_desc_sw128(sk + (kk >> 2) * (BN * 128) + (kk & 3) * 32, 16, 1024);
-          umma_bf16_ss(tmem + C::TCOL_S + sb * BN, ad, bd, IDESC_S, kk > 0 ? 1u : 0u);
-        }
-        umma_commit(BAR_SF(sb));
-        return true;
-      };
-      if (ok) ok = issue_s(0);
-      for (int j = 0; ok && j < ntiles; ++j) {
-        if (j + 1 < ntiles && !issue_s(j + 1)) break;
-        const int st = j % C::STAGES, pb = j % C::PBUF;
-        if (!mbar_wait(BAR_PF(pb), (j / C::PBUF) & 1, abort_p)) break;
-        if (!mbar_wait(BAR_VF(st), (j / C::STAGES) & 1, abort_p)) break;
-        tc_fence_after();
-        const uint32_t sp = sbase + C::OFF_P + pb * C::P_BYTES;
-        const uint32_t sv = sbase + C::OFF_V + st * C::KV_BYTES;
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
+            umma_bf16_ss(tmem + C::TCOL_S + x * BN, smem_desc_sw128(sq + off, 16, 1024),
+                         smem_desc_sw128(sk + off, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(BAR_SF(x));
+          ++sc[x];
+          return true;
+        };
+        // O_X += P_X V_j
+        auto issue_pv = [&](int x, int j) -> bool {
+          if (!mbar_wait(BAR_PF(x), pvc[x] & 1, abort_p)) return false;
+          if (j == 0 && uc[x] >= 1 && !mbar_wait(BAR_OE(x), (uc[x] - 1) & 1, abort_p)) return false;
+          tc_fence_after();
+          const uint32_t sp = sbase + C::OFF_P + x * C::P_BYTES;
+          const uint32_t sv = sbase + C::OFF_V + ((vc + j) % C::VST) * C::KV_BYTES;
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t ad = smem_desc_sw128(sp + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = smem_desc_sw128(sv + kk * 2048, BN * 128, 1024);
-          umma_bf16_ss(tmem + C::TCOL_O, ad, bd, IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            const uint64_t ad = smem_desc_sw128(sp + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd = smem_desc_sw128(sv + kk * 2048, BN * 128, 1024);
+            umma_bf16_ss(tmem + C::TCOL_O + x * HD, ad, bd, IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(BAR_PV(x));
+          ++pvc[x];
+          return true;
+        };
+        auto wait_k = [&](int j) {
+          const uint32_t k = kc + j;
+          return mbar_wait(BAR_KF(k % C::KST), (k / C::KST) & 1, abort_p);
+        };
+        auto wait_v = [&](int j) {
+          const uint32_t v = vc + j;
+          return mbar_wait(BAR_VF(v % C::VST), (v / C::VST) & 1, abort_p);
+        };
+        // prologue: S_A(0), S_B(0); K_0 is consumed once both are done
+        ok = wait_k(0) && issue_s(0, 0) && (n[1] == 0 || issue_s(1, 0));
+        if (ok) umma_commit(BAR_KE(kc % C::KST));
+        for (int j = 0; ok && j < un.nkv; ++j) {
+          if (!wait_v(j)) { ok = false; break; }
+          const bool lastA = (j + 1 >= n[0]);
+          if (j < n[0]) {
+            if (!issue_pv(0, j)) { ok = false; break; }
+            if (!lastA && (!wait_k(j + 1) || !issue_s(0, j + 1))) { ok = false; break; }
+          }
+          if (j < n[1]) {
+            if (!issue_pv(1, j)) { ok = false; break; }
+            if (j + 1 < n[1] && ((lastA && !wait_k(j + 1)) || !issue_s(1, j + 1))) { ok = false; break; }
+          }
+          umma_commit(BAR_VE((vc + j) % C::VST));                          // V_j consumed
+          if (j + 1 < un.nkv) umma_commit(BAR_KE((kc + j + 1) % C::KST));  // K_{j+1} consumed
+          if (j + 1 == un.nkv) umma_commit(BAR_QE(qs));                    // every S of the unit issued
         }
-        umma_commit(BAR_KVE(st));
-        umma_commit(BAR_PE(pb));
-        if (j + 1 == ntiles) umma_commit(BAR_O);
+        kc += un.nkv;
+        vc += un.nkv;
+        ++qc;
+        for (int x = 0; x < 2; ++x)
+          if (n[x] > 0) ++uc[x];
       }
     }
   } else {
+    reg_alloc<REGS_SOFTMAX>();
     // --------------------------------------------------------- softmax
+    const int x = (warp - 4) >> 2;               // 0: tile A (warps 4-7), 1: tile B (8-11)
+    const uint32_t wg_bar = 1 + x;               // named barrier of this warpgroup
     const int quarter = warp & 3;                // TMEM lane quarter of this warp
     const int row = quarter * 32 + lane;         // query row within the tile
-    const int grow = qt * BM + row;              // query position
     const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
+    const uint32_t tcol_s = C::TCOL_S + x * BN, tcol_o = C::TCOL_O + x * HD;
     const float c = prm.scale_log2;
-    float m_used = -INFINITY, l_sum = 0.0f;
+    const bool wg_leader = (warp == 4 + 4 * x) && lane == 0;
+    uint8_t* pbuf = gbase + C::OFF_P + x * C::P_BYTES;
+    uint32_t sc = 0;  // S_X consumed so far (== P_X produced)
     bool ok = true;
-    for (int j = 0; j < ntiles; ++j) {
-      const int sb = j & 1, pb = j % C::PBUF;
-      if (!mbar_wait_warp(BAR_SF(sb), (j >> 1) & 1, abort_p)) { ok = false; break; }
-      tc_fence_after();
-      float s[BN];
+    for (int u = blockIdx.x; ok && u < prm.nunits; u += gridDim.x) {
+      const Unit un = decode_unit(prm, u);
+      const int nt = x == 0 ? un.nA : un.nB;
+      if (nt == 0) continue;
+      const int qtile = 2 * un.pair + x;
+      // the previous unit's O store must have read the P buffer (its staging)
+      if (sc >= 1 && wg_leader) bulk_wait_read<0>();
+      bar_sync_named(wg_bar, 128);
+      float m_used = -INFINITY, l_sum = 0.0f;
+      for (int j = 0; ok && j < nt; ++j) {
+        if (!mbar_wait_warp(BAR_SF(x), sc & 1, abort_p)) { ok = false; break; }
+        tc_fence_after();
+        float s[BN];
 #pragma unroll
-      for (int cc = 0; cc < BN; cc += 64) {
-        uint32_t ra[32], rb[32];
-        tmem_ld32(trow + C::TCOL_S + sb * BN + cc, ra);
-        tmem_ld32(trow + C::TCOL_S + sb * BN + cc + 32, rb);
-        tmem_wait_ld_dep(ra, rb);
+        for (int cc = 0; cc < BN; cc += 64) {
+          uint32_t ra[32], rb[32];
+          tmem_ld32(trow + tcol_s + cc, ra);
+          tmem_ld32(trow + tcol_s + cc + 32, rb);
+          tmem_wait_ld_dep(ra, rb);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          s[cc + i] = __uint_as_float(ra[i]);
-          s[cc + 32 + i] = __uint_as_float(rb[i]);
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(BAR_SE(sb));
-      if (j == qt) {  // diagonal tile: mask keys after the query
-#pragma unroll
-        for (int i = 0; i < BN; ++i)
-          if (i > row) s[i] = -INFINITY;
-      }
-      // row maximum with 8 independent partial maxima (short dependency chains)
-      float pm[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) pm[u] = s[u];
-#pragma unroll
-      for (int i = 8; i < BN; i += 8)
-#pragma unroll
-        for (int u = 0; u < 8; ++u) pm[u] = fmaxf(pm[u], s[i + u]);
-      const float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
-                             fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
-      const float m_new = fmaxf(m_used, mx * c);
-      if (j == 0) {
-        m_used = m_new;
-      } else {
-        const bool need = m_new > m_used + RESCALE_THRESHOLD;
-        if (__any_sync(0xffffffffu, need)) {
-          const float alpha = need ? ex2(m_used - m_new) : 1.0f;
-          if (need) {
-            l_sum *= alpha;
-            m_used = m_new;
+          for (int i = 0; i < 32; ++i) {
+            s[cc + i] = __uint_as_float(ra[i]);
+            s[cc + 32 + i] = __uint_as_float(rb[i]);
           }
-          // O must be stable: wait for PV_{j-1}
-          const int pp = (j - 1) % C::PBUF;
-          if (!mbar_wait_warp(BAR_PE(pp), ((j - 1) / C::PBUF) & 1, abort_p)) { ok = false; break; }
-          tc_fence_after();
+        }
+        tc_fence_before();
+        mbar_arrive(BAR_SE(x));
+        if (j == qtile) {  // diagonal tile: mask keys after the query
 #pragma unroll
-          for (int cc = 0; cc < HD; cc += 16) {
-            uint32_t r[16];
-            tmem_ld16(trow + C::TCOL_O + cc, r);
-            tmem_wait_ld_dep(r);
+          for (int i = 0; i < BN; ++i)
+            if (i > row) s[i] = -INFINITY;
+        }
+        // row maximum with 8 independent partial maxima (short dependency chains)
+        float pm[8];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-            tmem_st16(trow + C::TCOL_O + cc, r);
+        for (int q = 0; q < 8; ++q) pm[q] = s[q];
+#pragma unroll
+        for (int i = 8; i < BN; i += 8)
+#pragma unroll
+          for (int q = 0; q < 8; ++q) pm[q] = fmaxf(pm[q], s[i + q]);
+        const float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
+                               fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
+        const float m_new = fmaxf(m_used, mx * c);
+        // PV_X(j-1) must be complete before P_X(j) overwrites the P buffer and
+        // before O_X is rescaled
+        if (j >= 1 && !mbar_wait_warp(BAR_PV(x), (sc - 1) & 1, abort_p)) { ok = false; break; }
+        if (j == 0) {
+          m_used = m_new;
+        } else {
+          const bool need = m_new > m_used + RESCALE_THRESHOLD;
+          if (__any_sync(0xffffffffu, need)) {
+            const float alpha = need ? ex2(m_used - m_new) : 1.0f;
+            if (need) {
+              l_sum *= alpha;
+              m_used = m_new;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int cc = 0; cc < HD; cc += 16) {
+              uint32_t r[16];
+              tmem_ld16(trow + tcol_o + cc, r);
+              tmem_wait_ld_dep(r);
+#pragma unroll
+              for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+              tmem_st16(trow + tcol_o + cc, r);
+            }
+            tmem_wait_st();
           }
-          tmem_wait_st();
         }
-      }
-      // P = 2^(S*c - m) with packed fp32x2 FMAs; row sum in 4 packed partials
-      const float2 c2 = make_float2(c, c), nm2 = make_float2(-m_used, -m_used);
-      float2 ps[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
-                      make_float2(0.f, 0.f)};
+        // P = 2^(S*c - m) with packed fp32x2 FMAs; row sum in 4 packed partials
+        const float2 c2 = make_float2(c, c), nm2 = make_float2(-m_used, -m_used);
+        float2 ps[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                        make_float2(0.f, 0.f)};
 #pragma unroll
-      for (int i = 0; i < BN; i += 2) {
-        const float2 t = __ffma2_rn(make_float2(s[i], s[i + 1]), c2, nm2);
-        s[i] = ex2(t.x);
-        s[i + 1] = ex2(t.y);
-        ps[(i >> 1) & 3] = __fadd2_rn(ps[(i >> 1) & 3], make_float2(s[i], s[i + 1]));
-      }
-      const float rs = (ps[0].x + ps[0].y) + (ps[1].x + ps[1].y) + (ps[2].x + ps[2].y) +
-                       (ps[3].x + ps[3].y);
-      l_sum += rs;
-      if (j >= C::PBUF && !mbar_wait_warp(BAR_PE(pb), ((j - C::PBUF) / C::PBUF) & 1, abort_p)) { ok = false; break; }
-      uint8_t* prow = gbase + C::OFF_P + pb * C::P_BYTES;
-#pragma unroll
-      for (int kb = 0; kb < BN / 64; ++kb) {
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          const int c0 = kb * 64 + ch * 8;
-          uint4 v;
-          v.x = pack_bf16(s[c0 + 0], s[c0 + 1]);
-          v.y = pack_bf16(s[c0 + 2], s[c0 + 3]);
-          v.z = pack_bf16(s[c0 + 4], s[c0 + 5]);
-          v.w = pack_bf16(s[c0 + 6], s[c0 + 7]);
-          *reinterpret_cast<uint4*>(prow + kb * (BM * 128) + row * 128 + ((ch ^ (row & 7)) * 16)) = v;
+        for (int i = 0; i < BN; i += 2) {
+          const float2 t = __ffma2_rn(make_float2(s[i], s[i + 1]), c2, nm2);
+          s[i] = ex2(t.x);
+          s[i + 1] = ex2(t.y);
+          ps[(i >> 1) & 3] = __fadd2_rn(ps[(i >> 1) & 3], make_float2(s[i], s[i + 1]));
         }
-      }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(BAR_PF(pb));
-    }
-    // ------------------------------------------------------- epilogue
-    const bool epi = ok && mbar_wait_warp(BAR_O, 0, abort_p);
-    if (epi) {
-      tc_fence_after();
-      const float inv = 1.0f / l_sum;
-      // stage O (bf16) in the P buffer 0 region, laid out like a TMA box
-      uint8_t* ostage = gbase + C::OFF_P;
+        l_sum += (ps[0].x + ps[0].y) + (ps[1].x + ps[1].y) + (ps[2].x + ps[2].y) +
+                 (ps[3].x + ps[3].y);
 #pragma unroll
-      for (int cc = 0; cc < HD; cc += 16) {
-        uint32_t r[16];
-        tmem_ld16(trow + C::TCOL_O + cc, r);
-        tmem_wait_ld_dep(r);
-        uint4 v0, v1;
-        v0.x = pack_bf16(__uint_as_float(r[0]) * inv, __uint_as_float(r[1]) * inv);
-        v0.y = pack_bf16(__uint_as_float(r[2]) * inv, __uint_as_float(r[3]) * inv);
-        v0.z = pack_bf16(__uint_as_float(r[4]) * inv, __uint_as_float(r[5]) * inv);
-        v0.w = pack_bf16(__uint_as_float(r[6]) * inv, __uint_as_float(r[7]) * inv);
-        v1.x = pack_bf16(__uint_as_float(r[8]) * inv, __uint_as_float(r[9]) * inv);
-        v1.y = pack_bf16(__uint_as_float(r[10]) * inv, __uint_as_float(r[11]) * inv);
-        v1.z = pack_bf16(__uint_as_float(r[12]) * inv, __uint_as_float(r[13]) * inv);
-        v1.w = pack_bf16(__uint_as_float(r[14]) * inv, __uint_as_float(r[15]) * inv);
-        const int kb = cc / 64, ch = (cc % 64) / 8;
-        uint8_t* blk = ostage + kb * (BM * 128) + row * 128;
-        *reinterpret_cast<uint4*>(blk + ((ch ^ (row & 7)) * 16)) = v0;
-        *reinterpret_cast<uint4*>(blk + (((ch + 1) ^ (row & 7)) * 16)) = v1;
+        for (int kb = 0; kb < BN / 64; ++kb) {
+#pragma unroll
+          for (int ch = 0; ch < 8; ++ch) {
+            const int c0 = kb * 64 + ch * 8;
+            uint4 v;
+            v.x = pack_bf16(s[c0 + 0], s[c0 + 1]);
+            v.y = pack_bf16(s[c0 + 2], s[c0 + 3]);
+            v.z = pack_bf16(s[c0 + 4], s[c0 + 5]);
+            v.w = pack_bf16(s[c0 + 6], s[c0 + 7]);
+            *reinterpret_cast<uint4*>(pbuf + kb * (BM * 128) + row * 128 + ((ch ^ (row & 7)) * 16)) = v;
+          }
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(BAR_PF(x));
+        ++sc;
       }
-      fence_proxy_async_smem();
-      if (grow < prm.T)
-        prm.lse[((long long)b * prm.T + grow) * prm.NH + h] = (m_used + log2f(l_sum)) * LN2;
+      // --------------------------------------------- epilogue of tile X
+      const bool epi = ok && mbar_wait_warp(BAR_PV(x), (sc - 1) & 1, abort_p);
+      if (epi) {
+        tc_fence_after();
+        const float inv = 1.0f / l_sum;
+        // stage O (bf16) in this tile's P buffer (free: its last PV is done)
+#pragma unroll
+        for (int cc = 0; cc < HD; cc += 16) {
+          uint32_t r[16];
+          tmem_ld16(trow + tcol_o + cc, r);
+          tmem_wait_ld_dep(r);
+          uint4 v0, v1;
+          v0.x = pack_bf16(__uint_as_float(r[0]) * inv, __uint_as_float(r[1]) * inv);
+          v0.y = pack_bf16(__uint_as_float(r[2]) * inv, __uint_as_float(r[3]) * inv);
+          v0.z = pack_bf16(__uint_as_float(r[4]) * inv, __uint_as_float(r[5]) * inv);
+          v0.w = pack_bf16(__uint_as_float(r[6]) * inv, __uint_as_float(r[7]) * inv);
+          v1.x = pack_bf16(__uint_as_float(r[8]) * inv, __uint_as_float(r[9]) * inv);
+          v1.y = pack_bf16(__uint_as_float(r[10]) * inv, __uint_as_float(r[11]) * inv);
+          v1.z = pack_bf16(__uint_as_float(r[12]) * inv, __uint_as_float(r[13]) * inv);
+          v1.w = pack_bf16(__uint_as_float(r[14]) * inv, __uint_as_float(r[15]) * inv);
+          const int kb = cc / 64, ch = (cc % 64) / 8;
+          uint8_t* blk = pbuf + kb * (BM * 128) + row * 128;
+          *reinterpret_cast<uint4*>(blk + ((ch ^ (row & 7)) * 16)) = v0;
+          *reinterpret_cast<uint4*>(blk + (((ch + 1) ^ (row & 7)) * 16)) = v1;
+        }
+        tc_fence_before();
+        mbar_arrive(BAR_OE(x));  // O_X may be overwritten by the next unit
+        fence_proxy_async_smem();
+        const int grow = qtile * BM + row;
+        if (grow < prm.T)
+          prm.lse[((long long)un.b * prm.T + grow) * prm.NH + un.h] = (m_used + log2f(l_sum)) * LN2;
+      }
+      // every thread of the warpgroup takes this barrier and leaves it with the
+      // same verdict, so the warpgroup stays in step after a failed wait
+      ok = bar_red_and(wg_bar, 128, epi);
+      if (ok && wg_leader) {
+        for (int kb = 0; kb < C::KB; ++kb)
+          tma_store_3d(&tmO, sbase + C::OFF_P + x * C::P_BYTES + kb * BM * 128, un.h * HD + kb * 64,
+                       qtile * BM, un.b);
+        bulk_commit();
+      }
     }
-    // every softmax thread reaches this barrier, whatever happened before
-    asm volatile("bar.sync 1, 128;" ::: "memory");
-    if (epi && warp == 2 && lane == 0) {
-      for (int kb = 0; kb < C::KB; ++kb)
-        tma_store_3d(&tmO, sbase + C::OFF_P + kb * BM * 128, col0 + kb * 64, qt * BM, b);
-      bulk_commit();
-      bulk_wait<0>();
-    }
+    if (wg_leader) bulk_wait<0>();
   }
 
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, C::TMEM_COLS);
+    tmem_dealloc(tmem, 512);
   }
   if (threadIdx.x == 0 && abort_flag) atomicOr(prm.status, STATUS_FWD_TIMEOUT);
 }
@@ -355,6 +454,15 @@ cudaError_t launch_fwd(const __nv_bfloat16* q, const __nv_bfloat16* k, const __n
                        __nv_bfloat16* out, float* lse, const AttnShape& s, uint32_t* status,
                        cudaStream_t st) {
   using C = FwdCfg<HD>;
+  // The setmaxnreg split assumes the kernel was compiled to exactly
+  // LAUNCH_REGS registers per thread; refuse to launch otherwise.
+  static const cudaError_t reg_check = [] {
+    cudaFuncAttributes a;
+    cudaError_t e = cudaFuncGetAttributes(&a, flash_fwd_kernel<HD>);
+    if (e != cudaSuccess) return e;
+    return a.numRegs == LAUNCH_REGS ? cudaSuccess : cudaErrorInvalidKernelImage;
+  }();
+  if (reg_check != cudaSuccess) return reg_check;
   CUtensorMap tq, tk, tv, to;
   const CUtensorMapDataType bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B;
@@ -365,19 +473,23 @@ cudaError_t launch_fwd(const __nv_bfloat16* q, const __nv_bfloat16* k, const __n
     return cudaErrorInvalidValue;
   FwdParams prm;
   prm.T = s.T;
-  prm.N = s.N;
   prm.NH = s.NH;
   prm.bh_begin = s.bh_begin;
   prm.nbh = s.bh_end - s.bh_begin;
   prm.nqt = (s.T + BM - 1) / BM;
+  prm.npairs = (prm.nqt + 1) / 2;
+  prm.nunits = prm.npairs * prm.nbh;
   prm.scale_log2 = LOG2E / sqrtf((float)HD);
   prm.lse = lse;
   prm.status = status;
   cudaError_t e = cudaFuncSetAttribute(flash_fwd_kernel<HD>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
   if (e != cudaSuccess) return e;
-  const long long nblocks = (long long)prm.nqt * prm.nbh;
-  flash_fwd_kernel<HD><<<(unsigned)nblocks, NUM_THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, to, prm);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int grid = prm.nunits < sms ? prm.nunits : sms;
+  flash_fwd_kernel<HD><<<grid, NUM_THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, to, prm);
   count_launches(1);
   return cudaGetLastError();
 }

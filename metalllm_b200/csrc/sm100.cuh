@@ -27,6 +27,21 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
+// ------------------------------------------------------- register split
+// setmaxnreg: a whole warpgroup (4 aligned warps) lowers or raises its
+// per-thread register budget.  Increases draw only on what other warpgroups
+// of the same CTA released, so a split must sum to the CTA's launch
+// allocation (threads x registers at launch); launchers check the compiled
+// register count before relying on a split.
+template <uint32_t N>
+__device__ __forceinline__ void reg_dealloc() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void reg_alloc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // ------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
@@ -86,6 +101,25 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
 __device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, volatile int* abort) {
   const bool ok = mbar_wait(bar, parity, abort);
   return __all_sync(0xffffffffu, ok);
+}
+
+// Named barrier `id` over `nthreads` threads that also returns the AND of
+// every participant's `v` (bar.red.and.pred), so a group can agree on a flag.
+__device__ __forceinline__ bool bar_red_and(uint32_t id, uint32_t nthreads, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
+
+__device__ __forceinline__ void bar_sync_named(uint32_t id, uint32_t nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 // ------------------------------------------------------------------ TMA
