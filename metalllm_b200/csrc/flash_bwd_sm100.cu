@@ -13,29 +13,31 @@
 //   dK  += dS^T Q_i                UMMA 128xDx128  (TMEM-resident)
 //   dQ_i = dS K                    UMMA 128xDx128  -> TMEM -> smem -> TMA
 //                                  bulk reduce-add into fp32 dQ in global
-// P^T and dS^T are written once to shared memory (bf16, K-major 128-byte
-// swizzle); the dQ MMA reads the same dS^T buffer as an MN-major operand.
-// dK/dV are owned by the CTA and stored once (bf16); dQ is accumulated in
-// fp32 by the bulk reductions of every key tile, so the launcher zeroes it
-// first (the reference's host zeroes it, model.h:549).
+// dS^T is written once to shared memory (bf16, K-major 128-byte swizzle); the
+// dQ UMMA reads the same buffer as an MN-major operand.  At D=64, P^T goes to
+// TMEM (bf16 pairs) and dV's UMMA takes it from there; at D=128 TMEM is full
+// and P^T goes to shared memory like dS^T.  dK/dV are owned by the CTA and
+// stored once (bf16); dQ is accumulated in fp32 by the bulk reductions of
+// every key tile, so the launcher zeroes it first (the reference's host zeroes
+// it, model.h:549).  The CTAs of one (batch, head) are launched next to each
+// other, so its Q/dO tiles are re-read from L2 rather than HBM.
 //
 // Roles (384 threads, three warpgroups):
 //   warpgroup 0 (120 registers per thread after setmaxnreg):
-//     warp 0   producer: TMA for K/V once and Q_i/dO_i per stage; its 32 lanes
-//              also stage the per-query statistics -l_i*log2(e) and
-//              -D_i/sqrt(D) (strided in global memory) into shared memory
+//     warp 0   TMA producer: K/V once, Q_i/dO_i into a STAGES-deep ring
 //     warp 1   TMEM owner; lane 0 issues every UMMA and commit
+//     warp 2   statistics: stages -l_i*log2(e) and -D_i/sqrt(D) per query
+//              (strided in global memory) 8 tiles ahead
+//     warp 3   lane 0 issues the dQ bulk reductions
 //   warpgroups 1, 2 (192 registers): compute, thread = key row = TMEM lane;
 //              warpgroup 1 takes query columns 0-63, warpgroup 2 columns
-//              64-127; dQ drain and dK/dV epilogue (thread = TMEM lane of the
-//              respective accumulator)
+//              64-127; dQ drain into the staging buffer and dK/dV epilogue.
 // D=64 schedule ("early S"): S^T/dP^T of tile i+1 are issued as soon as the
 // compute warps have read tile i's, so they run on the tensor core while the
-// compute warps form P^T_i/dS^T_i; dV_i, dK_i and dQ_i follow P^T_i.  dQ_{i-1}
-// is drained after P^T_i is handed over, and its bulk reduction is left in
-// flight until the next drain.  D=128 has no TMEM room for that (S^T, dP^T, dV,
-// dK fill all 512 columns; dQ reuses the S^T columns) and runs the steps in
-// order, draining dQ_i before S^T_{i+1}.
+// compute warps form P^T_i/dS^T_i; dV_i, dK_i and dQ_i follow.  dQ_{i-1} is
+// drained after tile i is handed over.  D=128 has no TMEM room for that (S^T,
+// dP^T, dV, dK fill all 512 columns; dQ reuses the S^T columns) and runs the
+// steps in order, draining dQ_i before S^T_{i+1}.
 //
 // Conventions as the reference: P = exp(S/sqrt(D) - l) with l read as stored,
 // D read as stored (bf16), dS includes 1/sqrt(D).  The reference rounds S,
@@ -44,8 +46,9 @@
 // bf16 (the UMMA operand type).
 //
 // All mbarrier waits are bounded (about 2 s); on time-out the CTA winds down,
-// frees its TMEM and sets STATUS_BWD_TIMEOUT.  Compute warps execute the same
-// named-barrier sequence whether or not a wait failed.
+// frees its TMEM and sets STATUS_BWD_TIMEOUT.  The compute warps meet only at
+// mbarriers inside the loop and at one named barrier (same count on every
+// path) for the epilogue.
 #include "common.cuh"
 #include "sm100.cuh"
 #include "tmap.h"
@@ -64,31 +67,39 @@ constexpr int REGS_PRODUCER = 120;  // warpgroup 0 after setmaxnreg.dec
 constexpr int REGS_COMPUTE = 192;   // warpgroups 1, 2 after setmaxnreg.inc
 static_assert(128 * REGS_PRODUCER + 256 * REGS_COMPUTE == NUM_THREADS * LAUNCH_REGS,
               "register split must equal the launch allocation");
+constexpr int SSTAGES = 8;  // statistics stages
 constexpr float LOG2E = 1.4426950408889634f;
 
 template <int HD>
 struct BwdCfg {
   static constexpr int KB = HD / 64;
-  static constexpr int STAGES = HD == 64 ? 2 : 1;
-  static constexpr bool DQ_ALIAS = HD != 64;  // dQ accumulator reuses the S^T columns
-  static constexpr bool EARLY_S = !DQ_ALIAS;
+  static constexpr bool D64 = HD == 64;
+  static constexpr int STAGES = D64 ? 3 : 1;     // Q_i/dO_i stages
+  static constexpr bool P_IN_TMEM = D64;         // P^T in TMEM (else smem)
+  static constexpr bool EARLY_S = D64;           // S_{i+1} before dV_i/dK_i/dQ_i
+  static constexpr bool DQ_ALIAS = !D64;         // dQ accumulator reuses the S^T columns
+  static constexpr bool DQS_ALIAS = !D64;        // dQ staging reuses the P^T/dS^T smem
   static constexpr uint32_t KV_BYTES = BK * HD * 2;
   static constexpr uint32_t QD_BYTES = BQ * HD * 2;
   static constexpr uint32_t PT_BYTES = BK * BQ * 2;
   static constexpr uint32_t DQS_BYTES = BQ * HD * 4;
-  static constexpr uint32_t STAT_BYTES = 2 * BQ * 4;  // per stage: -l*log2e[128], -D/sqrt(D)[128]
+  static constexpr uint32_t STAT_BYTES = 2 * BQ * 4;  // -l*log2e[128], -D/sqrt(D)[128]
   static constexpr uint32_t OFF_K = 0;
   static constexpr uint32_t OFF_V = OFF_K + KV_BYTES;
   static constexpr uint32_t OFF_Q = OFF_V + KV_BYTES;                // [STAGES]
   static constexpr uint32_t OFF_DO = OFF_Q + STAGES * QD_BYTES;      // [STAGES]
-  static constexpr uint32_t OFF_PT = OFF_DO + STAGES * QD_BYTES;
-  static constexpr uint32_t OFF_DST = OFF_PT + PT_BYTES;
-  // dQ staging: own region for D=64, the P^T/dS^T region for D=128
-  static constexpr uint32_t OFF_DQS = HD == 64 ? OFF_DST + PT_BYTES : OFF_PT;
-  static constexpr uint32_t OFF_STAT = HD == 64 ? OFF_DQS + DQS_BYTES : OFF_DST + PT_BYTES;
-  static constexpr uint32_t OFF_BAR = OFF_STAT + STAGES * STAT_BYTES;
-  // kv_full, qd_full[S], qd_empty[S], s_full, s_free, p_ready, p_free, dq_full, dq_free, done
-  static constexpr int NBAR = 1 + 2 * STAGES + 7;
+  static constexpr uint32_t OFF_PT = OFF_DO + STAGES * QD_BYTES;     // only without P_IN_TMEM
+  static constexpr uint32_t OFF_DST = OFF_PT + (P_IN_TMEM ? 0 : PT_BYTES);
+  static constexpr uint32_t OFF_DQS = DQS_ALIAS ? OFF_PT : OFF_DST + PT_BYTES;
+  static constexpr uint32_t OFF_STAT = DQS_ALIAS ? OFF_DST + PT_BYTES : OFF_DQS + DQS_BYTES;
+  static constexpr uint32_t OFF_BAR = OFF_STAT + SSTAGES * STAT_BYTES;
+  // epilogue staging of dV and dK (bf16): the P^T/dS^T region (D=128) or the
+  // dS^T region (D=64, 16 KB each)
+  static constexpr uint32_t OFF_EPI_V = P_IN_TMEM ? OFF_DST : OFF_PT;
+  static constexpr uint32_t OFF_EPI_K = P_IN_TMEM ? OFF_DST + BK * HD * 2 : OFF_DST;
+  // kv_full, qd_full[S], qd_empty[S], st_full[8], st_empty[8], s_full, s_free,
+  // p_ready, p_free, dq_full, dq_free, dqs_full, dqs_free, done
+  static constexpr int NBAR = 1 + 2 * STAGES + 2 * SSTAGES + 9;
   static constexpr uint32_t OFF_TSLOT = OFF_BAR + NBAR * 8;
   static constexpr uint32_t SMEM_BYTES = OFF_TSLOT + 16 + 1024;
   static constexpr uint32_t TCOL_S = 0;
@@ -96,6 +107,7 @@ struct BwdCfg {
   static constexpr uint32_t TCOL_DV = 256;
   static constexpr uint32_t TCOL_DK = 256 + HD;
   static constexpr uint32_t TCOL_DQ = DQ_ALIAS ? 0 : 256 + 2 * HD;
+  static constexpr uint32_t TCOL_PT = 256 + 3 * HD;  // D=64 only: 64 columns of bf16 pairs
 };
 
 struct BwdParams {
@@ -105,8 +117,6 @@ struct BwdParams {
   const __nv_bfloat16* Dv;
   uint32_t* status;
 };
-
-__device__ __forceinline__ void compute_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 // P^T and dS^T for 64 query columns of one key row.  s[] holds S^T on entry
 // and P^T on exit; dp[] holds dP^T on entry and dS^T on exit.  nl = -l*log2e
@@ -144,6 +154,21 @@ __device__ __forceinline__ void p_ds_row(float (&s)[64], float (&dp)[64], const 
   }
 }
 
+// 64 bf16 values of one row as 8 swizzled 16-byte chunks of a K-major SW128
+// row (row base `rowp`, swizzle phase `row & 7`).
+__device__ __forceinline__ void store_row_sw128(uint8_t* rowp, int row, const float (&v)[64]) {
+#pragma unroll
+  for (int ch = 0; ch < 8; ++ch) {
+    const int c0 = ch * 8;
+    uint4 w;
+    w.x = pack_bf16(v[c0 + 0], v[c0 + 1]);
+    w.y = pack_bf16(v[c0 + 2], v[c0 + 3]);
+    w.z = pack_bf16(v[c0 + 4], v[c0 + 5]);
+    w.w = pack_bf16(v[c0 + 6], v[c0 + 7]);
+    *reinterpret_cast<uint4*>(rowp + ((ch ^ (row & 7)) * 16)) = w;
+  }
+}
+
 template <int HD>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     flash_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -158,10 +183,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint8_t* gbase = smem_raw + (sbase - raw);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  // key tiles with the most query tiles (the first ones) launch first
+  // the key tiles of one (batch, head) are adjacent in launch order (heaviest
+  // first within the group), so they share Q/dO through L2
   const int idx = blockIdx.x;
-  const int kt = idx / prm.nbh;
-  const int bh = prm.bh_begin + idx % prm.nbh;
+  const int bh = prm.bh_begin + idx / prm.nkt;
+  const int kt = idx % prm.nkt;
   const int b = bh / prm.NH, h = bh % prm.NH;
   const int nq = prm.nkt - kt;  // query tiles kt .. nkt-1
   const int col0 = h * HD;
@@ -170,13 +196,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t BAR_KV = bar0;
   auto BAR_QF = [&](int s) { return bar0 + 8u * (1 + s); };
   auto BAR_QE = [&](int s) { return bar0 + 8u * (1 + C::STAGES + s); };
-  const uint32_t BAR_SF = bar0 + 8u * (1 + 2 * C::STAGES);
+  auto BAR_TF = [&](int s) { return bar0 + 8u * (1 + 2 * C::STAGES + s); };
+  auto BAR_TE = [&](int s) { return bar0 + 8u * (1 + 2 * C::STAGES + SSTAGES + s); };
+  const uint32_t BAR_SF = bar0 + 8u * (1 + 2 * C::STAGES + 2 * SSTAGES);
   const uint32_t BAR_SE = BAR_SF + 8;
   const uint32_t BAR_PR = BAR_SF + 16;
   const uint32_t BAR_PE = BAR_SF + 24;
   const uint32_t BAR_DQF = BAR_SF + 32;
   const uint32_t BAR_DQE = BAR_SF + 40;
-  const uint32_t BAR_DONE = BAR_SF + 48;
+  const uint32_t BAR_DSF = BAR_SF + 48;  // dQ staging written
+  const uint32_t BAR_DSE = BAR_SF + 56;  // dQ staging read by the reduction
+  const uint32_t BAR_DONE = BAR_SF + 64;
   const uint32_t tslot = sbase + C::OFF_TSLOT;
   float* stat_base = reinterpret_cast<float*>(gbase + C::OFF_STAT);
 
@@ -184,8 +214,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     abort_flag = 0;
     mbar_init(BAR_KV, 1);
     for (int s = 0; s < C::STAGES; ++s) {
-      mbar_init(BAR_QF(s), 1 + 32);  // TMA expect_tx arrival + 32 statistics lanes
+      mbar_init(BAR_QF(s), 1);
       mbar_init(BAR_QE(s), 1);
+    }
+    for (int s = 0; s < SSTAGES; ++s) {
+      mbar_init(BAR_TF(s), 32);
+      mbar_init(BAR_TE(s), NCOMP);
     }
     mbar_init(BAR_SF, 1);
     mbar_init(BAR_SE, NCOMP);
@@ -193,6 +227,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     mbar_init(BAR_PE, 1);
     mbar_init(BAR_DQF, 1);
     mbar_init(BAR_DQE, NCOMP);
+    mbar_init(BAR_DSF, NCOMP);
+    mbar_init(BAR_DSE, 1);
     mbar_init(BAR_DONE, 1);
     fence_mbar_init();
   }
@@ -209,7 +245,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp < 4) {
     reg_dealloc<REGS_PRODUCER>();
     if (warp == 0) {
-      // ------------------------------------------------------------ producer
+      // --------------------------------------------------------- producer
       if (lane == 0) {
         tma_prefetch_desc(&tmQ);
         tma_prefetch_desc(&tmdO);
@@ -218,15 +254,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tma_load_3d(sbase + C::OFF_K + kb * BK * 128, &tmK, BAR_KV, col0 + kb * 64, kt * BK, b);
           tma_load_3d(sbase + C::OFF_V + kb * BK * 128, &tmV, BAR_KV, col0 + kb * 64, kt * BK, b);
         }
-      }
-      const long long rbase = (long long)b * prm.T;
-      for (int i = 0; i < nq; ++i) {
-        const int st = i % C::STAGES;
-        if (i >= C::STAGES &&
-            !mbar_wait_warp(BAR_QE(st), ((i - C::STAGES) / C::STAGES) & 1, abort_p))
-          break;
-        const int qt = kt + i;
-        if (lane == 0) {
+        for (int i = 0; i < nq; ++i) {
+          const int st = i % C::STAGES;
+          if (i >= C::STAGES && !mbar_wait(BAR_QE(st), ((i - C::STAGES) / C::STAGES) & 1, abort_p))
+            break;
+          const int qt = kt + i;
           mbar_arrive_expect_tx(BAR_QF(st), 2 * C::QD_BYTES);
           for (int kb = 0; kb < C::KB; ++kb) {
             tma_load_3d(sbase + C::OFF_Q + st * C::QD_BYTES + kb * BQ * 128, &tmQ, BAR_QF(st),
@@ -235,25 +267,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         col0 + kb * 64, qt * BQ, b);
           }
         }
-        // per-query statistics of the tile: 4 queries per lane
-        float* stt = stat_base + st * (2 * BQ);
-  #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int qi = lane * 4 + u;
-          const int q = qt * BQ + qi;
-          float nl = 0.0f, nd = 0.0f;
-          if (q < prm.T) {
-            const long long si = (rbase + q) * prm.NH + h;
-            nl = -__ldg(prm.lse + si) * LOG2E;
-            nd = -__bfloat162float(prm.Dv[si]) * prm.scale;
-          }
-          stt[qi] = nl;
-          stt[BQ + qi] = nd;
-        }
-        mbar_arrive(BAR_QF(st));
       }
     } else if (warp == 1) {
-      // ------------------------------------------------------------------ MMA
+      // -------------------------------------------------------------- MMA
       if (lane == 0) {
         constexpr uint32_t IDESC_S = idesc_bf16_f32(BK, BQ, 0, 0);   // S^T, dP^T
         constexpr uint32_t IDESC_KV = idesc_bf16_f32(BK, HD, 0, 1);  // dV, dK
@@ -270,13 +286,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tc_fence_after();
           const uint32_t sq = sbase + C::OFF_Q + st * C::QD_BYTES;
           const uint32_t sdo = sbase + C::OFF_DO + st * C::QD_BYTES;
-  #pragma unroll
+#pragma unroll
           for (int kk = 0; kk < HD / 16; ++kk) {
             const uint32_t off = (kk >> 2) * (BK * 128) + (kk & 3) * 32;
             umma_bf16_ss(tmem + C::TCOL_S, smem_desc_sw128(sk + off, 16, 1024),
                          smem_desc_sw128(sq + off, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
           }
-  #pragma unroll
+#pragma unroll
           for (int kk = 0; kk < HD / 16; ++kk) {
             const uint32_t off = (kk >> 2) * (BK * 128) + (kk & 3) * 32;
             umma_bf16_ss(tmem + C::TCOL_DP, smem_desc_sw128(sv + off, 16, 1024),
@@ -293,13 +309,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint32_t sdo = sbase + C::OFF_DO + st * C::QD_BYTES;
           if (!mbar_wait(BAR_PR, i & 1, abort_p)) break;
           tc_fence_after();
-  #pragma unroll
+#pragma unroll
           for (int kk = 0; kk < BQ / 16; ++kk) {  // dV += P^T dO_i
-            const uint64_t ad = smem_desc_sw128(spt + (kk >> 2) * (BK * 128) + (kk & 3) * 32, 16, 1024);
             const uint64_t bd = smem_desc_sw128(sdo + kk * 2048, BQ * 128, 1024);
-            umma_bf16_ss(tmem + C::TCOL_DV, ad, bd, IDESC_KV, (i > 0 || kk > 0) ? 1u : 0u);
+            if (C::P_IN_TMEM) {
+              umma_bf16_ts(tmem + C::TCOL_DV, tmem + C::TCOL_PT + kk * 8, bd, IDESC_KV,
+                           (i > 0 || kk > 0) ? 1u : 0u);
+            } else {
+              const uint64_t ad = smem_desc_sw128(spt + (kk >> 2) * (BK * 128) + (kk & 3) * 32, 16, 1024);
+              umma_bf16_ss(tmem + C::TCOL_DV, ad, bd, IDESC_KV, (i > 0 || kk > 0) ? 1u : 0u);
+            }
           }
-  #pragma unroll
+#pragma unroll
           for (int kk = 0; kk < BQ / 16; ++kk) {  // dK += dS^T Q_i
             const uint64_t ad = smem_desc_sw128(sdst + (kk >> 2) * (BK * 128) + (kk & 3) * 32, 16, 1024);
             const uint64_t bd = smem_desc_sw128(sq + kk * 2048, BQ * 128, 1024);
@@ -309,7 +330,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           // the dQ columns must have been drained (dQ_{i-1})
           if (i >= 1 && !mbar_wait(BAR_DQE, (i - 1) & 1, abort_p)) break;
           tc_fence_after();
-  #pragma unroll
+#pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {  // dQ_i = dS K (A = dS^T as MN-major)
             const uint64_t ad = smem_desc_sw128(sdst + kk * 2048, BK * 128, 1024);
             const uint64_t bd = smem_desc_sw128(sk + kk * 2048, BK * 128, 1024);
@@ -321,70 +342,90 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (i + 1 == nq) umma_commit(BAR_DONE);
         }
       }
+    } else if (warp == 2) {
+      // ------------------------------------------------------- statistics
+      const long long rbase = (long long)b * prm.T;
+      for (int i = 0; i < nq; ++i) {
+        const int st = i % SSTAGES;
+        if (i >= SSTAGES && !mbar_wait_warp(BAR_TE(st), ((i / SSTAGES) - 1) & 1, abort_p)) break;
+        const int qt = kt + i;
+        float* stt = stat_base + st * (2 * BQ);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int qi = lane * 4 + u;
+          const int q = qt * BQ + qi;
+          float nl = 0.0f, nd = 0.0f;
+          if (q < prm.T) {
+            const long long si = (rbase + q) * prm.NH + h;
+            nl = -__ldg(prm.lse + si) * LOG2E;
+            nd = -__bfloat162float(prm.Dv[si]) * prm.scale;
+          }
+          stt[qi] = nl;
+          stt[BQ + qi] = nd;
+        }
+        mbar_arrive(BAR_TF(st));
+      }
+    } else {
+      // ------------------------------------------------- dQ reduce issuer
+      if (lane == 0) {
+        for (int j = 0; j < nq; ++j) {
+          if (!mbar_wait(BAR_DSF, j & 1, abort_p)) break;
+          for (int box = 0; box < HD / 32; ++box)
+            tma_reduce_add_3d(&tmdQ, sbase + C::OFF_DQS + box * (BQ * 128), col0 + box * 32,
+                              (kt + j) * BQ, b);
+          bulk_commit();
+          bulk_wait_read<0>();  // the staging buffer may be rewritten
+          mbar_arrive(BAR_DSE);
+        }
+        bulk_wait<0>();
+      }
     }
   } else {
     reg_alloc<REGS_COMPUTE>();
-    // -------------------------------------------------------------- compute
+    // ------------------------------------------------------------ compute
     const int cw = warp - 4;                   // 0..7
     const int quarter = warp & 3;              // TMEM lane quarter
     const int krow = quarter * 32 + lane;      // key row (and dQ query row) within the tile
     const int half = cw >> 2;                  // query columns half*64 .. +63
     const uint32_t tl = tmem + ((uint32_t)(quarter * 32) << 16);
-    const bool issuer = (cw == 0 && lane == 0);
     const float c = prm.scale_log2, sc = prm.scale;
-    // Failure handling: after a timed-out wait `ok` turns false and the work
-    // of the remaining tiles is skipped, but every thread still executes the
-    // same sequence of named barriers (compute_bar) so none can hang there.
     bool ok = true;
 
-    // dQ_j: TMEM -> fp32 staging (128-byte swizzle, 32-column boxes) -> TMA
-    // bulk reduce-add.  D=64 leaves the reduction in flight (its staging
-    // buffer is private); D=128 stages in the P^T/dS^T buffers and waits for
-    // the reduction to have read them before they are rewritten.
+    // dQ_j: TMEM -> fp32 staging (128-byte swizzle, 32-column boxes); the
+    // reduce issuer (warp 3) sends it to global memory
     auto drain_dq = [&](int j) {
       if (ok) ok = mbar_wait_warp(BAR_DQF, j & 1, abort_p);
-      if (C::EARLY_S) {
-        if (issuer) bulk_wait_read<0>();  // the previous reduction has read the staging
-        compute_bar();
-      }
-      if (ok) {
-        tc_fence_after();
-        constexpr int CPH = HD / 2;  // columns per half
-        uint8_t* dqs = gbase + C::OFF_DQS;
+      if (ok && j >= 1) ok = mbar_wait_warp(BAR_DSE, (j - 1) & 1, abort_p);
+      if (!ok) return;
+      tc_fence_after();
+      constexpr int CPH = HD / 2;  // columns per half
+      uint8_t* dqs = gbase + C::OFF_DQS;
 #pragma unroll
-        for (int cc = 0; cc < CPH; cc += 32) {
-          uint32_t r[32];
-          tmem_ld32(tl + C::TCOL_DQ + half * CPH + cc, r);
-          tmem_wait_ld_dep(r);
-          const int box = (half * CPH + cc) / 32;
-          uint8_t* rowp = dqs + box * (BQ * 128) + krow * 128;
+      for (int cc = 0; cc < CPH; cc += 32) {
+        uint32_t r[32];
+        tmem_ld32(tl + C::TCOL_DQ + half * CPH + cc, r);
+        tmem_wait_ld_dep(r);
+        const int box = (half * CPH + cc) / 32;
+        uint8_t* rowp = dqs + box * (BQ * 128) + krow * 128;
 #pragma unroll
-          for (int ch = 0; ch < 8; ++ch) {
-            uint4 v = make_uint4(r[ch * 4 + 0], r[ch * 4 + 1], r[ch * 4 + 2], r[ch * 4 + 3]);
-            *reinterpret_cast<uint4*>(rowp + ((ch ^ (krow & 7)) * 16)) = v;
-          }
+        for (int ch = 0; ch < 8; ++ch) {
+          uint4 v = make_uint4(r[ch * 4 + 0], r[ch * 4 + 1], r[ch * 4 + 2], r[ch * 4 + 3]);
+          *reinterpret_cast<uint4*>(rowp + ((ch ^ (krow & 7)) * 16)) = v;
         }
-        tc_fence_before();
-        mbar_arrive(BAR_DQE);
-        fence_proxy_async_smem();
       }
-      compute_bar();
-      if (issuer && ok && !*abort_p) {
-        const int qt = kt + j;
-        for (int box = 0; box < HD / 32; ++box)
-          tma_reduce_add_3d(&tmdQ, sbase + C::OFF_DQS + box * (BQ * 128), col0 + box * 32, qt * BQ, b);
-        bulk_commit();
-        if (!C::EARLY_S) bulk_wait_read<0>();
-      }
-      if (!C::EARLY_S) compute_bar();
+      tc_fence_before();
+      mbar_arrive(BAR_DQE);
+      fence_proxy_async_smem();
+      mbar_arrive(BAR_DSF);
     };
 
-    for (int i = 0; i < nq; ++i) {
-      const int st = i % C::STAGES;
-      if (ok) ok = mbar_wait_warp(BAR_SF, i & 1, abort_p);
+    for (int i = 0; ok && i < nq; ++i) {
+      const int ss = i % SSTAGES;
+      ok = mbar_wait_warp(BAR_SF, i & 1, abort_p);
+      if (!ok) break;
+      tc_fence_after();
       float s[64], dp[64];
-      if (ok) {
-        tc_fence_after();
+      {
         uint32_t ra[32], rb[32];
         tmem_ld32(tl + C::TCOL_S + half * 64, ra);
         tmem_ld32(tl + C::TCOL_S + half * 64 + 32, rb);
@@ -402,57 +443,52 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           dp[j] = __uint_as_float(ra[j]);
           dp[32 + j] = __uint_as_float(rb[j]);
         }
-        tc_fence_before();
-        mbar_arrive(BAR_SE);
-        // statistics of this tile were staged with Q_i/dO_i (BAR_QF), which
-        // completed before S^T_i could be computed
-        const float* stt = stat_base + st * (2 * BQ) + half * 64;
-        if (i == 0) p_ds_row<true>(s, dp, stt, stt + BQ, c, sc, krow, half * 64);
-        else p_ds_row<false>(s, dp, stt, stt + BQ, c, sc, krow, half * 64);
-        // P^T / dS^T buffers are free once the previous tile's MMAs are done
-        if (i >= 1) ok = mbar_wait_warp(BAR_PE, (i - 1) & 1, abort_p);
       }
-      if (ok) {
-        uint8_t* pt = gbase + C::OFF_PT + half * (BK * 128) + krow * 128;
-        uint8_t* dst = gbase + C::OFF_DST + half * (BK * 128) + krow * 128;
+      tc_fence_before();
+      mbar_arrive(BAR_SE);
+      ok = mbar_wait_warp(BAR_TF(ss), (i / SSTAGES) & 1, abort_p);
+      if (!ok) break;
+      const float* stt = stat_base + ss * (2 * BQ) + half * 64;
+      if (i == 0) p_ds_row<true>(s, dp, stt, stt + BQ, c, sc, krow, half * 64);
+      else p_ds_row<false>(s, dp, stt, stt + BQ, c, sc, krow, half * 64);
+      mbar_arrive(BAR_TE(ss));
+      // the previous tile's UMMAs must be done with P^T/dS^T (and, when the
+      // dQ staging shares their smem, its reduction must have read it)
+      if (i >= 1) ok = mbar_wait_warp(BAR_PE, (i - 1) & 1, abort_p);
+      if (ok && C::DQS_ALIAS && i >= 1) ok = mbar_wait_warp(BAR_DSE, (i - 1) & 1, abort_p);
+      if (!ok) break;
+      if (C::P_IN_TMEM) {
+        uint32_t pk[32];
 #pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          const int c0 = ch * 8;
-          uint4 v, w;
-          v.x = pack_bf16(s[c0 + 0], s[c0 + 1]);
-          v.y = pack_bf16(s[c0 + 2], s[c0 + 3]);
-          v.z = pack_bf16(s[c0 + 4], s[c0 + 5]);
-          v.w = pack_bf16(s[c0 + 6], s[c0 + 7]);
-          w.x = pack_bf16(dp[c0 + 0], dp[c0 + 1]);
-          w.y = pack_bf16(dp[c0 + 2], dp[c0 + 3]);
-          w.z = pack_bf16(dp[c0 + 4], dp[c0 + 5]);
-          w.w = pack_bf16(dp[c0 + 6], dp[c0 + 7]);
-          const int sw = (ch ^ (krow & 7)) * 16;
-          *reinterpret_cast<uint4*>(pt + sw) = v;
-          *reinterpret_cast<uint4*>(dst + sw) = w;
-        }
-        fence_proxy_async_smem();
-        tc_fence_before();
-        mbar_arrive(BAR_PR);
+        for (int j = 0; j < 32; ++j) pk[j] = pack_bf16(s[2 * j], s[2 * j + 1]);
+        tmem_st32(tl + C::TCOL_PT + half * 32, pk);
+        tmem_wait_st();
+      } else {
+        store_row_sw128(gbase + C::OFF_PT + half * (BK * 128) + krow * 128, krow, s);
       }
+      store_row_sw128(gbase + C::OFF_DST + half * (BK * 128) + krow * 128, krow, dp);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(BAR_PR);
       if (C::EARLY_S) {
         if (i >= 1) drain_dq(i - 1);
       } else {
         drain_dq(i);
       }
     }
-    if (C::EARLY_S && nq >= 1) drain_dq(nq - 1);
+    if (C::EARLY_S && ok && nq >= 1) drain_dq(nq - 1);
 
-    // ------------------------------------------------ dK / dV epilogue
-    const bool epi = ok && mbar_wait_warp(BAR_DONE, 0, abort_p);
+    // --------------------------------------------------- dK / dV epilogue
+    bool epi = ok && mbar_wait_warp(BAR_DONE, 0, abort_p);
+    // D=128: the last dQ staging (in the P^T/dS^T smem) must have been read
+    if (epi && C::DQS_ALIAS) epi = mbar_wait_warp(BAR_DSE, (nq - 1) & 1, abort_p);
     if (epi) {
       tc_fence_after();
-      // stage dV then dK (bf16) in the P^T / dS^T regions, one row per thread-half
       constexpr int CPH = HD / 2;
 #pragma unroll
       for (int which = 0; which < 2; ++which) {
         const uint32_t tcol = which == 0 ? C::TCOL_DV : C::TCOL_DK;
-        uint8_t* stage = gbase + (which == 0 ? C::OFF_PT : C::OFF_DST);
+        uint8_t* stage = gbase + (which == 0 ? C::OFF_EPI_V : C::OFF_EPI_K);
 #pragma unroll
         for (int cc = 0; cc < CPH; cc += 16) {
           uint32_t r[16];
@@ -476,16 +512,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       fence_proxy_async_smem();
     }
-    compute_bar();
-    if (issuer) {
-      if (epi) {
-        for (int kb = 0; kb < C::KB; ++kb) {
-          tma_store_3d(&tmdV, sbase + C::OFF_PT + kb * BK * 128, col0 + kb * 64, kt * BK, b);
-          tma_store_3d(&tmdK, sbase + C::OFF_DST + kb * BK * 128, col0 + kb * 64, kt * BK, b);
-        }
-        bulk_commit();
+    // one named barrier for the 256 compute threads, reached on every path
+    epi = bar_red_and(1, NCOMP, epi);
+    if (epi && cw == 0 && lane == 0) {
+      for (int kb = 0; kb < C::KB; ++kb) {
+        tma_store_3d(&tmdV, sbase + C::OFF_EPI_V + kb * BK * 128, col0 + kb * 64, kt * BK, b);
+        tma_store_3d(&tmdK, sbase + C::OFF_EPI_K + kb * BK * 128, col0 + kb * 64, kt * BK, b);
       }
-      bulk_wait<0>();  // every bulk operation of this CTA has completed
+      bulk_commit();
+      bulk_wait<0>();
     }
   }
 
