@@ -4,9 +4,8 @@
 // roles in a persistent kernel.
 //
 // Work unit: one (batch*head, 256-row query pair) = two 128-row query tiles
-// A (rows 256p..256p+127) and B (the next 128 rows).  Units are ordered
-// heaviest first (causal work grows with p) and dealt round-robin to one CTA
-// per SM.  Per key tile j (128 keys) of a unit:
+// A (rows 256p..256p+127) and B (the next 128 rows), dealt to one CTA per SM
+// (see unit_of_round).  Per key tile j (128 keys) of a unit:
 //   S_X  = Q_X K_j^T          UMMA 128x128xD, fp32 in TMEM      (X = A, B)
 //   P_X  = exp2(S_X c - m_X)  softmax warpgroup X, c = log2(e)/sqrt(D), bf16
 //   O_X += P_X V_j            UMMA 128xDx128, fp32 in TMEM
@@ -84,21 +83,35 @@ struct FwdParams {
   uint32_t* status;
 };
 
-// Unit u (heaviest first) -> (pair, bh) and its tiles' key-tile counts.
+// Work units in (batch*head)-major order, pairs heaviest first within a
+// (batch, head): k -> (bh = k / npairs, pair = npairs-1 - k % npairs).  They
+// are dealt in rounds of gridDim.x: in round g CTA c takes k = g*G + c when
+// g is even and g*G + (G-1-c) when g is odd, so the units running at the same
+// time come from a few (batch, head) pairs (their K/V stay in L2) and every
+// CTA alternates between heavier and lighter query pairs.
 struct Unit {
   int pair, b, h, nA, nB, nkv;
 };
 
-__device__ __forceinline__ Unit decode_unit(const FwdParams& prm, int u) {
+__device__ __forceinline__ Unit decode_unit(const FwdParams& prm, int k) {
   Unit x;
-  x.pair = prm.npairs - 1 - u / prm.nbh;
-  const int bh = prm.bh_begin + u % prm.nbh;
+  x.pair = prm.npairs - 1 - k % prm.npairs;
+  const int bh = prm.bh_begin + k / prm.npairs;
   x.b = bh / prm.NH;
   x.h = bh % prm.NH;
   x.nA = 2 * x.pair + 1;                                   // key tiles 0..2p
   x.nB = (2 * x.pair + 1 < prm.nqt) ? 2 * x.pair + 2 : 0;  // tile B inside T?
   x.nkv = x.nB > 0 ? x.nB : x.nA;
   return x;
+}
+
+// The g-th unit of this CTA, or -1 when it has none left (-2: none this round).
+__device__ __forceinline__ int unit_of_round(const FwdParams& prm, int g) {
+  const int G = gridDim.x;
+  if ((long long)g * G >= prm.nunits) return -1;
+  const int c = blockIdx.x;
+  const int k = g * G + ((g & 1) ? G - 1 - c : c);
+  return k < prm.nunits ? k : -2;
 }
 
 template <int HD>
@@ -172,8 +185,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tma_prefetch_desc(&tmV);
       uint32_t qc = 0, kc = 0, vc = 0;
       bool ok = true;
-      for (int u = blockIdx.x; ok && u < prm.nunits; u += gridDim.x) {
-        const Unit un = decode_unit(prm, u);
+      for (int g = 0; ok; ++g) {
+        const int k = unit_of_round(prm, g);
+        if (k == -1) break;
+        if (k < 0) continue;
+        const Unit un = decode_unit(prm, k);
         const int col0 = un.h * HD;
         const int qs = qc % C::QST;
         if (qc >= C::QST && !mbar_wait(BAR_QE(qs), ((qc / C::QST) - 1) & 1, abort_p)) break;
@@ -210,8 +226,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t pvc[2] = {0, 0};  // PV_X issued so far
       uint32_t uc[2] = {0, 0};   // units in which tile X was active
       bool ok = true;
-      for (int u = blockIdx.x; ok && u < prm.nunits; u += gridDim.x) {
-        const Unit un = decode_unit(prm, u);
+      for (int g = 0; ok; ++g) {
+        const int k = unit_of_round(prm, g);
+        if (k == -1) break;
+        if (k < 0) continue;
+        const Unit un = decode_unit(prm, k);
         const int n[2] = {un.nA, un.nB};
         const int qs = qc % C::QST;
         if (!mbar_wait(BAR_QF(qs), (qc / C::QST) & 1, abort_p)) break;
@@ -295,8 +314,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint8_t* pbuf = gbase + C::OFF_P + x * C::P_BYTES;
     uint32_t sc = 0;  // S_X consumed so far (== P_X produced)
     bool ok = true;
-    for (int u = blockIdx.x; ok && u < prm.nunits; u += gridDim.x) {
-      const Unit un = decode_unit(prm, u);
+    for (int g = 0; ok; ++g) {
+      const int k = unit_of_round(prm, g);
+      if (k == -1) break;
+      if (k < 0) continue;
+      const Unit un = decode_unit(prm, k);
       const int nt = x == 0 ? un.nA : un.nB;
       if (nt == 0) continue;
       const int qtile = 2 * un.pair + x;
@@ -327,16 +349,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           for (int i = 0; i < BN; ++i)
             if (i > row) s[i] = -INFINITY;
         }
-        // row maximum with 8 independent partial maxima (short dependency chains)
+        // row maximum: 8 independent partial maxima, 3-input max (short chains)
         float pm[8];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) pm[q] = s[q];
+        for (int q = 0; q < 8; ++q) pm[q] = fmaxf(s[q], s[8 + q]);
 #pragma unroll
-        for (int i = 8; i < BN; i += 8)
+        for (int i = 16; i < BN; i += 16)
 #pragma unroll
-          for (int q = 0; q < 8; ++q) pm[q] = fmaxf(pm[q], s[i + q]);
-        const float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
-                               fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
+          for (int q = 0; q < 8; ++q) pm[q] = fmax3(pm[q], s[i + q], s[i + 8 + q]);
+        const float mx = fmax3(fmax3(pm[0], pm[1], pm[2]), fmax3(pm[3], pm[4], pm[5]),
+                               fmaxf(pm[6], pm[7]));
         const float m_new = fmaxf(m_used, mx * c);
         // PV_X(j-1) must be complete before P_X(j) overwrites the P buffer and
         // before O_X is rescaled
@@ -364,15 +386,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tmem_wait_st();
           }
         }
-        // P = 2^(S*c - m) with packed fp32x2 FMAs; row sum in 4 packed partials
+        // P = 2^(S*c - m) with packed fp32x2 FMAs; 3 of every 8 column pairs
+        // on the FMA pipe (ex2_poly2), the rest on MUFU; row sum in 4 packed
+        // partials
         const float2 c2 = make_float2(c, c), nm2 = make_float2(-m_used, -m_used);
+        const float2 lo2 = make_float2(-127.0f, -127.0f);
         float2 ps[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                         make_float2(0.f, 0.f)};
 #pragma unroll
         for (int i = 0; i < BN; i += 2) {
           const float2 t = __ffma2_rn(make_float2(s[i], s[i + 1]), c2, nm2);
-          s[i] = ex2(t.x);
-          s[i + 1] = ex2(t.y);
+          if (((i >> 1) & 7) >= 5) {
+            const float2 e = ex2_poly2(make_float2(fmaxf(t.x, lo2.x), fmaxf(t.y, lo2.y)));
+            s[i] = e.x;
+            s[i + 1] = e.y;
+          } else {
+            s[i] = ex2(t.x);
+            s[i + 1] = ex2(t.y);
+          }
           ps[(i >> 1) & 3] = __fadd2_rn(ps[(i >> 1) & 3], make_float2(s[i], s[i + 1]));
         }
         l_sum += (ps[0].x + ps[0].y) + (ps[1].x + ps[1].y) + (ps[2].x + ps[2].y) +
