@@ -375,30 +375,6 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return r;
 }
 
-// 2^x on the FMA pipe, for two values at once (offloads the MUFU unit).
-// Range reduction x = n + f, f in [-1/2, 1/2], by adding 1.5*2^23 (round to
-// nearest; Cody & Waite); 2^f by a degree-3 polynomial with p(0) = 1 whose
-// other coefficients were fitted for minimum relative error on [-1/2, 1/2]
-// (max relative error 1.0e-4); 2^n by adding n to the exponent field
-// (Schraudolph 1999).  Requires x >= -127 (then 2^-127 maps to +0.0 exactly)
-// and x < 128.
-__device__ __forceinline__ float2 ex2_poly2(float2 x) {
-  const float2 magic = make_float2(12582912.0f, 12582912.0f);
-  const float2 nmagic = make_float2(-12582912.0f, -12582912.0f);
-  const float2 c3 = make_float2(0x1.c2a15cp-5f, 0x1.c2a15cp-5f);
-  const float2 c2 = make_float2(0x1.f00bfep-3f, 0x1.f00bfep-3f);
-  const float2 c1 = make_float2(0x1.62f5fap-1f, 0x1.62f5fap-1f);
-  const float2 one = make_float2(1.0f, 1.0f);
-  const float2 y = __fadd2_rn(x, magic);      // low mantissa bits hold round(x)
-  const float2 n = __fadd2_rn(y, nmagic);     // round(x) as a float
-  const float2 f = __fadd2_rn(x, make_float2(-n.x, -n.y));
-  float2 p = __ffma2_rn(f, c3, c2);
-  p = __ffma2_rn(p, f, c1);
-  p = __ffma2_rn(p, f, one);
-  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(y.x) << 23)),
-                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(y.y) << 23)));
-}
-
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
