@@ -9,10 +9,11 @@
 //   S_X  = Q_X K_j^T          UMMA 128x128xD, fp32 in TMEM      (X = A, B)
 //   P_X  = exp2(S_X c - m_X)  softmax warpgroup X, c = log2(e)/sqrt(D), bf16
 //   O_X += P_X V_j            UMMA 128xDx128, fp32 in TMEM
-// Tile A needs key tiles 0..2p, tile B 0..2p+1 (causal).  S_X(j+1) is issued
-// as soon as softmax X has read S_X(j) into registers, so each softmax
-// warpgroup finds its next scores ready and the tensor core works on one tile
-// while the other's softmax runs; K_j/V_j are loaded once for both tiles.
+// Tile A needs key tiles 0..2p, tile B 0..2p+1 (causal).  The tensor core
+// works on one tile while the other tile's softmax runs (ping-pong); at D=64
+// S_X(j+1) is issued as soon as softmax X has read S_X(j) into registers, so
+// each softmax warpgroup finds its next scores ready.  K_j/V_j are loaded once
+// for both tiles.
 // Roles (384 threads, three warpgroups):
 //   warpgroup 0  warp 0 TMA producer (Q pair per unit, K/V tile rings);
 //                warp 1 owns TMEM (S_A, S_B, O_A, O_B) and issues every UMMA;
@@ -57,6 +58,10 @@ struct FwdCfg {
   static constexpr int QST = HD == 64 ? 2 : 1;  // Q-pair stages
   static constexpr int KST = 2;                 // K tile stages
   static constexpr int VST = HD == 64 ? 2 : 1;  // V tile stages
+  // UMMA issue order: D=64 issues S_X(j+1) before PV_X(j) (softmax-bound: the
+  // next scores should be ready early); D=128 interleaves PV_X(j), S_X(j+1)
+  // (tensor-bound: keeps PV close to its P)
+  static constexpr bool EARLY_S = HD == 64;
   static constexpr uint32_t QT_BYTES = BM * HD * 2;  // one query tile
   static constexpr uint32_t KV_BYTES = BN * HD * 2;
   static constexpr uint32_t P_BYTES = BM * BN * 2;
@@ -271,17 +276,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         ok = wait_k(0) && issue_s(0, 0) && (n[1] == 0 || issue_s(1, 0));
         if (ok) umma_commit(BAR_KE(kc % C::KST));
         for (int j = 0; ok && j < un.nkv; ++j) {
-          // S_X(j+1) as soon as softmax X has read S_X(j) (issue_s waits for
-          // that), so the next scores are ready before this tile's softmax ends
-          if (j + 1 < un.nkv) {
-            if (!wait_k(j + 1)) { ok = false; break; }
-            if (j + 1 < n[0] && !issue_s(0, j + 1)) { ok = false; break; }
-            if (j + 1 < n[1] && !issue_s(1, j + 1)) { ok = false; break; }
-            umma_commit(BAR_KE((kc + j + 1) % C::KST));    // K_{j+1} consumed
+          if (C::EARLY_S) {
+            // S_X(j+1) as soon as softmax X has read S_X(j) (issue_s waits for
+            // that), so the next scores are ready before this tile's softmax ends
+            if (j + 1 < un.nkv) {
+              if (!wait_k(j + 1)) { ok = false; break; }
+              if (j + 1 < n[0] && !issue_s(0, j + 1)) { ok = false; break; }
+              if (j + 1 < n[1] && !issue_s(1, j + 1)) { ok = false; break; }
+              umma_commit(BAR_KE((kc + j + 1) % C::KST));  // K_{j+1} consumed
+            }
+            if (!wait_v(j)) { ok = false; break; }
+            if (j < n[0] && !issue_pv(0, j)) { ok = false; break; }
+            if (j < n[1] && !issue_pv(1, j)) { ok = false; break; }
+          } else {
+            // PV_A(j) S_A(j+1) | PV_B(j) S_B(j+1)
+            if (!wait_v(j)) { ok = false; break; }
+            const bool lastA = (j + 1 >= n[0]);
+            if (j < n[0]) {
+              if (!issue_pv(0, j)) { ok = false; break; }
+              if (!lastA && (!wait_k(j + 1) || !issue_s(0, j + 1))) { ok = false; break; }
+            }
+            if (j < n[1]) {
+              if (!issue_pv(1, j)) { ok = false; break; }
+              if (j + 1 < n[1] && ((lastA && !wait_k(j + 1)) || !issue_s(1, j + 1))) { ok = false; break; }
+            }
+            if (j + 1 < un.nkv) umma_commit(BAR_KE((kc + j + 1) % C::KST));  // K_{j+1} consumed
           }
-          if (!wait_v(j)) { ok = false; break; }
-          if (j < n[0] && !issue_pv(0, j)) { ok = false; break; }
-          if (j < n[1] && !issue_pv(1, j)) { ok = false; break; }
           umma_commit(BAR_VE((vc + j) % C::VST));           // V_j consumed
           if (j + 1 == un.nkv) umma_commit(BAR_QE(qs));     // every S of the unit issued
         }
