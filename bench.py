@@ -73,7 +73,7 @@ class ClockSampler:
             self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=self.tmp, stderr=subprocess.DEVNULL)
+                 "-lms", "50"], stdout=self.tmp, stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
 
@@ -466,8 +466,8 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--impl", default="native", choices=["native", "reference"])

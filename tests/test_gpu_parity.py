@@ -183,14 +183,20 @@ def test_determinism(A):
     check("dQ rerun", f32(r1[3]), f32(r2[3]), 1e-5, 1e-6)
 
 
-def test_compute_qkv(A, oracle_mod):
-    B, M, H, D = 2, 256, 6, 64
+@pytest.mark.parametrize("B,M,H,D", [
+    (2, 256, 6, 64),     # N = 384 (128-column tiles)
+    (1, 64, 3, 64),      # N = 192 (64-column tiles), one partial row tile
+    (3, 192, 2, 128),    # N = 256, rows not a multiple of 128
+    (64, 256, 6, 64),    # config 5: rows = 16384, N = 384
+])
+def test_compute_qkv(A, oracle_mod, B, M, H, D):
     N = H * D
     X = normal_bf16(B * M * N, 31, 5).reshape(B, M, N)
     W = [normal_bf16(N * N, 31, 6 + i, 0.02).reshape(N, N) for i in range(3)]
     p = A.make_params(M, H, D)
     q, k, v = A.computeQKV(up(X), up(W[0]), up(W[1]), up(W[2]), p, B)
     torch.cuda.synchronize()
+    assert A.device_status() == 0
     rq, rk, rv, rq32, rk32, rv32 = oracle_mod.compute_qkv(X, *W, want_f32=True)
     check("Q", bf(q), rq32, 1e-2, 5e-3)
     check("K", bf(k), rk32, 1e-2, 5e-3)
