@@ -1,10 +1,10 @@
 // flash_bwd_sm100.cu -- flashAttentionBackward (attention.metal:198-299) on
 // sm_100a with tcgen05 UMMA, TMEM accumulators and TMA.
 //
-// Work unit, as in the reference (attention.metal:219-223): one CTA owns one
-// 128-key tile of one (batch, head) and walks the query tiles i from the
-// diagonal to the end (causal: earlier queries never see these keys).  Per
-// query tile (128 queries):
+// Work unit, as in the reference (attention.metal:219-223): one 128-key tile
+// of one (batch, head), walking the query tiles i from the diagonal to the end
+// (causal: earlier queries never see these keys).  Per query tile (128
+// queries):
 //   S^T  = K Q_i^T                 UMMA 128x128xD  -> TMEM
 //   dP^T = V dO_i^T                UMMA 128x128xD  -> TMEM
 //   P^T  = exp2(S^T c - l_i log2e), 0 where key > query   (compute warps)
@@ -16,28 +16,39 @@
 // dS^T is written once to shared memory (bf16, K-major 128-byte swizzle); the
 // dQ UMMA reads the same buffer as an MN-major operand.  At D=64, P^T goes to
 // TMEM (bf16 pairs) and dV's UMMA takes it from there; at D=128 TMEM is full
-// and P^T goes to shared memory like dS^T.  dK/dV are owned by the CTA and
-// stored once (bf16); dQ is accumulated in fp32 by the bulk reductions of
-// every key tile, so the launcher zeroes it first (the reference's host zeroes
-// it, model.h:549).  The CTAs of one (batch, head) are launched next to each
-// other, so its Q/dO tiles are re-read from L2 rather than HBM.
+// and P^T goes to shared memory like dS^T.  dK/dV are owned by the unit and
+// stored once (bf16, straight from registers to global memory); dQ is
+// accumulated in fp32 by the bulk reductions of every key tile, so the
+// launcher zeroes it first (the reference's host zeroes it, model.h:549).
+//
+// Scheduling: units are ordered (batch, head)-major, key tiles in order
+// (heaviest first), and dealt in rounds of gridDim.x, alternating direction
+// (CTA c takes position c in even rounds and gridDim.x-1-c in odd ones), so
+// the units in flight share a few (batch, head) Q/dO sets in L2.  For short
+// sequences at D=64 the kernel is persistent (one CTA per SM walks many
+// units): the next unit's K/V (double-buffered), Q/dO tiles and first S^T/dP^T
+// are fetched and computed while the current unit finishes, and a unit's
+// dK/dV epilogue runs after the next unit's first step has been handed to the
+// tensor core; otherwise every CTA takes one unit and the smem goes to a
+// deeper Q/dO ring.
 //
 // Roles (384 threads, three warpgroups):
 //   warpgroup 0 (120 registers per thread after setmaxnreg):
-//     warp 0   TMA producer: K/V once, Q_i/dO_i into a STAGES-deep ring
+//     warp 0   TMA producer: K/V per unit, Q_i/dO_i into a STAGES-deep ring
 //     warp 1   TMEM owner; lane 0 issues every UMMA and commit
 //     warp 2   statistics: stages -l_i*log2(e) and -D_i/sqrt(D) per query
 //              (strided in global memory) 8 tiles ahead
 //     warp 3   lane 0 issues the dQ bulk reductions
 //   warpgroups 1, 2 (192 registers): compute, thread = key row = TMEM lane;
 //              warpgroup 1 takes query columns 0-63, warpgroup 2 columns
-//              64-127; dQ drain into the staging buffer and dK/dV epilogue.
-// D=64 schedule ("early S"): S^T/dP^T of tile i+1 are issued as soon as the
-// compute warps have read tile i's, so they run on the tensor core while the
-// compute warps form P^T_i/dS^T_i; dV_i, dK_i and dQ_i follow.  dQ_{i-1} is
-// drained after tile i is handed over.  D=128 has no TMEM room for that (S^T,
-// dP^T, dV, dK fill all 512 columns; dQ reuses the S^T columns) and runs the
-// steps in order, draining dQ_i before S^T_{i+1}.
+//              64-127; dQ drain into the staging buffer and dK/dV epilogue
+//              (each thread stores its key row's slice).
+// D=64 schedule ("early S"): S^T/dP^T of the next query tile are issued as
+// soon as the compute warps have read the current one, so they run on the
+// tensor core while the compute warps form P^T/dS^T; dV, dK and dQ follow, and
+// dQ of a tile is drained after the next tile is handed over.  D=128 has no
+// TMEM room for that (S^T, dP^T, dV, dK fill all 512 columns; dQ reuses the
+// S^T columns) and runs the steps in order, draining dQ before the next S^T.
 //
 // Conventions as the reference: P = exp(S/sqrt(D) - l) with l read as stored,
 // D read as stored (bf16), dS includes 1/sqrt(D).  The reference rounds S,
@@ -46,9 +57,8 @@
 // bf16 (the UMMA operand type).
 //
 // All mbarrier waits are bounded (about 2 s); on time-out the CTA winds down,
-// frees its TMEM and sets STATUS_BWD_TIMEOUT.  The compute warps meet only at
-// mbarriers inside the loop and at one named barrier (same count on every
-// path) for the epilogue.
+// frees its TMEM and sets STATUS_BWD_TIMEOUT.  Warps meet only at mbarriers
+// (no named barriers), so a failed wait cannot leave a warp stuck at one.
 #include "common.cuh"
 #include "sm100.cuh"
 #include "tmap.h"
@@ -58,7 +68,7 @@ namespace {
 
 using namespace sm100;
 
-constexpr int BK = 128;  // keys per CTA
+constexpr int BK = 128;  // keys per unit
 constexpr int BQ = 128;  // queries per step
 constexpr int NUM_THREADS = 384;
 constexpr int NCOMP = 256;  // compute threads (warpgroups 1 and 2)
@@ -68,15 +78,19 @@ constexpr int REGS_COMPUTE = 192;   // warpgroups 1, 2 after setmaxnreg.inc
 static_assert(128 * REGS_PRODUCER + 256 * REGS_COMPUTE == NUM_THREADS * LAUNCH_REGS,
               "register split must equal the launch allocation");
 constexpr int SSTAGES = 8;  // statistics stages
+constexpr int PERSIST_MAX_NKT = 16;  // persistent launch when T/128 <= this (D=64)
 constexpr float LOG2E = 1.4426950408889634f;
 
-template <int HD>
+template <int HD, bool PERSIST>
 struct BwdCfg {
   static constexpr int KB = HD / 64;
   static constexpr bool D64 = HD == 64;
-  static constexpr int STAGES = D64 ? 3 : 1;     // Q_i/dO_i stages
+  // Q_i/dO_i stages and K/V buffers: a persistent CTA double-buffers K/V to
+  // prefetch the next unit; otherwise the smem goes to a deeper Q/dO ring
+  static constexpr int STAGES = D64 ? (PERSIST ? 2 : 3) : 1;
+  static constexpr int KVB = (D64 && PERSIST) ? 2 : 1;
   static constexpr bool P_IN_TMEM = D64;         // P^T in TMEM (else smem)
-  static constexpr bool EARLY_S = D64;           // S_{i+1} before dV_i/dK_i/dQ_i
+  static constexpr bool EARLY_S = D64;           // next S^T before dV/dK/dQ
   static constexpr bool DQ_ALIAS = !D64;         // dQ accumulator reuses the S^T columns
   static constexpr bool DQS_ALIAS = !D64;        // dQ staging reuses the P^T/dS^T smem
   static constexpr uint32_t KV_BYTES = BK * HD * 2;
@@ -84,22 +98,19 @@ struct BwdCfg {
   static constexpr uint32_t PT_BYTES = BK * BQ * 2;
   static constexpr uint32_t DQS_BYTES = BQ * HD * 4;
   static constexpr uint32_t STAT_BYTES = 2 * BQ * 4;  // -l*log2e[128], -D/sqrt(D)[128]
-  static constexpr uint32_t OFF_K = 0;
-  static constexpr uint32_t OFF_V = OFF_K + KV_BYTES;
-  static constexpr uint32_t OFF_Q = OFF_V + KV_BYTES;                // [STAGES]
-  static constexpr uint32_t OFF_DO = OFF_Q + STAGES * QD_BYTES;      // [STAGES]
-  static constexpr uint32_t OFF_PT = OFF_DO + STAGES * QD_BYTES;     // only without P_IN_TMEM
+  static constexpr uint32_t OFF_K = 0;                                // [KVB]
+  static constexpr uint32_t OFF_V = OFF_K + KVB * KV_BYTES;           // [KVB]
+  static constexpr uint32_t OFF_Q = OFF_V + KVB * KV_BYTES;           // [STAGES]
+  static constexpr uint32_t OFF_DO = OFF_Q + STAGES * QD_BYTES;       // [STAGES]
+  static constexpr uint32_t OFF_PT = OFF_DO + STAGES * QD_BYTES;      // only without P_IN_TMEM
   static constexpr uint32_t OFF_DST = OFF_PT + (P_IN_TMEM ? 0 : PT_BYTES);
   static constexpr uint32_t OFF_DQS = DQS_ALIAS ? OFF_PT : OFF_DST + PT_BYTES;
   static constexpr uint32_t OFF_STAT = DQS_ALIAS ? OFF_DST + PT_BYTES : OFF_DQS + DQS_BYTES;
   static constexpr uint32_t OFF_BAR = OFF_STAT + SSTAGES * STAT_BYTES;
-  // epilogue staging of dV and dK (bf16): the P^T/dS^T region (D=128) or the
-  // dS^T region (D=64, 16 KB each)
-  static constexpr uint32_t OFF_EPI_V = P_IN_TMEM ? OFF_DST : OFF_PT;
-  static constexpr uint32_t OFF_EPI_K = P_IN_TMEM ? OFF_DST + BK * HD * 2 : OFF_DST;
-  // kv_full, qd_full[S], qd_empty[S], st_full[8], st_empty[8], s_full, s_free,
-  // p_ready, p_free, dq_full, dq_free, dqs_full, dqs_free, done
-  static constexpr int NBAR = 1 + 2 * STAGES + 2 * SSTAGES + 9;
+  // kv_full/empty[KVB], qd_full/empty[S], st_full/empty[8], then s_full,
+  // s_free, p_ready, p_free, dq_full, dq_free, dqs_full, dqs_free, done,
+  // acc_free
+  static constexpr int NBAR = 2 * KVB + 2 * STAGES + 2 * SSTAGES + 10;
   static constexpr uint32_t OFF_TSLOT = OFF_BAR + NBAR * 8;
   static constexpr uint32_t SMEM_BYTES = OFF_TSLOT + 16 + 1024;
   static constexpr uint32_t TCOL_S = 0;
@@ -111,12 +122,81 @@ struct BwdCfg {
 };
 
 struct BwdParams {
-  int T, N, NH, bh_begin, nbh, nkt;
+  int T, N, NH, bh_begin, nbh, nkt, nunits;
   float scale, scale_log2;
   const float* lse;
   const __nv_bfloat16* Dv;
   uint32_t* status;
 };
+
+// Unit k -> (batch, head, key tile); its query tiles are kt .. nkt-1.
+struct BUnit {
+  int b, h, kt, nq;
+};
+
+__device__ __forceinline__ BUnit bwd_unit(const BwdParams& prm, int k) {
+  BUnit u;
+  const int bh = prm.bh_begin + k / prm.nkt;
+  u.kt = k % prm.nkt;
+  u.b = bh / prm.NH;
+  u.h = bh % prm.NH;
+  u.nq = prm.nkt - u.kt;
+  return u;
+}
+
+// The unit of this CTA in round g: -1 when rounds are exhausted, -2 when this
+// CTA has none in round g (last, partial round).
+__device__ __forceinline__ int bwd_unit_of_round(const BwdParams& prm, int g) {
+  const int G = gridDim.x;
+  if ((long long)g * G >= prm.nunits) return -1;
+  const int c = blockIdx.x;
+  const int k = g * G + ((g & 1) ? G - 1 - c : c);
+  return k < prm.nunits ? k : -2;
+}
+
+// Walks this CTA's (unit, query tile) steps in order.  t counts steps over
+// all units, uc counts units.
+struct StepIter {
+  int g;        // next round to look at
+  BUnit u;
+  int i;        // query tile index within the unit
+  uint32_t t;   // global step
+  uint32_t uc;  // unit counter
+  bool valid;
+};
+
+__device__ __forceinline__ bool next_unit(const BwdParams& prm, StepIter& s) {
+  for (;;) {
+    const int k = bwd_unit_of_round(prm, s.g);
+    if (k == -1) return false;
+    ++s.g;
+    if (k >= 0) {
+      s.u = bwd_unit(prm, k);
+      return true;
+    }
+  }
+}
+
+__device__ __forceinline__ StepIter first_step(const BwdParams& prm) {
+  StepIter s;
+  s.g = 0;
+  s.i = 0;
+  s.t = 0;
+  s.uc = 0;
+  s.valid = next_unit(prm, s);
+  return s;
+}
+
+__device__ __forceinline__ void advance(const BwdParams& prm, StepIter& s) {
+  ++s.t;
+  if (s.i + 1 < s.u.nq) {
+    ++s.i;
+    return;
+  }
+  s.i = 0;
+  ++s.uc;
+  s.valid = next_unit(prm, s);
+}
 
 // P^T and dS^T for 64 query columns of one key row.  s[] holds S^T on entry
 // and P^T on exit; dp[] holds dP^T on entry and dS^T on exit.  nl = -l*log2e
@@ -169,50 +249,46 @@ __device__ __forceinline__ void store_row_sw128(uint8_t* rowp, int row, const fl
   }
 }
 
-template <int HD>
+template <int HD, bool PERSIST>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     flash_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
-                     const __grid_constant__ CUtensorMap tmdQ, const __grid_constant__ CUtensorMap tmdK,
-                     const __grid_constant__ CUtensorMap tmdV, const BwdParams prm) {
-  using C = BwdCfg<HD>;
+                     const __grid_constant__ CUtensorMap tmdQ, __nv_bfloat16* __restrict__ dK,
+                     __nv_bfloat16* __restrict__ dV, const BwdParams prm) {
+  using C = BwdCfg<HD, PERSIST>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ int abort_flag;
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t sbase = (raw + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (sbase - raw);
-
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  // the key tiles of one (batch, head) are adjacent in launch order (heaviest
-  // first within the group), so they share Q/dO through L2
-  const int idx = blockIdx.x;
-  const int bh = prm.bh_begin + idx / prm.nkt;
-  const int kt = idx % prm.nkt;
-  const int b = bh / prm.NH, h = bh % prm.NH;
-  const int nq = prm.nkt - kt;  // query tiles kt .. nkt-1
-  const int col0 = h * HD;
 
   const uint32_t bar0 = sbase + C::OFF_BAR;
-  const uint32_t BAR_KV = bar0;
-  auto BAR_QF = [&](int s) { return bar0 + 8u * (1 + s); };
-  auto BAR_QE = [&](int s) { return bar0 + 8u * (1 + C::STAGES + s); };
-  auto BAR_TF = [&](int s) { return bar0 + 8u * (1 + 2 * C::STAGES + s); };
-  auto BAR_TE = [&](int s) { return bar0 + 8u * (1 + 2 * C::STAGES + SSTAGES + s); };
-  const uint32_t BAR_SF = bar0 + 8u * (1 + 2 * C::STAGES + 2 * SSTAGES);
+  auto BAR_KF = [&](int s) { return bar0 + 8u * s; };
+  auto BAR_KE = [&](int s) { return bar0 + 8u * (C::KVB + s); };
+  auto BAR_QF = [&](int s) { return bar0 + 8u * (2 * C::KVB + s); };
+  auto BAR_QE = [&](int s) { return bar0 + 8u * (2 * C::KVB + C::STAGES + s); };
+  auto BAR_TF = [&](int s) { return bar0 + 8u * (2 * C::KVB + 2 * C::STAGES + s); };
+  auto BAR_TE = [&](int s) { return bar0 + 8u * (2 * C::KVB + 2 * C::STAGES + SSTAGES + s); };
+  const uint32_t BAR_SF = bar0 + 8u * (2 * C::KVB + 2 * C::STAGES + 2 * SSTAGES);
   const uint32_t BAR_SE = BAR_SF + 8;
   const uint32_t BAR_PR = BAR_SF + 16;
   const uint32_t BAR_PE = BAR_SF + 24;
   const uint32_t BAR_DQF = BAR_SF + 32;
   const uint32_t BAR_DQE = BAR_SF + 40;
-  const uint32_t BAR_DSF = BAR_SF + 48;  // dQ staging written
-  const uint32_t BAR_DSE = BAR_SF + 56;  // dQ staging read by the reduction
-  const uint32_t BAR_DONE = BAR_SF + 64;
+  const uint32_t BAR_DSF = BAR_SF + 48;   // dQ staging written
+  const uint32_t BAR_DSE = BAR_SF + 56;   // dQ staging read by the reduction
+  const uint32_t BAR_DONE = BAR_SF + 64;  // a unit's last UMMA completed
+  const uint32_t BAR_ACC = BAR_SF + 72;   // dK/dV TMEM read by the epilogue
   const uint32_t tslot = sbase + C::OFF_TSLOT;
   float* stat_base = reinterpret_cast<float*>(gbase + C::OFF_STAT);
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
-    mbar_init(BAR_KV, 1);
+    for (int s = 0; s < C::KVB; ++s) {
+      mbar_init(BAR_KF(s), 1);
+      mbar_init(BAR_KE(s), 1);
+    }
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(BAR_QF(s), 1);
       mbar_init(BAR_QE(s), 1);
@@ -230,6 +306,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     mbar_init(BAR_DSF, NCOMP);
     mbar_init(BAR_DSE, 1);
     mbar_init(BAR_DONE, 1);
+    mbar_init(BAR_ACC, NCOMP);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -249,22 +326,28 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (lane == 0) {
         tma_prefetch_desc(&tmQ);
         tma_prefetch_desc(&tmdO);
-        mbar_arrive_expect_tx(BAR_KV, 2 * C::KV_BYTES);
-        for (int kb = 0; kb < C::KB; ++kb) {
-          tma_load_3d(sbase + C::OFF_K + kb * BK * 128, &tmK, BAR_KV, col0 + kb * 64, kt * BK, b);
-          tma_load_3d(sbase + C::OFF_V + kb * BK * 128, &tmV, BAR_KV, col0 + kb * 64, kt * BK, b);
-        }
-        for (int i = 0; i < nq; ++i) {
-          const int st = i % C::STAGES;
-          if (i >= C::STAGES && !mbar_wait(BAR_QE(st), ((i - C::STAGES) / C::STAGES) & 1, abort_p))
-            break;
-          const int qt = kt + i;
+        for (StepIter s = first_step(prm); s.valid; advance(prm, s)) {
+          const int col0 = s.u.h * HD;
+          if (s.i == 0) {  // K/V of a new unit
+            const int kvs = s.uc % C::KVB;
+            if (s.uc >= C::KVB && !mbar_wait(BAR_KE(kvs), ((s.uc / C::KVB) - 1) & 1, abort_p)) break;
+            mbar_arrive_expect_tx(BAR_KF(kvs), 2 * C::KV_BYTES);
+            for (int kb = 0; kb < C::KB; ++kb) {
+              tma_load_3d(sbase + C::OFF_K + kvs * C::KV_BYTES + kb * BK * 128, &tmK, BAR_KF(kvs),
+                          col0 + kb * 64, s.u.kt * BK, s.u.b);
+              tma_load_3d(sbase + C::OFF_V + kvs * C::KV_BYTES + kb * BK * 128, &tmV, BAR_KF(kvs),
+                          col0 + kb * 64, s.u.kt * BK, s.u.b);
+            }
+          }
+          const int st = s.t % C::STAGES;
+          if (s.t >= C::STAGES && !mbar_wait(BAR_QE(st), ((s.t / C::STAGES) - 1) & 1, abort_p)) break;
+          const int qt = s.u.kt + s.i;
           mbar_arrive_expect_tx(BAR_QF(st), 2 * C::QD_BYTES);
           for (int kb = 0; kb < C::KB; ++kb) {
             tma_load_3d(sbase + C::OFF_Q + st * C::QD_BYTES + kb * BQ * 128, &tmQ, BAR_QF(st),
-                        col0 + kb * 64, qt * BQ, b);
+                        col0 + kb * 64, qt * BQ, s.u.b);
             tma_load_3d(sbase + C::OFF_DO + st * C::QD_BYTES + kb * BQ * 128, &tmdO, BAR_QF(st),
-                        col0 + kb * 64, qt * BQ, b);
+                        col0 + kb * 64, qt * BQ, s.u.b);
           }
         }
       }
@@ -274,16 +357,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         constexpr uint32_t IDESC_S = idesc_bf16_f32(BK, BQ, 0, 0);   // S^T, dP^T
         constexpr uint32_t IDESC_KV = idesc_bf16_f32(BK, HD, 0, 1);  // dV, dK
         constexpr uint32_t IDESC_Q = idesc_bf16_f32(BQ, HD, 1, 1);   // dQ
-        const uint32_t sk = sbase + C::OFF_K, sv = sbase + C::OFF_V;
         const uint32_t spt = sbase + C::OFF_PT, sdst = sbase + C::OFF_DST;
-        bool ok = mbar_wait(BAR_KV, 0, abort_p);
-        // S^T_i and dP^T_i into their TMEM columns
-        auto issue_s = [&](int i) -> bool {
-          const int st = i % C::STAGES;
-          if (!mbar_wait(BAR_QF(st), (i / C::STAGES) & 1, abort_p)) return false;
-          if (i >= 1 && !mbar_wait(BAR_SE, (i - 1) & 1, abort_p)) return false;
-          if (C::DQ_ALIAS && i >= 1 && !mbar_wait(BAR_DQE, (i - 1) & 1, abort_p)) return false;
+        // S^T and dP^T of step s into their TMEM columns
+        auto issue_s = [&](const StepIter& s) -> bool {
+          const int st = s.t % C::STAGES;
+          const int kvs = s.uc % C::KVB;
+          if (s.i == 0 && !mbar_wait(BAR_KF(kvs), (s.uc / C::KVB) & 1, abort_p)) return false;
+          if (!mbar_wait(BAR_QF(st), (s.t / C::STAGES) & 1, abort_p)) return false;
+          if (s.t >= 1 && !mbar_wait(BAR_SE, (s.t - 1) & 1, abort_p)) return false;
+          if (C::DQ_ALIAS && s.t >= 1 && !mbar_wait(BAR_DQE, (s.t - 1) & 1, abort_p)) return false;
           tc_fence_after();
+          const uint32_t sk = sbase + C::OFF_K + kvs * C::KV_BYTES;
+          const uint32_t sv = sbase + C::OFF_V + kvs * C::KV_BYTES;
           const uint32_t sq = sbase + C::OFF_Q + st * C::QD_BYTES;
           const uint32_t sdo = sbase + C::OFF_DO + st * C::QD_BYTES;
 #pragma unroll
@@ -301,34 +386,47 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           umma_commit(BAR_SF);
           return true;
         };
-        if (ok) ok = issue_s(0);
-        for (int i = 0; ok && i < nq; ++i) {
-          if (C::EARLY_S && i + 1 < nq && !issue_s(i + 1)) break;
-          const int st = i % C::STAGES;
+        StepIter cur = first_step(prm);
+        StepIter la = cur;  // next step whose S^T/dP^T is to be issued
+        bool ok = true;
+        if (la.valid) {
+          ok = issue_s(la);
+          advance(prm, la);
+        }
+        for (; ok && cur.valid; advance(prm, cur)) {
+          if (C::EARLY_S && la.valid) {
+            if (!issue_s(la)) break;
+            advance(prm, la);
+          }
+          const int st = cur.t % C::STAGES;
+          const int kvs = cur.uc % C::KVB;
+          const uint32_t sk = sbase + C::OFF_K + kvs * C::KV_BYTES;
           const uint32_t sq = sbase + C::OFF_Q + st * C::QD_BYTES;
           const uint32_t sdo = sbase + C::OFF_DO + st * C::QD_BYTES;
-          if (!mbar_wait(BAR_PR, i & 1, abort_p)) break;
+          if (!mbar_wait(BAR_PR, cur.t & 1, abort_p)) break;
+          // the previous unit's epilogue must have read dK/dV out of TMEM
+          if (cur.i == 0 && cur.uc >= 1 && !mbar_wait(BAR_ACC, (cur.uc - 1) & 1, abort_p)) break;
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < BQ / 16; ++kk) {  // dV += P^T dO_i
             const uint64_t bd = smem_desc_sw128(sdo + kk * 2048, BQ * 128, 1024);
             if (C::P_IN_TMEM) {
               umma_bf16_ts(tmem + C::TCOL_DV, tmem + C::TCOL_PT + kk * 8, bd, IDESC_KV,
-                           (i > 0 || kk > 0) ? 1u : 0u);
+                           (cur.i > 0 || kk > 0) ? 1u : 0u);
             } else {
               const uint64_t ad = smem_desc_sw128(spt + (kk >> 2) * (BK * 128) + (kk & 3) * 32, 16, 1024);
-              umma_bf16_ss(tmem + C::TCOL_DV, ad, bd, IDESC_KV, (i > 0 || kk > 0) ? 1u : 0u);
+              umma_bf16_ss(tmem + C::TCOL_DV, ad, bd, IDESC_KV, (cur.i > 0 || kk > 0) ? 1u : 0u);
             }
           }
 #pragma unroll
           for (int kk = 0; kk < BQ / 16; ++kk) {  // dK += dS^T Q_i
             const uint64_t ad = smem_desc_sw128(sdst + (kk >> 2) * (BK * 128) + (kk & 3) * 32, 16, 1024);
             const uint64_t bd = smem_desc_sw128(sq + kk * 2048, BQ * 128, 1024);
-            umma_bf16_ss(tmem + C::TCOL_DK, ad, bd, IDESC_KV, (i > 0 || kk > 0) ? 1u : 0u);
+            umma_bf16_ss(tmem + C::TCOL_DK, ad, bd, IDESC_KV, (cur.i > 0 || kk > 0) ? 1u : 0u);
           }
           umma_commit(BAR_QE(st));
-          // the dQ columns must have been drained (dQ_{i-1})
-          if (i >= 1 && !mbar_wait(BAR_DQE, (i - 1) & 1, abort_p)) break;
+          // the dQ columns must have been drained (previous step)
+          if (cur.t >= 1 && !mbar_wait(BAR_DQE, (cur.t - 1) & 1, abort_p)) break;
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {  // dQ_i = dS K (A = dS^T as MN-major)
@@ -338,25 +436,31 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           umma_commit(BAR_DQF);
           umma_commit(BAR_PE);
-          if (!C::EARLY_S && i + 1 < nq && !issue_s(i + 1)) break;
-          if (i + 1 == nq) umma_commit(BAR_DONE);
+          if (cur.i + 1 == cur.u.nq) {  // the unit's last UMMA
+            umma_commit(BAR_KE(kvs));
+            umma_commit(BAR_DONE);
+          }
+          if (!C::EARLY_S && la.valid) {
+            if (!issue_s(la)) break;
+            advance(prm, la);
+          }
         }
       }
     } else if (warp == 2) {
       // ------------------------------------------------------- statistics
-      const long long rbase = (long long)b * prm.T;
-      for (int i = 0; i < nq; ++i) {
-        const int st = i % SSTAGES;
-        if (i >= SSTAGES && !mbar_wait_warp(BAR_TE(st), ((i / SSTAGES) - 1) & 1, abort_p)) break;
-        const int qt = kt + i;
+      for (StepIter s = first_step(prm); s.valid; advance(prm, s)) {
+        const int st = s.t % SSTAGES;
+        if (s.t >= SSTAGES && !mbar_wait_warp(BAR_TE(st), ((s.t / SSTAGES) - 1) & 1, abort_p)) break;
+        const int qt = s.u.kt + s.i;
+        const long long rbase = (long long)s.u.b * prm.T;
         float* stt = stat_base + st * (2 * BQ);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int qi = lane * 4 + u;
+        for (int v = 0; v < 4; ++v) {
+          const int qi = lane * 4 + v;
           const int q = qt * BQ + qi;
           float nl = 0.0f, nd = 0.0f;
           if (q < prm.T) {
-            const long long si = (rbase + q) * prm.NH + h;
+            const long long si = (rbase + q) * prm.NH + s.u.h;
             nl = -__ldg(prm.lse + si) * LOG2E;
             nd = -__bfloat162float(prm.Dv[si]) * prm.scale;
           }
@@ -368,11 +472,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     } else {
       // ------------------------------------------------- dQ reduce issuer
       if (lane == 0) {
-        for (int j = 0; j < nq; ++j) {
-          if (!mbar_wait(BAR_DSF, j & 1, abort_p)) break;
+        for (StepIter s = first_step(prm); s.valid; advance(prm, s)) {
+          if (!mbar_wait(BAR_DSF, s.t & 1, abort_p)) break;
           for (int box = 0; box < HD / 32; ++box)
-            tma_reduce_add_3d(&tmdQ, sbase + C::OFF_DQS + box * (BQ * 128), col0 + box * 32,
-                              (kt + j) * BQ, b);
+            tma_reduce_add_3d(&tmdQ, sbase + C::OFF_DQS + box * (BQ * 128), s.u.h * HD + box * 32,
+                              (s.u.kt + s.i) * BQ, s.u.b);
           bulk_commit();
           bulk_wait_read<0>();  // the staging buffer may be rewritten
           mbar_arrive(BAR_DSE);
@@ -391,11 +495,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const float c = prm.scale_log2, sc = prm.scale;
     bool ok = true;
 
-    // dQ_j: TMEM -> fp32 staging (128-byte swizzle, 32-column boxes); the
-    // reduce issuer (warp 3) sends it to global memory
-    auto drain_dq = [&](int j) {
-      if (ok) ok = mbar_wait_warp(BAR_DQF, j & 1, abort_p);
-      if (ok && j >= 1) ok = mbar_wait_warp(BAR_DSE, (j - 1) & 1, abort_p);
+    // dQ of global step t: TMEM -> fp32 staging (128-byte swizzle, 32-column
+    // boxes); the reduce issuer (warp 3) sends it to global memory
+    auto drain_dq = [&](uint32_t t) {
+      if (ok) ok = mbar_wait_warp(BAR_DQF, t & 1, abort_p);
+      if (ok && t >= 1) ok = mbar_wait_warp(BAR_DSE, (t - 1) & 1, abort_p);
       if (!ok) return;
       tc_fence_after();
       constexpr int CPH = HD / 2;  // columns per half
@@ -419,9 +523,62 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_arrive(BAR_DSF);
     };
 
-    for (int i = 0; ok && i < nq; ++i) {
-      const int ss = i % SSTAGES;
-      ok = mbar_wait_warp(BAR_SF, i & 1, abort_p);
+    // dK/dV of unit v (its UMMAs complete, BAR_DONE phase vuc): TMEM ->
+    // registers; frees the accumulators (BAR_ACC) for the next unit, then
+    // converts to bf16 and stores this thread's row slice straight to global
+    // memory (rows past T are not stored)
+    auto epilogue = [&](const BUnit& v, uint32_t vuc) {
+      if (ok) ok = mbar_wait_warp(BAR_DONE, vuc & 1, abort_p);
+      if (!ok) return;
+      tc_fence_after();
+      constexpr int CPH = HD / 2;
+      uint32_t acc[2][CPH];
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
+        const uint32_t tcol = which == 0 ? C::TCOL_DV : C::TCOL_DK;
+#pragma unroll
+        for (int cc = 0; cc < CPH; cc += 16) {
+          uint32_t r[16];
+          tmem_ld16(tl + tcol + half * CPH + cc, r);
+          tmem_wait_ld_dep(r);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) acc[which][cc + j] = r[j];
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(BAR_ACC);  // the next unit may overwrite dK/dV in TMEM
+      const int key = v.kt * BK + krow;
+      if (key < prm.T) {
+        const long long off = ((long long)v.b * prm.T + key) * prm.N + v.h * HD + half * CPH;
+#pragma unroll
+        for (int which = 0; which < 2; ++which) {
+          uint4* dst = reinterpret_cast<uint4*>((which == 0 ? dV : dK) + off);
+#pragma unroll
+          for (int cc = 0; cc < CPH; cc += 8) {
+            uint4 w;
+            w.x = pack_bf16(__uint_as_float(acc[which][cc + 0]), __uint_as_float(acc[which][cc + 1]));
+            w.y = pack_bf16(__uint_as_float(acc[which][cc + 2]), __uint_as_float(acc[which][cc + 3]));
+            w.z = pack_bf16(__uint_as_float(acc[which][cc + 4]), __uint_as_float(acc[which][cc + 5]));
+            w.w = pack_bf16(__uint_as_float(acc[which][cc + 6]), __uint_as_float(acc[which][cc + 7]));
+            dst[cc / 8] = w;
+          }
+        }
+      }
+    };
+
+    // A unit's last dQ drain and its dK/dV epilogue run after the first step
+    // of the next unit has been handed to the tensor core (or after the last
+    // step of the last unit), so they overlap the next unit's UMMAs.
+    BUnit prev{};
+    uint32_t t = 0, uc = 0;
+    bool have_prev = false;
+    for (StepIter st_it = first_step(prm); ok && st_it.valid; advance(prm, st_it)) {
+      const BUnit& u = st_it.u;
+      const int i = st_it.i;
+      t = st_it.t;
+      uc = st_it.uc;
+      const int ss = t % SSTAGES;
+      ok = mbar_wait_warp(BAR_SF, t & 1, abort_p);
       if (!ok) break;
       tc_fence_after();
       float s[64], dp[64];
@@ -446,16 +603,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       tc_fence_before();
       mbar_arrive(BAR_SE);
-      ok = mbar_wait_warp(BAR_TF(ss), (i / SSTAGES) & 1, abort_p);
+      ok = mbar_wait_warp(BAR_TF(ss), (t / SSTAGES) & 1, abort_p);
       if (!ok) break;
       const float* stt = stat_base + ss * (2 * BQ) + half * 64;
       if (i == 0) p_ds_row<true>(s, dp, stt, stt + BQ, c, sc, krow, half * 64);
       else p_ds_row<false>(s, dp, stt, stt + BQ, c, sc, krow, half * 64);
       mbar_arrive(BAR_TE(ss));
-      // the previous tile's UMMAs must be done with P^T/dS^T (and, when the
-      // dQ staging shares their smem, its reduction must have read it)
-      if (i >= 1) ok = mbar_wait_warp(BAR_PE, (i - 1) & 1, abort_p);
-      if (ok && C::DQS_ALIAS && i >= 1) ok = mbar_wait_warp(BAR_DSE, (i - 1) & 1, abort_p);
+      // the previous step's UMMAs must be done with P^T/dS^T, and when the dQ
+      // staging shares their smem its reduction must have read it
+      if (t >= 1) ok = mbar_wait_warp(BAR_PE, (t - 1) & 1, abort_p);
+      if (ok && C::DQS_ALIAS && t >= 1) ok = mbar_wait_warp(BAR_DSE, (t - 1) & 1, abort_p);
       if (!ok) break;
       if (C::P_IN_TMEM) {
         uint32_t pk[32];
@@ -471,56 +628,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_before();
       mbar_arrive(BAR_PR);
       if (C::EARLY_S) {
-        if (i >= 1) drain_dq(i - 1);
+        if (t >= 1) drain_dq(t - 1);
       } else {
-        drain_dq(i);
+        drain_dq(t);
       }
+      if (i == 0 && have_prev) epilogue(prev, uc - 1);
+      prev = u;
+      have_prev = true;
     }
-    if (C::EARLY_S && ok && nq >= 1) drain_dq(nq - 1);
-
-    // --------------------------------------------------- dK / dV epilogue
-    bool epi = ok && mbar_wait_warp(BAR_DONE, 0, abort_p);
-    // D=128: the last dQ staging (in the P^T/dS^T smem) must have been read
-    if (epi && C::DQS_ALIAS) epi = mbar_wait_warp(BAR_DSE, (nq - 1) & 1, abort_p);
-    if (epi) {
-      tc_fence_after();
-      constexpr int CPH = HD / 2;
-#pragma unroll
-      for (int which = 0; which < 2; ++which) {
-        const uint32_t tcol = which == 0 ? C::TCOL_DV : C::TCOL_DK;
-        uint8_t* stage = gbase + (which == 0 ? C::OFF_EPI_V : C::OFF_EPI_K);
-#pragma unroll
-        for (int cc = 0; cc < CPH; cc += 16) {
-          uint32_t r[16];
-          tmem_ld16(tl + tcol + half * CPH + cc, r);
-          tmem_wait_ld_dep(r);
-          const int col = half * CPH + cc;  // column within the head
-          const int kb = col / 64, ch = (col % 64) / 8;
-          uint8_t* rowp = stage + kb * (BK * 128) + krow * 128;
-          uint4 v0, v1;
-          v0.x = pack_bf16(__uint_as_float(r[0]), __uint_as_float(r[1]));
-          v0.y = pack_bf16(__uint_as_float(r[2]), __uint_as_float(r[3]));
-          v0.z = pack_bf16(__uint_as_float(r[4]), __uint_as_float(r[5]));
-          v0.w = pack_bf16(__uint_as_float(r[6]), __uint_as_float(r[7]));
-          v1.x = pack_bf16(__uint_as_float(r[8]), __uint_as_float(r[9]));
-          v1.y = pack_bf16(__uint_as_float(r[10]), __uint_as_float(r[11]));
-          v1.z = pack_bf16(__uint_as_float(r[12]), __uint_as_float(r[13]));
-          v1.w = pack_bf16(__uint_as_float(r[14]), __uint_as_float(r[15]));
-          *reinterpret_cast<uint4*>(rowp + ((ch ^ (krow & 7)) * 16)) = v0;
-          *reinterpret_cast<uint4*>(rowp + (((ch + 1) ^ (krow & 7)) * 16)) = v1;
-        }
-      }
-      fence_proxy_async_smem();
-    }
-    // one named barrier for the 256 compute threads, reached on every path
-    epi = bar_red_and(1, NCOMP, epi);
-    if (epi && cw == 0 && lane == 0) {
-      for (int kb = 0; kb < C::KB; ++kb) {
-        tma_store_3d(&tmdV, sbase + C::OFF_EPI_V + kb * BK * 128, col0 + kb * 64, kt * BK, b);
-        tma_store_3d(&tmdK, sbase + C::OFF_EPI_K + kb * BK * 128, col0 + kb * 64, kt * BK, b);
-      }
-      bulk_commit();
-      bulk_wait<0>();
+    if (ok && have_prev) {  // the last unit of this CTA
+      if (C::EARLY_S) drain_dq(t);
+      epilogue(prev, uc);
     }
   }
 
@@ -548,32 +666,44 @@ __global__ void zero_dq_shard_kernel(float4* __restrict__ dQ, int T, int N, int 
   }
 }
 
-template <int HD>
-cudaError_t launch_bwd(const __nv_bfloat16* dO, const __nv_bfloat16* Dv, const float* lse,
-                       const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* v,
-                       float* dQ, __nv_bfloat16* dK, __nv_bfloat16* dV, const AttnShape& s,
-                       uint32_t* status, cudaStream_t st) {
-  using C = BwdCfg<HD>;
+template <int HD, bool PERSIST>
+cudaError_t launch_bwd_kernel(const __nv_bfloat16* dO, const __nv_bfloat16* q,
+                              const __nv_bfloat16* k, const __nv_bfloat16* v, float* dQ,
+                              __nv_bfloat16* dK, __nv_bfloat16* dV, const AttnShape& s,
+                              const BwdParams& prm, int grid, cudaStream_t st) {
+  using C = BwdCfg<HD, PERSIST>;
   // The setmaxnreg split assumes the kernel was compiled to exactly
   // LAUNCH_REGS registers per thread; refuse to launch otherwise.
   static const cudaError_t reg_check = [] {
     cudaFuncAttributes a;
-    cudaError_t e = cudaFuncGetAttributes(&a, flash_bwd_kernel<HD>);
+    cudaError_t e = cudaFuncGetAttributes(&a, flash_bwd_kernel<HD, PERSIST>);
     if (e != cudaSuccess) return e;
     return a.numRegs == LAUNCH_REGS ? cudaSuccess : cudaErrorInvalidKernelImage;
   }();
   if (reg_check != cudaSuccess) return reg_check;
-  CUtensorMap tq, tk, tv, tdo, tdq, tdk, tdv;
+  CUtensorMap tq, tk, tv, tdo, tdq;
   const CUtensorMapDataType bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B;
   if (!make_tmap_3d(&tq, q, bf, 2, s.N, s.T, s.B, 64, BQ, sw) ||
       !make_tmap_3d(&tk, k, bf, 2, s.N, s.T, s.B, 64, BK, sw) ||
       !make_tmap_3d(&tv, v, bf, 2, s.N, s.T, s.B, 64, BK, sw) ||
       !make_tmap_3d(&tdo, dO, bf, 2, s.N, s.T, s.B, 64, BQ, sw) ||
-      !make_tmap_3d(&tdq, dQ, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, s.N, s.T, s.B, 32, BQ, sw) ||
-      !make_tmap_3d(&tdk, dK, bf, 2, s.N, s.T, s.B, 64, BK, sw) ||
-      !make_tmap_3d(&tdv, dV, bf, 2, s.N, s.T, s.B, 64, BK, sw))
+      !make_tmap_3d(&tdq, dQ, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, s.N, s.T, s.B, 32, BQ, sw))
     return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(flash_bwd_kernel<HD, PERSIST>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+  if (e != cudaSuccess) return e;
+  flash_bwd_kernel<HD, PERSIST><<<grid, NUM_THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, tdo, tdq, dK,
+                                                                        dV, prm);
+  count_launches(1);
+  return cudaGetLastError();
+}
+
+template <int HD>
+cudaError_t launch_bwd(const __nv_bfloat16* dO, const __nv_bfloat16* Dv, const float* lse,
+                       const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* v,
+                       float* dQ, __nv_bfloat16* dK, __nv_bfloat16* dV, const AttnShape& s,
+                       uint32_t* status, cudaStream_t st) {
   // dQ is accumulated by bulk reductions: zero the shard's columns first
   const int nbh = s.bh_end - s.bh_begin;
   cudaError_t e;
@@ -593,19 +723,21 @@ cudaError_t launch_bwd(const __nv_bfloat16* dO, const __nv_bfloat16* Dv, const f
   prm.bh_begin = s.bh_begin;
   prm.nbh = nbh;
   prm.nkt = (s.T + BK - 1) / BK;
+  prm.nunits = prm.nkt * nbh;
   prm.scale = 1.0f / sqrtf((float)HD);
   prm.scale_log2 = LOG2E / sqrtf((float)HD);
   prm.lse = lse;
   prm.Dv = Dv;
   prm.status = status;
-  e = cudaFuncSetAttribute(flash_bwd_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           C::SMEM_BYTES);
-  if (e != cudaSuccess) return e;
-  const long long nblocks = (long long)prm.nkt * nbh;
-  flash_bwd_kernel<HD><<<(unsigned)nblocks, NUM_THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, tdo, tdq,
-                                                                            tdk, tdv, prm);
-  count_launches(1);
-  return cudaGetLastError();
+  // persistent (one CTA per SM) for short sequences at D=64, else one unit per CTA
+  if (HD == 64 && prm.nkt <= PERSIST_MAX_NKT) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int grid = prm.nunits < sms ? prm.nunits : sms;
+    return launch_bwd_kernel<HD, true>(dO, q, k, v, dQ, dK, dV, s, prm, grid, st);
+  }
+  return launch_bwd_kernel<HD, false>(dO, q, k, v, dQ, dK, dV, s, prm, prm.nunits, st);
 }
 
 }  // namespace
