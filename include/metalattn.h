@@ -119,6 +119,31 @@ MA_API int ma_flashAttentionBackward_shard(const ma_bf16* dZ, const ma_bf16* d, 
                                     const AttentionParams* p, uint32_t B, uint32_t bh_begin,
                                     uint32_t bh_end, ma_stream_t stream);
 
+/* Allocation-free backward pass: computeD followed by flashAttentionBackward,
+ * for callers that cannot let a library allocate device memory (hosts whose
+ * own arena or caching allocator owns all of the GPU's memory, processes under
+ * a fixed device-memory budget, loops that must not take the implicit device
+ * synchronisation of cudaMalloc/cudaFree).  It takes the attention output O
+ * instead of D and writes the same dQ, dK, dV as ma_computeD +
+ * ma_flashAttentionBackward.  D and a status word live in a scratch array
+ * compiled into the library (about 4 MiB, held by every GPU that loads it
+ * until the process exits); it calls no cudaMalloc or cudaFree.
+ *   - B*M*NH must not exceed MA_NOALLOC_MAX_D_ENTRIES, else MA_ERR_LIMIT.
+ *   - The first call on a device looks the scratch's device address up (and
+ *     may load the library's device code); make that first call before any
+ *     stream capture.
+ *   - All calls on a device share the scratch: calls that overlap on the GPU
+ *     (other streams, other host threads) race and give wrong results.
+ *   - A bounded wait that runs out in its kernels is recorded only in the
+ *     scratch (cleared by the next call), not in ma_device_status.
+ * No counterpart in the reference. */
+#define MA_NOALLOC_MAX_D_ENTRIES (1u << 21)
+MA_API int ma_flashAttentionBackward_noalloc(const ma_bf16* dZ, const ma_bf16* O, const float* l,
+                                             const ma_bf16* q, const ma_bf16* k, const ma_bf16* v,
+                                             float* dQ, ma_bf16* dK, ma_bf16* dV,
+                                             const AttentionParams* p, uint32_t B,
+                                             ma_stream_t stream);
+
 /* Text for the last MA_ERR_* returned on the calling host thread ("" if none).
  * Replaces the reference's printed command-buffer error (model.h:361-365). */
 MA_API const char* ma_last_error_string(void);

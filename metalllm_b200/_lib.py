@@ -49,6 +49,7 @@ SIGNATURES = {
     "ma_flashAttentionForward_shard": [_P, _P, _P, _P, _P, _PP, _U32, _U32, _U32, _P],
     "ma_computeD_shard": [_P, _P, _P, _PP, _U32, _U32, _U32, _P],
     "ma_flashAttentionBackward_shard": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _PP, _U32, _U32, _U32, _P],
+    "ma_flashAttentionBackward_noalloc": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _PP, _U32, _P],
     "ma_device_status": [ctypes.POINTER(ctypes.c_uint32), _P],
     "ma_version": [],
 }

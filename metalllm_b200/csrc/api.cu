@@ -277,3 +277,96 @@ uint64_t ma_kernel_launch_count(void) { return g_launches.load(std::memory_order
 int ma_version(void) { return 100; }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free backward pass.
+//
+// Some callers cannot let a library allocate device memory: hosts that hand
+// all of a GPU's memory to their own arena or caching allocator at start-up
+// (so a cudaMalloc outside it fails or fragments the arena), processes run
+// under a fixed device-memory budget, and latency-critical loops that must not
+// take the implicit device-wide synchronisation cudaMalloc/cudaFree can cause.
+// The entry points above allocate a 4-byte status word on their first call on
+// each device, and the backward pass needs the caller to allocate the D
+// buffer between computeD and flashAttentionBackward.
+// ma_flashAttentionBackward_noalloc needs neither: its scratch (the D values
+// and a status word) lives in the file-scope array below, which every GPU that
+// loads the library holds until the process exits.
+namespace {
+
+constexpr size_t kNoallocHeaderBytes = 256;  // status word, padded to keep D 256-byte aligned
+constexpr size_t kNoallocScratchBytes = kNoallocHeaderBytes + (size_t)MA_NOALLOC_MAX_D_ENTRIES * 2;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocScratchBytes];
+
+// In host code g_noalloc_scratch names a host-side stand-in, not device
+// memory: kernels get the device address looked up here, once per device.
+void* g_noalloc_base[kMaxDevices] = {};
+std::mutex g_noalloc_mu;
+
+int noalloc_scratch(void** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(MA_ERR_NO_DEVICE, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_base[dev]) {
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    if (major != 10 || minor != 0)
+      return fail(MA_ERR_NO_DEVICE, "device %d is sm_%d%d; libmetalattn is built for sm_100a only", dev,
+                  major, minor);
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
+    g_noalloc_base[dev] = p;
+  }
+  *out = g_noalloc_base[dev];
+  return MA_OK;
+}
+
+}  // namespace
+
+extern "C" int ma_flashAttentionBackward_noalloc(const ma_bf16* dZ, const ma_bf16* O,
+                                                 const float* l, const ma_bf16* q,
+                                                 const ma_bf16* k, const ma_bf16* v, float* dQ,
+                                                 ma_bf16* dK, ma_bf16* dV,
+                                                 const AttentionParams* p, uint32_t B,
+                                                 ma_stream_t stream) {
+  ma::AttnShape s;
+  int rc = check_shape(p, B, 0, 0, false, &s);
+  if (rc) return rc;
+  MA_REQUIRE_PTR(dZ);
+  MA_REQUIRE_PTR(O);
+  MA_REQUIRE_PTR(l);
+  MA_REQUIRE_PTR(q);
+  MA_REQUIRE_PTR(k);
+  MA_REQUIRE_PTR(v);
+  MA_REQUIRE_PTR(dQ);
+  MA_REQUIRE_PTR(dK);
+  MA_REQUIRE_PTR(dV);
+  const uint64_t entries = (uint64_t)B * p->M * p->NH;
+  if (entries > MA_NOALLOC_MAX_D_ENTRIES)
+    return fail(MA_ERR_LIMIT,
+                "ma_flashAttentionBackward_noalloc: B*M*NH = %llu exceeds the scratch maximum of %u "
+                "(row, head) entries; use ma_computeD + ma_flashAttentionBackward",
+                (unsigned long long)entries, (unsigned)MA_NOALLOC_MAX_D_ENTRIES);
+  void* base = nullptr;
+  rc = noalloc_scratch(&base);
+  if (rc) return rc;
+  uint32_t* status = static_cast<uint32_t*>(base);
+  __nv_bfloat16* Dv = reinterpret_cast<__nv_bfloat16*>(static_cast<unsigned char*>(base) + kNoallocHeaderBytes);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // The scratch keeps the previous call's contents: the status word must
+  // start at zero; D is overwritten in full by computeD below.
+  cudaError_t e = cudaMemsetAsync(status, 0, sizeof(uint32_t), st);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(no-alloc status word)");
+  e = ma::launch_compute_d(reinterpret_cast<bf16p>(dZ), reinterpret_cast<bf16p>(O), Dv, s, st);
+  if (e != cudaSuccess) return cuda_fail(e, "computeD launch (no-alloc)");
+  e = ma::launch_flash_bwd(reinterpret_cast<bf16p>(dZ), Dv, l, reinterpret_cast<bf16p>(q),
+                           reinterpret_cast<bf16p>(k), reinterpret_cast<bf16p>(v), dQ,
+                           reinterpret_cast<bf16m>(dK), reinterpret_cast<bf16m>(dV), s, status, st);
+  if (e != cudaSuccess) return cuda_fail(e, "flashAttentionBackward launch (no-alloc)");
+  return ok();
+}
