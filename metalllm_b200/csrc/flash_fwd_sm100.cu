@@ -31,6 +31,8 @@
 // Every mbarrier wait is bounded (about 2 s); on time-out the CTA sets an
 // abort flag that all roles poll, winds down, frees its TMEM and sets
 // STATUS_FWD_TIMEOUT in the device status word.
+#include <type_traits>
+
 #include "common.cuh"
 #include "sm100.cuh"
 #include "tmap.h"
@@ -56,21 +58,27 @@ template <int HD>
 struct FwdCfg {
   static constexpr int KB = HD / 64;  // 64-column blocks per row
   static constexpr int QST = HD == 64 ? 2 : 1;  // Q-pair stages
-  static constexpr int KST = 2;                 // K tile stages
-  static constexpr int VST = HD == 64 ? 2 : 1;  // V tile stages
+  static constexpr int KST = HD == 64 ? 3 : 2;  // K tile stages
+  static constexpr int VST = HD == 64 ? 3 : 1;  // V tile stages
   // UMMA issue order: D=64 issues S_X(j+1) before PV_X(j) (softmax-bound: the
   // next scores should be ready early); D=128 interleaves PV_X(j), S_X(j+1)
   // (tensor-bound: keeps PV close to its P)
   static constexpr bool EARLY_S = HD == 64;
+  // D=64: P_X lives in TMEM (bf16 pairs) and PV_X reads it from there, which
+  // halves the shared-memory traffic of the tensor core; D=128 has no TMEM
+  // columns left and stages P in shared memory
+  static constexpr bool P_TMEM = HD == 64;
   static constexpr uint32_t QT_BYTES = BM * HD * 2;  // one query tile
   static constexpr uint32_t KV_BYTES = BN * HD * 2;
   static constexpr uint32_t P_BYTES = BM * BN * 2;
+  // per tile X: P (shared-memory P) or only the epilogue's O staging
+  static constexpr uint32_t STG_BYTES = P_TMEM ? BM * HD * 2 : P_BYTES;
   // shared memory map (offsets from a 1024-aligned base)
   static constexpr uint32_t OFF_Q = 0;                          // [QST][2 tiles]
   static constexpr uint32_t OFF_K = OFF_Q + QST * 2 * QT_BYTES;  // [KST]
   static constexpr uint32_t OFF_V = OFF_K + KST * KV_BYTES;      // [VST]
-  static constexpr uint32_t OFF_P = OFF_V + VST * KV_BYTES;      // [2 tiles]
-  static constexpr uint32_t OFF_BAR = OFF_P + 2 * P_BYTES;
+  static constexpr uint32_t OFF_P = OFF_V + VST * KV_BYTES;      // [2 tiles] P / O staging
+  static constexpr uint32_t OFF_BAR = OFF_P + 2 * STG_BYTES;
   // q_full/empty[QST], k_full/empty[KST], v_full/empty[VST], per tile X:
   // s_full, s_free, p_full, pv_done, o_free
   static constexpr int NBAR = 2 * QST + 2 * KST + 2 * VST + 2 * 5;
@@ -78,6 +86,9 @@ struct FwdCfg {
   static constexpr uint32_t SMEM_BYTES = OFF_TSLOT + 16 + 1024;  // + alignment slack
   static constexpr uint32_t TCOL_S = 0;     // S_A, S_B at columns 0, 128
   static constexpr uint32_t TCOL_O = 256;   // O_A, O_B at 256, 256+HD
+  static constexpr uint32_t TCOL_P = 256 + 2 * HD;  // P_A, P_B (D=64): 64 columns each
+  static_assert(!P_TMEM || TCOL_P + 2 * (BN / 2) <= 512, "TMEM columns");
+  static_assert(OFF_BAR + NBAR * 8 + 16 + 1024 <= 232448, "shared memory");
 };
 
 struct FwdParams {
@@ -252,13 +263,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (!mbar_wait(BAR_PF(x), pvc[x] & 1, abort_p)) return false;
           if (j == 0 && uc[x] >= 1 && !mbar_wait(BAR_OE(x), (uc[x] - 1) & 1, abort_p)) return false;
           tc_fence_after();
-          const uint32_t sp = sbase + C::OFF_P + x * C::P_BYTES;
+          const uint32_t sp = sbase + C::OFF_P + x * C::STG_BYTES;
           const uint32_t sv = sbase + C::OFF_V + ((vc + j) % C::VST) * C::KV_BYTES;
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk) {
-            const uint64_t ad = smem_desc_sw128(sp + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
             const uint64_t bd = smem_desc_sw128(sv + kk * 2048, BN * 128, 1024);
-            umma_bf16_ss(tmem + C::TCOL_O + x * HD, ad, bd, IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
+            if (C::P_TMEM) {  // A = P_X from TMEM: 8 columns per 16 keys
+              umma_bf16_ts(tmem + C::TCOL_O + x * HD, tmem + C::TCOL_P + x * (BN / 2) + kk * 8, bd,
+                           IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
+            } else {
+              const uint64_t ad = smem_desc_sw128(sp + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
+              umma_bf16_ss(tmem + C::TCOL_O + x * HD, ad, bd, IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
+            }
           }
           umma_commit(BAR_PV(x));
           ++pvc[x];
@@ -323,7 +339,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const uint32_t tcol_s = C::TCOL_S + x * BN, tcol_o = C::TCOL_O + x * HD;
     const float c = prm.scale_log2;
     const bool wg_leader = (warp == 4 + 4 * x) && lane == 0;
-    uint8_t* pbuf = gbase + C::OFF_P + x * C::P_BYTES;
+    uint8_t* pbuf = gbase + C::OFF_P + x * C::STG_BYTES;
     uint32_t sc = 0;  // S_X consumed so far (== P_X produced)
     bool ok = true;
     for (int g = 0; ok; ++g) {
@@ -337,8 +353,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (sc >= 1 && wg_leader) bulk_wait_read<0>();
       bar_sync_named(wg_bar, 128);
       float m_used = -INFINITY, l_sum = 0.0f;
-      for (int j = 0; ok && j < nt; ++j) {
-        if (!mbar_wait_warp(BAR_SF(x), sc & 1, abort_p)) { ok = false; break; }
+      // one key tile; DIAG: the diagonal tile (keys after the query masked).
+      // Instantiated twice so that the other tiles carry no masking code.
+      auto tile = [&](auto diag_tag, int j) -> bool {
+        constexpr bool DIAG = decltype(diag_tag)::value;
+        if (!mbar_wait_warp(BAR_SF(x), sc & 1, abort_p)) return false;
         tc_fence_after();
         float s[BN];
 #pragma unroll
@@ -355,7 +374,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         tc_fence_before();
         mbar_arrive(BAR_SE(x));
-        if (j == qtile) {  // diagonal tile: mask keys after the query
+        if constexpr (DIAG) {
 #pragma unroll
           for (int i = 0; i < BN; ++i)
             if (i > row) s[i] = -INFINITY;
@@ -371,63 +390,82 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const float mx = fmax3(fmax3(pm[0], pm[1], pm[2]), fmax3(pm[3], pm[4], pm[5]),
                                fmaxf(pm[6], pm[7]));
         const float m_new = fmaxf(m_used, mx * c);
-        // PV_X(j-1) must be complete before P_X(j) overwrites the P buffer and
-        // before O_X is rescaled
-        if (j >= 1 && !mbar_wait_warp(BAR_PV(x), (sc - 1) & 1, abort_p)) { ok = false; break; }
+        // lazy rescaling: only rows whose maximum grew by more than 2^8 move
+        // m_used; O_X is rescaled below, once PV_X(j-1) has completed
+        bool rescale = false;
+        float alpha = 1.0f;
         if (j == 0) {
           m_used = m_new;
         } else {
           const bool need = m_new > m_used + RESCALE_THRESHOLD;
-          if (__any_sync(0xffffffffu, need)) {
-            const float alpha = need ? ex2(m_used - m_new) : 1.0f;
-            if (need) {
-              l_sum *= alpha;
-              m_used = m_new;
-            }
-            tc_fence_after();
-#pragma unroll
-            for (int cc = 0; cc < HD; cc += 16) {
-              uint32_t r[16];
-              tmem_ld16(trow + tcol_o + cc, r);
-              tmem_wait_ld_dep(r);
-#pragma unroll
-              for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-              tmem_st16(trow + tcol_o + cc, r);
-            }
-            tmem_wait_st();
+          rescale = __any_sync(0xffffffffu, need);
+          if (need) {
+            alpha = ex2(m_used - m_new);
+            l_sum *= alpha;
+            m_used = m_new;
           }
         }
         // P = 2^(S*c - m) with packed fp32x2 FMAs; row sum in 4 packed partials
         const float2 c2 = make_float2(c, c), nm2 = make_float2(-m_used, -m_used);
         float2 ps[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                         make_float2(0.f, 0.f)};
+        uint32_t pk[BN / 2];  // P as bf16 pairs, even key in the low half
 #pragma unroll
         for (int i = 0; i < BN; i += 2) {
           const float2 t = __ffma2_rn(make_float2(s[i], s[i + 1]), c2, nm2);
-          s[i] = ex2(t.x);
-          s[i + 1] = ex2(t.y);
-          ps[(i >> 1) & 3] = __fadd2_rn(ps[(i >> 1) & 3], make_float2(s[i], s[i + 1]));
+          const float e0 = ex2(t.x), e1 = ex2(t.y);
+          ps[(i >> 1) & 3] = __fadd2_rn(ps[(i >> 1) & 3], make_float2(e0, e1));
+          pk[i / 2] = pack_bf16(e0, e1);
         }
         l_sum += (ps[0].x + ps[0].y) + (ps[1].x + ps[1].y) + (ps[2].x + ps[2].y) +
                  (ps[3].x + ps[3].y);
-#pragma unroll
-        for (int kb = 0; kb < BN / 64; ++kb) {
-#pragma unroll
-          for (int ch = 0; ch < 8; ++ch) {
-            const int c0 = kb * 64 + ch * 8;
-            uint4 v;
-            v.x = pack_bf16(s[c0 + 0], s[c0 + 1]);
-            v.y = pack_bf16(s[c0 + 2], s[c0 + 3]);
-            v.z = pack_bf16(s[c0 + 4], s[c0 + 5]);
-            v.w = pack_bf16(s[c0 + 6], s[c0 + 7]);
-            *reinterpret_cast<uint4*>(pbuf + kb * (BM * 128) + row * 128 + ((ch ^ (row & 7)) * 16)) = v;
-          }
+        // PV_X(j-1) must be complete before O_X is rescaled and before P_X(j)
+        // overwrites P_X (waited for only now, so the exponentials overlap it)
+        if (j >= 1) {
+          if (!mbar_wait_warp(BAR_PV(x), (sc - 1) & 1, abort_p)) return false;
+          tc_fence_after();
         }
-        fence_proxy_async_smem();
+        if (rescale) {
+#pragma unroll
+          for (int cc = 0; cc < HD; cc += 16) {
+            uint32_t r[16];
+            tmem_ld16(trow + tcol_o + cc, r);
+            tmem_wait_ld_dep(r);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+            tmem_st16(trow + tcol_o + cc, r);
+          }
+          tmem_wait_st();
+        }
+        if constexpr (C::P_TMEM) {
+          // this lane's P row into P_X
+#pragma unroll
+          for (int q = 0; q < BN / 32; ++q) {
+            uint32_t r[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) r[i] = pk[q * 16 + i];
+            tmem_st16(trow + C::TCOL_P + x * (BN / 2) + q * 16, r);
+          }
+          tmem_wait_st();
+        } else {
+#pragma unroll
+          for (int kb = 0; kb < BN / 64; ++kb) {
+#pragma unroll
+            for (int ch = 0; ch < 8; ++ch) {
+              const int c0 = (kb * 64 + ch * 8) / 2;
+              const uint4 v = make_uint4(pk[c0], pk[c0 + 1], pk[c0 + 2], pk[c0 + 3]);
+              *reinterpret_cast<uint4*>(pbuf + kb * (BM * 128) + row * 128 + ((ch ^ (row & 7)) * 16)) = v;
+            }
+          }
+          fence_proxy_async_smem();
+        }
         tc_fence_before();
         mbar_arrive(BAR_PF(x));
         ++sc;
-      }
+        return true;
+      };
+      for (int j = 0; ok && j < nt; ++j)
+        ok = (j == qtile) ? tile(std::true_type{}, j) : tile(std::false_type{}, j);
       // --------------------------------------------- epilogue of tile X
       const bool epi = ok && mbar_wait_warp(BAR_PV(x), (sc - 1) & 1, abort_p);
       if (epi) {
@@ -465,7 +503,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       ok = bar_red_and(wg_bar, 128, epi);
       if (ok && wg_leader) {
         for (int kb = 0; kb < C::KB; ++kb)
-          tma_store_3d(&tmO, sbase + C::OFF_P + x * C::P_BYTES + kb * BM * 128, un.h * HD + kb * 64,
+          tma_store_3d(&tmO, sbase + C::OFF_P + x * C::STG_BYTES + kb * BM * 128, un.h * HD + kb * 64,
                        qtile * BM, un.b);
         bulk_commit();
       }
