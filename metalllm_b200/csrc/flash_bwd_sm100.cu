@@ -70,13 +70,7 @@ using namespace sm100;
 
 constexpr int BK = 128;  // keys per unit
 constexpr int BQ = 128;  // queries per step
-constexpr int NUM_THREADS = 384;
 constexpr int NCOMP = 256;  // compute threads (warpgroups 1 and 2)
-constexpr int LAUNCH_REGS = 168;    // 65536 / 384, rounded down to a multiple of 8
-constexpr int REGS_PRODUCER = 120;  // warpgroup 0 after setmaxnreg.dec
-constexpr int REGS_COMPUTE = 192;   // warpgroups 1, 2 after setmaxnreg.inc
-static_assert(128 * REGS_PRODUCER + 256 * REGS_COMPUTE == NUM_THREADS * LAUNCH_REGS,
-              "register split must equal the launch allocation");
 constexpr int SSTAGES = 8;  // statistics stages
 constexpr int PERSIST_MAX_NKT = 16;  // persistent launch when T/128 <= this (D=64)
 constexpr float LOG2E = 1.4426950408889634f;
@@ -85,6 +79,20 @@ template <int HD, bool PERSIST>
 struct BwdCfg {
   static constexpr int KB = HD / 64;
   static constexpr bool D64 = HD == 64;
+  // D=64: a fourth warpgroup drains dQ and stores dK/dV, so the compute
+  // warpgroups only form P^T and dS^T.  Register split per thread after
+  // setmaxnreg: warpgroup 0 80, compute 184, drain 64; without
+  // it (D=128, 384 threads): warpgroup 0 120, compute 192.
+  static constexpr bool DRAIN_WG = D64;
+  static constexpr int NUM_THREADS = DRAIN_WG ? 512 : 384;
+  static constexpr int LAUNCH_REGS = DRAIN_WG ? 128 : 168;  // 65536 / threads, multiple of 8
+  static constexpr int REGS_PRODUCER = DRAIN_WG ? 80 : 120;
+  static constexpr int REGS_COMPUTE = DRAIN_WG ? 184 : 192;
+  static constexpr int REGS_DRAIN = DRAIN_WG ? 64 : 0;
+  static constexpr int NDRAIN = DRAIN_WG ? 128 : NCOMP;  // arrivals on DQE, DSF, ACC
+  static_assert(128 * REGS_PRODUCER + 256 * REGS_COMPUTE + 128 * REGS_DRAIN ==
+                    NUM_THREADS * LAUNCH_REGS,
+                "register split must equal the launch allocation");
   // Q_i/dO_i stages and K/V buffers: a persistent CTA double-buffers K/V to
   // prefetch the next unit; otherwise the smem goes to a deeper Q/dO ring
   static constexpr int STAGES = D64 ? (PERSIST ? 2 : 3) : 1;
@@ -250,7 +258,7 @@ __device__ __forceinline__ void store_row_sw128(uint8_t* rowp, int row, const fl
 }
 
 template <int HD, bool PERSIST>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+__global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
     flash_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
                      const __grid_constant__ CUtensorMap tmdQ, __nv_bfloat16* __restrict__ dK,
@@ -302,11 +310,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     mbar_init(BAR_PR, NCOMP);
     mbar_init(BAR_PE, 1);
     mbar_init(BAR_DQF, 1);
-    mbar_init(BAR_DQE, NCOMP);
-    mbar_init(BAR_DSF, NCOMP);
+    mbar_init(BAR_DQE, C::NDRAIN);
+    mbar_init(BAR_DSF, C::NDRAIN);
     mbar_init(BAR_DSE, 1);
     mbar_init(BAR_DONE, 1);
-    mbar_init(BAR_ACC, NCOMP);
+    mbar_init(BAR_ACC, C::NDRAIN);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -320,7 +328,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   volatile int* abort_p = &abort_flag;
 
   if (warp < 4) {
-    reg_dealloc<REGS_PRODUCER>();
+    reg_dealloc<C::REGS_PRODUCER>();
     if (warp == 0) {
       // --------------------------------------------------------- producer
       if (lane == 0) {
@@ -484,8 +492,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         bulk_wait<0>();
       }
     }
-  } else {
-    reg_alloc<REGS_COMPUTE>();
+  } else if (!C::DRAIN_WG || warp < 12) {
+    reg_alloc<C::REGS_COMPUTE>();
     // ------------------------------------------------------------ compute
     const int cw = warp - 4;                   // 0..7
     const int quarter = warp & 3;              // TMEM lane quarter
@@ -627,18 +635,93 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(BAR_PR);
-      if (C::EARLY_S) {
-        if (t >= 1) drain_dq(t - 1);
-      } else {
-        drain_dq(t);
+      if constexpr (!C::DRAIN_WG) {
+        if (C::EARLY_S) {
+          if (t >= 1) drain_dq(t - 1);
+        } else {
+          drain_dq(t);
+        }
+        if (i == 0 && have_prev) epilogue(prev, uc - 1);
+        prev = u;
+        have_prev = true;
       }
-      if (i == 0 && have_prev) epilogue(prev, uc - 1);
-      prev = u;
-      have_prev = true;
     }
-    if (ok && have_prev) {  // the last unit of this CTA
-      if (C::EARLY_S) drain_dq(t);
-      epilogue(prev, uc);
+    if constexpr (!C::DRAIN_WG) {
+      if (ok && have_prev) {  // the last unit of this CTA
+        if (C::EARLY_S) drain_dq(t);
+        epilogue(prev, uc);
+      }
+    }
+  } else {
+    reg_dealloc<C::REGS_DRAIN>();
+    // ------------------------------------------- dQ drain, dK/dV epilogue
+    // (D=64, warps 12-15): thread = TMEM lane = dQ query row = key row
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t tl = tmem + ((uint32_t)(quarter * 32) << 16);
+    uint8_t* dqs = gbase + C::OFF_DQS;
+    bool ok = true;
+    for (StepIter s = first_step(prm); ok && s.valid; advance(prm, s)) {
+      const uint32_t t = s.t;
+      // dQ of step t: TMEM -> fp32 staging (128-byte swizzle, 32-column
+      // boxes); the reduce issuer (warp 3) adds it into global dQ
+      ok = mbar_wait_warp(BAR_DQF, t & 1, abort_p);
+      if (ok && t >= 1) ok = mbar_wait_warp(BAR_DSE, (t - 1) & 1, abort_p);
+      if (!ok) break;
+      tc_fence_after();
+#pragma unroll
+      for (int cc = 0; cc < HD; cc += 16) {
+        uint32_t r[16];
+        tmem_ld16(tl + C::TCOL_DQ + cc, r);
+        tmem_wait_ld_dep(r);
+        uint8_t* rowp = dqs + (cc / 32) * (BQ * 128) + row * 128;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int ch = (cc % 32) / 4 + q;
+          const uint4 v = make_uint4(r[q * 4 + 0], r[q * 4 + 1], r[q * 4 + 2], r[q * 4 + 3]);
+          *reinterpret_cast<uint4*>(rowp + ((ch ^ (row & 7)) * 16)) = v;
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(BAR_DQE);
+      fence_proxy_async_smem();
+      mbar_arrive(BAR_DSF);
+      if (s.i + 1 == s.u.nq) {
+        // the unit's dK/dV (all its UMMAs complete): TMEM -> bf16 -> this
+        // key row's slices in global memory (rows past T are not stored),
+        // then the accumulators are released to the next unit
+        ok = mbar_wait_warp(BAR_DONE, s.uc & 1, abort_p);
+        if (!ok) break;
+        tc_fence_after();
+        const int key = s.u.kt * BK + row;
+        const long long off = ((long long)s.u.b * prm.T + key) * prm.N + s.u.h * HD;
+#pragma unroll
+        for (int which = 0; which < 2; ++which) {
+          uint4* dst = reinterpret_cast<uint4*>((which == 0 ? dV : dK) + off);
+          const uint32_t tcol = which == 0 ? C::TCOL_DV : C::TCOL_DK;
+#pragma unroll
+          for (int cc = 0; cc < HD; cc += 16) {
+            uint32_t r[16];
+            tmem_ld16(tl + tcol + cc, r);
+            tmem_wait_ld_dep(r);
+            if (key < prm.T) {
+              uint4 w0, w1;
+              w0.x = pack_bf16(__uint_as_float(r[0]), __uint_as_float(r[1]));
+              w0.y = pack_bf16(__uint_as_float(r[2]), __uint_as_float(r[3]));
+              w0.z = pack_bf16(__uint_as_float(r[4]), __uint_as_float(r[5]));
+              w0.w = pack_bf16(__uint_as_float(r[6]), __uint_as_float(r[7]));
+              w1.x = pack_bf16(__uint_as_float(r[8]), __uint_as_float(r[9]));
+              w1.y = pack_bf16(__uint_as_float(r[10]), __uint_as_float(r[11]));
+              w1.z = pack_bf16(__uint_as_float(r[12]), __uint_as_float(r[13]));
+              w1.w = pack_bf16(__uint_as_float(r[14]), __uint_as_float(r[15]));
+              dst[cc / 8] = w0;
+              dst[cc / 8 + 1] = w1;
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(BAR_ACC);
+      }
     }
   }
 
@@ -678,7 +761,7 @@ cudaError_t launch_bwd_kernel(const __nv_bfloat16* dO, const __nv_bfloat16* q,
     cudaFuncAttributes a;
     cudaError_t e = cudaFuncGetAttributes(&a, flash_bwd_kernel<HD, PERSIST>);
     if (e != cudaSuccess) return e;
-    return a.numRegs == LAUNCH_REGS ? cudaSuccess : cudaErrorInvalidKernelImage;
+    return a.numRegs == C::LAUNCH_REGS ? cudaSuccess : cudaErrorInvalidKernelImage;
   }();
   if (reg_check != cudaSuccess) return reg_check;
   CUtensorMap tq, tk, tv, tdo, tdq;
@@ -693,7 +776,7 @@ cudaError_t launch_bwd_kernel(const __nv_bfloat16* dO, const __nv_bfloat16* q,
   cudaError_t e = cudaFuncSetAttribute(flash_bwd_kernel<HD, PERSIST>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
   if (e != cudaSuccess) return e;
-  flash_bwd_kernel<HD, PERSIST><<<grid, NUM_THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, tdo, tdq, dK,
+  flash_bwd_kernel<HD, PERSIST><<<grid, C::NUM_THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, tdo, tdq, dK,
                                                                         dV, prm);
   count_launches(1);
   return cudaGetLastError();
