@@ -21,9 +21,11 @@
  *   - Outputs are written, never accumulated: callers need not pre-zero
  *     dQ/dK/dV or Q/K/V (a caller that does, as model.h:418-424 and
  *     model.h:549-551 do, gets identical results).
- *   - Supported shapes: D in {64, 128}; M a multiple of 64 (the reference's
- *     own requirement, attention.metal:74); N == NH*D; B >= 1.  Anything else
- *     returns MA_ERR_SHAPE and computes nothing.
+ *   - Supported shapes: D in {64, 128}; any M >= 1 (the reference needs a
+ *     multiple of 64, attention.metal:74; partial tiles are zero-filled on
+ *     load and clipped on store here); N == NH*D; B >= 1.  computeQKV needs
+ *     N a multiple of 64.  Anything else returns MA_ERR_SHAPE and computes
+ *     nothing.
  *   - The library allocates nothing per call on the device except a cached
  *     4-byte error word per device.
  */

@@ -87,8 +87,6 @@ int check_shape(const AttentionParams* p, uint32_t B, uint32_t bh_begin, uint32_
     return fail(MA_ERR_SHAPE, "empty shape: M=%u NH=%u B=%u", p->M, p->NH, B);
   if ((uint64_t)p->NH * p->D != p->N)
     return fail(MA_ERR_SHAPE, "N=%u must equal NH*D=%u*%u", p->N, p->NH, p->D);
-  if (p->M % 64 != 0)
-    return fail(MA_ERR_SHAPE, "sequence length M=%u must be a multiple of 64", p->M);
   const uint64_t nbh = (uint64_t)B * p->NH;
   if ((uint64_t)B * p->M * p->N >= (1ull << 40) || nbh >= (1ull << 30) || p->M > (1u << 24))
     return fail(MA_ERR_LIMIT, "problem too large: B=%u M=%u N=%u", B, p->M, p->N);
@@ -195,7 +193,6 @@ int ma_computeQKV(const ma_bf16* X, ma_bf16* q, ma_bf16* k, ma_bf16* v, const ma
   if (!p) return fail(MA_ERR_NULL, "AttentionParams pointer is NULL");
   if (p->N == 0 || p->M == 0 || B == 0) return fail(MA_ERR_SHAPE, "empty shape: M=%u N=%u B=%u", p->M, p->N, B);
   if (p->N % 64 != 0) return fail(MA_ERR_SHAPE, "N=%u must be a multiple of 64", p->N);
-  if (p->M % 64 != 0) return fail(MA_ERR_SHAPE, "M=%u must be a multiple of 64", p->M);
   if ((uint64_t)B * p->M >= (1ull << 31) || p->N > 16384)
     return fail(MA_ERR_LIMIT, "problem too large: B*M=%llu N=%u", (unsigned long long)B * p->M, p->N);
   MA_REQUIRE_PTR(X);

@@ -77,7 +77,7 @@ ALIGNED = 1 << 20  # a fake (never dereferenced) 16-byte aligned address
 @pytest.mark.parametrize("params,code", [
     (dict(D=32, N=192), 1),              # unsupported head size
     (dict(N=383), 1),                    # N != NH*D
-    (dict(M=100), 1),                    # M not a multiple of 64
+    (dict(D=96, N=384), 1),              # head size 96
     (dict(NH=0, N=0), 1),                # empty
 ])
 def test_forward_rejects_bad_shapes_without_device(cuda_lib, params, code):

@@ -98,6 +98,11 @@ def test_golden_vectors(A, name, case):
 SHAPES = [
     (1, 64, 1, 64), (2, 128, 3, 64), (1, 192, 2, 128), (2, 256, 2, 64), (1, 320, 1, 128),
     (1, 1024, 2, 64), (1, 1024, 2, 128), (16, 256, 6, 64),  # the last one is config 1
+    # sequence lengths that are not a multiple of the 64/128-row tiles (the
+    # reference requires multiples of 64; here partial tiles are zero-filled
+    # on load and clipped on store, per batch row)
+    (1, 1, 1, 64), (2, 100, 2, 64), (3, 200, 3, 64), (2, 130, 2, 128), (1, 257, 2, 128),
+    (2, 1000, 1, 64),
 ]
 
 
@@ -129,10 +134,11 @@ def test_row0_equals_v_row0(A):
     assert np.array_equal(down(out)[:, 0, :], v[:, 0, :])
 
 
-def test_shard_entry_points(A):
+@pytest.mark.parametrize("T", [256, 200])
+def test_shard_entry_points(A, T):
     """Shard variants write exactly their (batch, head) slabs, bit-identical to
-    the full call, and leave the rest untouched."""
-    B, T, H, D = 2, 256, 3, 64
+    the full call, and leave the rest untouched (also at a ragged length)."""
+    B, H, D = 2, 3, 64
     q, k, v, do = inputs(B, T, H, D, seed=9)
     full = gpu_chain(A, q, k, v, do, B, T, H, D)
     p = A.make_params(T, H, D)
@@ -188,6 +194,7 @@ def test_determinism(A):
     (1, 64, 3, 64),      # N = 192 (64-column tiles), one partial row tile
     (3, 192, 2, 128),    # N = 256, rows not a multiple of 128
     (64, 256, 6, 64),    # config 5: rows = 16384, N = 384
+    (3, 100, 3, 64),     # M not a multiple of 64: rows = 300
 ])
 def test_compute_qkv(A, oracle_mod, B, M, H, D):
     N = H * D
@@ -218,8 +225,8 @@ def test_cuda_attention_class_and_stream(A, oracle_mod):
 
 
 def test_bad_call_on_gpu_raises(A):
-    p = A.make_params(96, 1, 64)  # M not a multiple of 64
-    x = torch.zeros(1, 96, 64, dtype=torch.bfloat16, device="cuda")
+    p = A.make_params(96, 1, 32)  # head size 32
+    x = torch.zeros(1, 96, 32, dtype=torch.bfloat16, device="cuda")
     with pytest.raises(A.MetalAttnError, match="MA_ERR_SHAPE"):
         A.flashAttentionForward(x, x, x, p, 1)
 
