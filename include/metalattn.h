@@ -121,6 +121,41 @@ MA_API int ma_flashAttentionBackward_shard(const ma_bf16* dZ, const ma_bf16* d, 
                                     const AttentionParams* p, uint32_t B, uint32_t bh_begin,
                                     uint32_t bh_end, ma_stream_t stream);
 
+/* ---- GEMMs around attention (the rest of the attention block).  The
+ * activations have B*M rows; weights are [N][N] bf16 with row = input
+ * feature; weight gradients sum over all B*M rows.  N must be a multiple of
+ * 64.  Outputs are written (the reference accumulates into buffers its host
+ * zeroes first, model.h:552-556, which gives the same values). */
+
+/* projForward: out = attn_out * proj_w (bf16).  Replaces attention.metal:
+ * 395-416 (buffers 0..3) dispatched at model.h:474-481. */
+MA_API int ma_projForward(const ma_bf16* attn_out, const ma_bf16* proj_w, ma_bf16* out,
+                          const AttentionParams* p, uint32_t B, ma_stream_t stream);
+
+/* projBackwarddW: dProjw = attn_out^T * dZ (bf16, fp32 accumulation).
+ * Replaces attention.metal:418-430 (buffers 0..3) dispatched at model.h:621-628. */
+MA_API int ma_projBackwarddW(const ma_bf16* attn_out, const ma_bf16* dZ, ma_bf16* dProjw,
+                             const AttentionParams* p, uint32_t B, ma_stream_t stream);
+
+/* projBackwarddX: dAttn = dZ * proj_w^T (bf16).  Replaces attention.metal:
+ * 432-455 (buffers 0..3) dispatched at model.h:629-636. */
+MA_API int ma_projBackwarddX(const ma_bf16* dZ, const ma_bf16* proj_w, ma_bf16* dAttn,
+                             const AttentionParams* p, uint32_t B, ma_stream_t stream);
+
+/* computeGradDx: dX = dQ * Wq^T + dK * Wk^T + dV * Wv^T, fp32 (dQ fp32, the
+ * rest bf16; dQ enters the tensor core rounded to bf16).  Replaces
+ * attention.metal:301-342 (buffers 0..7) dispatched at model.h:666-678. */
+MA_API int ma_computeGradDx(float* dX, const ma_bf16* qw, const ma_bf16* kw, const ma_bf16* vw,
+                            const float* dQ, const ma_bf16* dK, const ma_bf16* dV,
+                            const AttentionParams* p, uint32_t B, ma_stream_t stream);
+
+/* computeGradDw: dQw = X^T * dQ (fp32), dKw = X^T * dK, dVw = X^T * dV
+ * (bf16), fp32 accumulation (dQ rounded to bf16 on entry).  Replaces
+ * attention.metal:344-393 (buffers 0..7) dispatched at model.h:679-691. */
+MA_API int ma_computeGradDw(const ma_bf16* x, const float* dQ, const ma_bf16* dK,
+                            const ma_bf16* dV, float* dQw, ma_bf16* dKw, ma_bf16* dVw,
+                            const AttentionParams* p, uint32_t B, ma_stream_t stream);
+
 /* Allocation-free backward pass: computeD followed by flashAttentionBackward,
  * for callers that cannot let a library allocate device memory (hosts whose
  * own arena or caching allocator owns all of the GPU's memory, processes under

@@ -50,6 +50,11 @@ SIGNATURES = {
     "ma_computeD_shard": [_P, _P, _P, _PP, _U32, _U32, _U32, _P],
     "ma_flashAttentionBackward_shard": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _PP, _U32, _U32, _U32, _P],
     "ma_flashAttentionBackward_noalloc": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _PP, _U32, _P],
+    "ma_projForward": [_P, _P, _P, _PP, _U32, _P],
+    "ma_projBackwarddW": [_P, _P, _P, _PP, _U32, _P],
+    "ma_projBackwarddX": [_P, _P, _P, _PP, _U32, _P],
+    "ma_computeGradDx": [_P, _P, _P, _P, _P, _P, _P, _PP, _U32, _P],
+    "ma_computeGradDw": [_P, _P, _P, _P, _P, _P, _P, _PP, _U32, _P],
     "ma_device_status": [ctypes.POINTER(ctypes.c_uint32), _P],
     "ma_version": [],
 }

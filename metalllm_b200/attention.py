@@ -83,6 +83,80 @@ def computeQKV(X: torch.Tensor, q_w: torch.Tensor, k_w: torch.Tensor, v_w: torch
     return q, k, v
 
 
+def projForward(attn_out: torch.Tensor, proj_w: torch.Tensor, p: AttentionParams, B: int,
+                out: Optional[torch.Tensor] = None, stream: Optional[torch.cuda.Stream] = None):
+    """out = attn_out . proj_w (attention.metal:395-416)."""
+    act = (B, p.M, p.N)
+    _check(attn_out, "attn_out", torch.bfloat16, act)
+    _check(proj_w, "proj_w", torch.bfloat16, (p.N, p.N))
+    out = _out(out, attn_out, act, torch.bfloat16, "out")
+    _lib.call("ma_projForward", _ptr(attn_out), _ptr(proj_w), _ptr(out), ctypes.byref(p), B,
+              _stream(stream))
+    return out
+
+
+def projBackwarddW(attn_out: torch.Tensor, dZ: torch.Tensor, p: AttentionParams, B: int,
+                   dProjw: Optional[torch.Tensor] = None,
+                   stream: Optional[torch.cuda.Stream] = None):
+    """dProjw = attn_out^T . dZ over all B*M rows (attention.metal:418-430)."""
+    act = (B, p.M, p.N)
+    _check(attn_out, "attn_out", torch.bfloat16, act)
+    _check(dZ, "dZ", torch.bfloat16, act)
+    dProjw = _out(dProjw, attn_out, (p.N, p.N), torch.bfloat16, "dProjw")
+    _lib.call("ma_projBackwarddW", _ptr(attn_out), _ptr(dZ), _ptr(dProjw), ctypes.byref(p), B,
+              _stream(stream))
+    return dProjw
+
+
+def projBackwarddX(dZ: torch.Tensor, proj_w: torch.Tensor, p: AttentionParams, B: int,
+                   dAttn: Optional[torch.Tensor] = None,
+                   stream: Optional[torch.cuda.Stream] = None):
+    """dAttn = dZ . proj_w^T (attention.metal:432-455)."""
+    act = (B, p.M, p.N)
+    _check(dZ, "dZ", torch.bfloat16, act)
+    _check(proj_w, "proj_w", torch.bfloat16, (p.N, p.N))
+    dAttn = _out(dAttn, dZ, act, torch.bfloat16, "dAttn")
+    _lib.call("ma_projBackwarddX", _ptr(dZ), _ptr(proj_w), _ptr(dAttn), ctypes.byref(p), B,
+              _stream(stream))
+    return dAttn
+
+
+def computeGradDx(q_w: torch.Tensor, k_w: torch.Tensor, v_w: torch.Tensor, dQ: torch.Tensor,
+                  dK: torch.Tensor, dV: torch.Tensor, p: AttentionParams, B: int,
+                  dX: Optional[torch.Tensor] = None, stream: Optional[torch.cuda.Stream] = None):
+    """dX = dQ.Wq^T + dK.Wk^T + dV.Wv^T in fp32 (attention.metal:301-342)."""
+    act = (B, p.M, p.N)
+    for w, n in ((q_w, "q_w"), (k_w, "k_w"), (v_w, "v_w")):
+        _check(w, n, torch.bfloat16, (p.N, p.N))
+    _check(dQ, "dQ", torch.float32, act)
+    _check(dK, "dK", torch.bfloat16, act)
+    _check(dV, "dV", torch.bfloat16, act)
+    dX = _out(dX, dK, act, torch.float32, "dX")
+    _lib.call("ma_computeGradDx", _ptr(dX), _ptr(q_w), _ptr(k_w), _ptr(v_w), _ptr(dQ), _ptr(dK),
+              _ptr(dV), ctypes.byref(p), B, _stream(stream))
+    return dX
+
+
+def computeGradDw(x: torch.Tensor, dQ: torch.Tensor, dK: torch.Tensor, dV: torch.Tensor,
+                  p: AttentionParams, B: int, dQw: Optional[torch.Tensor] = None,
+                  dKw: Optional[torch.Tensor] = None, dVw: Optional[torch.Tensor] = None,
+                  stream: Optional[torch.cuda.Stream] = None):
+    """dQw = X^T.dQ (fp32), dKw = X^T.dK, dVw = X^T.dV (bf16) over all B*M rows
+    (attention.metal:344-393)."""
+    act = (B, p.M, p.N)
+    _check(x, "x", torch.bfloat16, act)
+    _check(dQ, "dQ", torch.float32, act)
+    _check(dK, "dK", torch.bfloat16, act)
+    _check(dV, "dV", torch.bfloat16, act)
+    w = (p.N, p.N)
+    dQw = _out(dQw, x, w, torch.float32, "dQw")
+    dKw = _out(dKw, x, w, torch.bfloat16, "dKw")
+    dVw = _out(dVw, x, w, torch.bfloat16, "dVw")
+    _lib.call("ma_computeGradDw", _ptr(x), _ptr(dQ), _ptr(dK), _ptr(dV), _ptr(dQw), _ptr(dKw),
+              _ptr(dVw), ctypes.byref(p), B, _stream(stream))
+    return dQw, dKw, dVw
+
+
 def flashAttentionForward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, p: AttentionParams,
                           B: int, out: Optional[torch.Tensor] = None,
                           l: Optional[torch.Tensor] = None, shard: Optional[tuple] = None,

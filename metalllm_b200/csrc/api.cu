@@ -250,6 +250,122 @@ int ma_flashAttentionBackward_shard(const ma_bf16* dZ, const ma_bf16* d, const f
   return backward_impl(dZ, d, l, q, k, v, dQ, dK, dV, p, B, bh_begin, bh_end, true, stream);
 }
 
+// ---------------------------------------------------------------- GEMMs
+// Shared validation of the GEMM entry points: N a positive multiple of 64
+// (16-byte TMA strides, whole 64-column weight tiles), B*M rows >= 1.
+static int gemm_shape(const AttentionParams* p, uint32_t B, int* rows, int* n) {
+  if (!p) return fail(MA_ERR_NULL, "AttentionParams pointer is NULL");
+  if (p->N == 0 || p->M == 0 || B == 0) return fail(MA_ERR_SHAPE, "empty shape: M=%u N=%u B=%u", p->M, p->N, B);
+  if (p->N % 64 != 0) return fail(MA_ERR_SHAPE, "N=%u must be a multiple of 64", p->N);
+  if ((uint64_t)B * p->M >= (1ull << 31) || p->N > 16384)
+    return fail(MA_ERR_LIMIT, "problem too large: B*M=%llu N=%u", (unsigned long long)B * p->M, p->N);
+  *rows = (int)(B * p->M);
+  *n = (int)p->N;
+  return MA_OK;
+}
+
+int ma_projForward(const ma_bf16* attn_out, const ma_bf16* proj_w, ma_bf16* out,
+                   const AttentionParams* p, uint32_t B, ma_stream_t stream) {
+  int rows = 0, n = 0;
+  int rc = gemm_shape(p, B, &rows, &n);
+  if (rc) return rc;
+  MA_REQUIRE_PTR(attn_out);
+  MA_REQUIRE_PTR(proj_w);
+  MA_REQUIRE_PTR(out);
+  uint32_t* status = nullptr;
+  rc = device_status_word(&status);
+  if (rc) return rc;
+  cudaError_t e = ma::launch_proj_forward(reinterpret_cast<bf16p>(attn_out), reinterpret_cast<bf16p>(proj_w),
+                                          reinterpret_cast<bf16m>(out), rows, n, status,
+                                          reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "projForward launch");
+  return ok();
+}
+
+int ma_projBackwarddW(const ma_bf16* attn_out, const ma_bf16* dZ, ma_bf16* dProjw,
+                      const AttentionParams* p, uint32_t B, ma_stream_t stream) {
+  int rows = 0, n = 0;
+  int rc = gemm_shape(p, B, &rows, &n);
+  if (rc) return rc;
+  MA_REQUIRE_PTR(attn_out);
+  MA_REQUIRE_PTR(dZ);
+  MA_REQUIRE_PTR(dProjw);
+  uint32_t* status = nullptr;
+  rc = device_status_word(&status);
+  if (rc) return rc;
+  cudaError_t e = ma::launch_proj_backward_dw(reinterpret_cast<bf16p>(attn_out), reinterpret_cast<bf16p>(dZ),
+                                              reinterpret_cast<bf16m>(dProjw), rows, n, status,
+                                              reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "projBackwarddW launch");
+  return ok();
+}
+
+int ma_projBackwarddX(const ma_bf16* dZ, const ma_bf16* proj_w, ma_bf16* dAttn,
+                      const AttentionParams* p, uint32_t B, ma_stream_t stream) {
+  int rows = 0, n = 0;
+  int rc = gemm_shape(p, B, &rows, &n);
+  if (rc) return rc;
+  MA_REQUIRE_PTR(dZ);
+  MA_REQUIRE_PTR(proj_w);
+  MA_REQUIRE_PTR(dAttn);
+  uint32_t* status = nullptr;
+  rc = device_status_word(&status);
+  if (rc) return rc;
+  cudaError_t e = ma::launch_proj_backward_dx(reinterpret_cast<bf16p>(dZ), reinterpret_cast<bf16p>(proj_w),
+                                              reinterpret_cast<bf16m>(dAttn), rows, n, status,
+                                              reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "projBackwarddX launch");
+  return ok();
+}
+
+int ma_computeGradDx(float* dX, const ma_bf16* qw, const ma_bf16* kw, const ma_bf16* vw,
+                     const float* dQ, const ma_bf16* dK, const ma_bf16* dV,
+                     const AttentionParams* p, uint32_t B, ma_stream_t stream) {
+  int rows = 0, n = 0;
+  int rc = gemm_shape(p, B, &rows, &n);
+  if (rc) return rc;
+  MA_REQUIRE_PTR(dX);
+  MA_REQUIRE_PTR(qw);
+  MA_REQUIRE_PTR(kw);
+  MA_REQUIRE_PTR(vw);
+  MA_REQUIRE_PTR(dQ);
+  MA_REQUIRE_PTR(dK);
+  MA_REQUIRE_PTR(dV);
+  uint32_t* status = nullptr;
+  rc = device_status_word(&status);
+  if (rc) return rc;
+  cudaError_t e = ma::launch_grad_dx(dX, reinterpret_cast<bf16p>(qw), reinterpret_cast<bf16p>(kw),
+                                     reinterpret_cast<bf16p>(vw), dQ, reinterpret_cast<bf16p>(dK),
+                                     reinterpret_cast<bf16p>(dV), rows, n, status,
+                                     reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "computeGradDx launch");
+  return ok();
+}
+
+int ma_computeGradDw(const ma_bf16* x, const float* dQ, const ma_bf16* dK, const ma_bf16* dV,
+                     float* dQw, ma_bf16* dKw, ma_bf16* dVw, const AttentionParams* p, uint32_t B,
+                     ma_stream_t stream) {
+  int rows = 0, n = 0;
+  int rc = gemm_shape(p, B, &rows, &n);
+  if (rc) return rc;
+  MA_REQUIRE_PTR(x);
+  MA_REQUIRE_PTR(dQ);
+  MA_REQUIRE_PTR(dK);
+  MA_REQUIRE_PTR(dV);
+  MA_REQUIRE_PTR(dQw);
+  MA_REQUIRE_PTR(dKw);
+  MA_REQUIRE_PTR(dVw);
+  uint32_t* status = nullptr;
+  rc = device_status_word(&status);
+  if (rc) return rc;
+  cudaError_t e = ma::launch_grad_dw(reinterpret_cast<bf16p>(x), dQ, reinterpret_cast<bf16p>(dK),
+                                     reinterpret_cast<bf16p>(dV), dQw, reinterpret_cast<bf16m>(dKw),
+                                     reinterpret_cast<bf16m>(dVw), rows, n, status,
+                                     reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "computeGradDw launch");
+  return ok();
+}
+
 const char* ma_last_error_string(void) { return g_last_error.c_str(); }
 
 int ma_device_status(uint32_t* status, ma_stream_t stream) {

@@ -14,6 +14,7 @@ enum : uint32_t {
   STATUS_FWD_TIMEOUT = 1u << 0,
   STATUS_BWD_TIMEOUT = 1u << 1,
   STATUS_QKV_TIMEOUT = 1u << 2,
+  STATUS_GEMM_TIMEOUT = 1u << 3,
 };
 
 // Problem description shared by the attention kernels.  Row strides are in
@@ -47,5 +48,21 @@ cudaError_t launch_qkv(const __nv_bfloat16* X, __nv_bfloat16* q, __nv_bfloat16* 
                        __nv_bfloat16* v, const __nv_bfloat16* qw, const __nv_bfloat16* kw,
                        const __nv_bfloat16* vw, int rows, int N, uint32_t* status,
                        cudaStream_t st);
+
+// GEMMs around attention (gemm_sm100.cu); rows = B*M activation rows, n = N.
+cudaError_t launch_proj_forward(const __nv_bfloat16* attn, const __nv_bfloat16* w, __nv_bfloat16* out,
+                                int rows, int n, uint32_t* status, cudaStream_t st);
+cudaError_t launch_proj_backward_dx(const __nv_bfloat16* dz, const __nv_bfloat16* w,
+                                    __nv_bfloat16* dattn, int rows, int n, uint32_t* status,
+                                    cudaStream_t st);
+cudaError_t launch_proj_backward_dw(const __nv_bfloat16* attn, const __nv_bfloat16* dz,
+                                    __nv_bfloat16* dw, int rows, int n, uint32_t* status,
+                                    cudaStream_t st);
+cudaError_t launch_grad_dx(float* dx, const __nv_bfloat16* qw, const __nv_bfloat16* kw,
+                           const __nv_bfloat16* vw, const float* dq, const __nv_bfloat16* dk,
+                           const __nv_bfloat16* dv, int rows, int n, uint32_t* status, cudaStream_t st);
+cudaError_t launch_grad_dw(const __nv_bfloat16* x, const float* dq, const __nv_bfloat16* dk,
+                           const __nv_bfloat16* dv, float* dqw, __nv_bfloat16* dkw, __nv_bfloat16* dvw,
+                           int rows, int n, uint32_t* status, cudaStream_t st);
 
 }  // namespace ma

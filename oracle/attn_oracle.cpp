@@ -5,6 +5,9 @@
 //   flashAttentionForward  attention.metal:56-164  (dispatch model.h:459-473)
 //   computeD               attention.metal:166-195 (dispatch model.h:639-647)
 //   flashAttentionBackward attention.metal:198-299 (dispatch model.h:648-665)
+//   computeGradDx, computeGradDw, projForward, projBackwarddW, projBackwarddX
+//                          attention.metal:301-455 (dispatch model.h:474-481,
+//                          621-636, 666-691)
 //
 // PARITY UNPINNED: the reference runs only on Apple Metal and ships no tests,
 // golden vectors or fixtures, and its contractions run inside the closed
@@ -41,6 +44,7 @@
 #include <cstdint>
 #include <cstring>
 #include <thread>
+#include <functional>
 #include <vector>
 
 namespace {
@@ -496,6 +500,133 @@ int oracle_flash_backward(const uint16_t* dO, const uint16_t* Dv, const float* l
   } else {
     bwd_exact<float>(dO, Dv, lse, q, k, v, dQ, dK, dV, dk32, dv32, s, bh_begin, bh_end, nthreads);
   }
+  return 0;
+}
+
+// ---------------------------------------------------------------- GEMMs
+// The GEMMs around attention (attention.metal:301-455), fp32 accumulation.
+// Activations are [rows][N] (rows = B*M), weights [N][N] with row = input
+// feature.  Operands marked fp32 are read as fp32 (the reference's dQ);
+// everything else is bf16.  `sel` / `nsel` (optional) restrict the work to
+// those output rows (the rest is left untouched): large shapes are checked on
+// a sample of rows.  c32 (optional) receives the unrounded fp32 results.
+namespace {
+
+inline float ld(const void* p, bool f32, int64_t i) {
+  return f32 ? static_cast<const float*>(p)[i] : bf2f(static_cast<const uint16_t*>(p)[i]);
+}
+
+// C[r][n] = sum_p sum_k A_p[r][k] * W_p[n][k]   (A times W^T; row r of C)
+void rows_times_wt(int np, const void* const* A, const bool* af32, const uint16_t* const* W,
+                   int64_t rows, int64_t N, const int64_t* sel, int64_t nsel, int nthreads,
+                   std::function<void(int64_t, int64_t, float)> put) {
+  const int64_t nr = sel ? nsel : rows;
+  parallel_for(nr, nthreads, [&](int64_t idx) {
+    const int64_t r = sel ? sel[idx] : idx;
+    for (int64_t n = 0; n < N; ++n) {
+      float acc = 0.0f;
+      for (int p = 0; p < np; ++p)
+        for (int64_t k = 0; k < N; ++k) acc += ld(A[p], af32[p], r * N + k) * bf2f(W[p][n * N + k]);
+      put(r, n, acc);
+    }
+  });
+}
+
+// C[i][j] = sum_r X[r][i] * G[r][j]   (X^T times G; row i of C)
+void xt_times_g(const uint16_t* X, const void* G, bool gf32, int64_t rows, int64_t N,
+                const int64_t* sel, int64_t nsel, int nthreads,
+                std::function<void(int64_t, int64_t, float)> put) {
+  const int64_t nr = sel ? nsel : N;
+  parallel_for(nr, nthreads, [&](int64_t idx) {
+    const int64_t i = sel ? sel[idx] : idx;
+    std::vector<float> acc(N, 0.0f);
+    for (int64_t r = 0; r < rows; ++r) {
+      const float x = bf2f(X[r * N + i]);
+      if (x == 0.0f) continue;
+      for (int64_t j = 0; j < N; ++j) acc[j] += x * ld(G, gf32, r * N + j);
+    }
+    for (int64_t j = 0; j < N; ++j) put(i, j, acc[j]);
+  });
+}
+
+}  // namespace
+
+// projForward (attention.metal:395-416): out = attn_out . proj_w
+int oracle_proj_forward(const uint16_t* attn, const uint16_t* w, uint16_t* out, uint32_t rows,
+                        uint32_t N, const int64_t* sel, int64_t nsel, int nthreads, float* out32) {
+  if (!attn || !w || !out || rows == 0 || N == 0) return 1;
+  const int64_t nr = sel ? nsel : rows;
+  parallel_for(nr, nthreads, [&](int64_t idx) {
+    const int64_t r = sel ? sel[idx] : idx;
+    std::vector<float> acc(N, 0.0f);
+    for (int64_t k = 0; k < N; ++k) {
+      const float a = bf2f(attn[r * N + k]);
+      if (a == 0.0f) continue;
+      for (int64_t n = 0; n < N; ++n) acc[n] += a * bf2f(w[k * N + n]);
+    }
+    for (int64_t n = 0; n < N; ++n) {
+      out[r * N + n] = f2bf(acc[n]);
+      if (out32) out32[r * N + n] = acc[n];
+    }
+  });
+  return 0;
+}
+
+// projBackwarddX (attention.metal:432-455): dAttn = dZ . proj_w^T
+int oracle_proj_backward_dx(const uint16_t* dz, const uint16_t* w, uint16_t* dattn, uint32_t rows,
+                            uint32_t N, const int64_t* sel, int64_t nsel, int nthreads, float* d32) {
+  if (!dz || !w || !dattn || rows == 0 || N == 0) return 1;
+  const void* A[1] = {dz};
+  const bool af[1] = {false};
+  const uint16_t* W[1] = {w};
+  rows_times_wt(1, A, af, W, rows, N, sel, nsel, nthreads, [&](int64_t r, int64_t n, float v) {
+    dattn[r * N + n] = f2bf(v);
+    if (d32) d32[r * N + n] = v;
+  });
+  return 0;
+}
+
+// projBackwarddW (attention.metal:418-430): dProjw = attn_out^T . dZ
+int oracle_proj_backward_dw(const uint16_t* attn, const uint16_t* dz, uint16_t* dw, uint32_t rows,
+                            uint32_t N, const int64_t* sel, int64_t nsel, int nthreads, float* dw32) {
+  if (!attn || !dz || !dw || rows == 0 || N == 0) return 1;
+  xt_times_g(attn, dz, false, rows, N, sel, nsel, nthreads, [&](int64_t i, int64_t j, float v) {
+    dw[i * N + j] = f2bf(v);
+    if (dw32) dw32[i * N + j] = v;
+  });
+  return 0;
+}
+
+// computeGradDx (attention.metal:301-342): dX = dQ.Wq^T + dK.Wk^T + dV.Wv^T
+// (fp32 dQ and dX, the three products summed in one fp32 accumulator)
+int oracle_grad_dx(float* dx, const uint16_t* qw, const uint16_t* kw, const uint16_t* vw,
+                   const float* dq, const uint16_t* dk, const uint16_t* dv, uint32_t rows, uint32_t N,
+                   const int64_t* sel, int64_t nsel, int nthreads) {
+  if (!dx || !qw || !kw || !vw || !dq || !dk || !dv || rows == 0 || N == 0) return 1;
+  const void* A[3] = {dq, dk, dv};
+  const bool af[3] = {true, false, false};
+  const uint16_t* W[3] = {qw, kw, vw};
+  rows_times_wt(3, A, af, W, rows, N, sel, nsel, nthreads,
+                [&](int64_t r, int64_t n, float v) { dx[r * N + n] = v; });
+  return 0;
+}
+
+// computeGradDw (attention.metal:344-393): dQw = X^T.dQ (fp32), dKw = X^T.dK,
+// dVw = X^T.dV (bf16; dk32/dv32 optional unrounded values)
+int oracle_grad_dw(const uint16_t* x, const float* dq, const uint16_t* dk, const uint16_t* dv,
+                   float* dqw, uint16_t* dkw, uint16_t* dvw, uint32_t rows, uint32_t N,
+                   const int64_t* sel, int64_t nsel, int nthreads, float* dk32, float* dv32) {
+  if (!x || !dq || !dk || !dv || !dqw || !dkw || !dvw || rows == 0 || N == 0) return 1;
+  xt_times_g(x, dq, true, rows, N, sel, nsel, nthreads,
+             [&](int64_t i, int64_t j, float v) { dqw[i * N + j] = v; });
+  xt_times_g(x, dk, false, rows, N, sel, nsel, nthreads, [&](int64_t i, int64_t j, float v) {
+    dkw[i * N + j] = f2bf(v);
+    if (dk32) dk32[i * N + j] = v;
+  });
+  xt_times_g(x, dv, false, rows, N, sel, nsel, nthreads, [&](int64_t i, int64_t j, float v) {
+    dvw[i * N + j] = f2bf(v);
+    if (dv32) dv32[i * N + j] = v;
+  });
   return 0;
 }
 

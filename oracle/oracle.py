@@ -42,8 +42,15 @@ def load():
         lib.oracle_flash_backward.argtypes = [P, P, P, P, P, P, P, P, P, U, U, U, U, U, U, U, I, I, P, P]
         lib.oracle_fp64_loss.argtypes = [P, P, P, P, U, U]
         lib.oracle_fp64_loss.restype = ctypes.c_double
+        L = ctypes.c_int64
+        lib.oracle_proj_forward.argtypes = [P, P, P, U, U, P, L, I, P]
+        lib.oracle_proj_backward_dx.argtypes = [P, P, P, U, U, P, L, I, P]
+        lib.oracle_proj_backward_dw.argtypes = [P, P, P, U, U, P, L, I, P]
+        lib.oracle_grad_dx.argtypes = [P, P, P, P, P, P, P, U, U, P, L, I]
+        lib.oracle_grad_dw.argtypes = [P, P, P, P, P, P, P, U, U, P, L, I, P, P]
         for n in ("oracle_compute_qkv", "oracle_flash_forward", "oracle_compute_d",
-                  "oracle_flash_backward"):
+                  "oracle_flash_backward", "oracle_proj_forward", "oracle_proj_backward_dx",
+                  "oracle_proj_backward_dw", "oracle_grad_dx", "oracle_grad_dw"):
             getattr(lib, n).restype = ctypes.c_int
         _lib = lib
     return _lib
@@ -137,3 +144,72 @@ def compare(got, want, max_abs=2e-2, rel_l2=1e-2):
     rl2 = float(np.linalg.norm(g - w) / denom) if denom > 0 else float(np.linalg.norm(g - w))
     ok = bool(np.isfinite(g).all()) and mae <= max_abs and rl2 <= rel_l2
     return ok, mae, rl2
+
+
+# ------------------------------------------------------------------ GEMMs
+# attention.metal:301-455.  Activations are [rows, N] (any leading shape is
+# flattened), weights [N, N] bf16 bits; dQ and the fp32 outputs are float32.
+# `rows` (optional) restricts the computed output rows; the others are NaN.
+
+def _sel(rows):
+    if rows is None:
+        return None, 0
+    r = np.ascontiguousarray(np.asarray(rows, dtype=np.int64))
+    return r, len(r)
+
+
+def _flat(a):
+    return np.ascontiguousarray(a).reshape(-1, a.shape[-1])
+
+
+def proj_forward(attn, w, rows=None, nthreads=0):
+    """out = attn . w (attention.metal:395-416); returns (bf16 bits, fp32)."""
+    a = _flat(attn); R, N = a.shape
+    out = np.full(a.shape, 0x7FC0, np.uint16); o32 = np.full(a.shape, np.nan, np.float32)
+    sel, ns = _sel(rows)
+    assert load().oracle_proj_forward(_p(a), _p(w), _p(out), R, N, _p(sel), ns, nthreads, _p(o32)) == 0
+    return out, o32
+
+
+def proj_backward_dx(dz, w, rows=None, nthreads=0):
+    """dAttn = dz . w^T (attention.metal:432-455); returns (bf16 bits, fp32)."""
+    a = _flat(dz); R, N = a.shape
+    out = np.full(a.shape, 0x7FC0, np.uint16); o32 = np.full(a.shape, np.nan, np.float32)
+    sel, ns = _sel(rows)
+    assert load().oracle_proj_backward_dx(_p(a), _p(w), _p(out), R, N, _p(sel), ns, nthreads, _p(o32)) == 0
+    return out, o32
+
+
+def proj_backward_dw(attn, dz, rows=None, nthreads=0):
+    """dW = attn^T . dz (attention.metal:418-430); returns (bf16 bits, fp32) [N, N]."""
+    a = _flat(attn); g = _flat(dz); R, N = a.shape
+    out = np.full((N, N), 0x7FC0, np.uint16); o32 = np.full((N, N), np.nan, np.float32)
+    sel, ns = _sel(rows)
+    assert load().oracle_proj_backward_dw(_p(a), _p(g), _p(out), R, N, _p(sel), ns, nthreads, _p(o32)) == 0
+    return out, o32
+
+
+def grad_dx(qw, kw, vw, dq, dk, dv, rows=None, nthreads=0):
+    """dX = dQ.Wq^T + dK.Wk^T + dV.Wv^T, fp32 (attention.metal:301-342)."""
+    q32 = np.ascontiguousarray(dq, dtype=np.float32).reshape(-1, dq.shape[-1])
+    k = _flat(dk); v = _flat(dv); R, N = k.shape
+    dx = np.full((R, N), np.nan, np.float32)
+    sel, ns = _sel(rows)
+    assert load().oracle_grad_dx(_p(dx), _p(qw), _p(kw), _p(vw), _p(q32), _p(k), _p(v), R, N,
+                                 _p(sel), ns, nthreads) == 0
+    return dx
+
+
+def grad_dw(x, dq, dk, dv, rows=None, nthreads=0):
+    """dQw = X^T.dQ (fp32), dKw = X^T.dK, dVw = X^T.dV (attention.metal:344-393).
+    Returns dQw, dKw bits, dVw bits, dKw fp32, dVw fp32 ([N, N] each)."""
+    xx = _flat(x); R, N = xx.shape
+    q32 = np.ascontiguousarray(dq, dtype=np.float32).reshape(-1, N)
+    k = _flat(dk); v = _flat(dv)
+    dqw = np.full((N, N), np.nan, np.float32)
+    dkw = np.full((N, N), 0x7FC0, np.uint16); dvw = np.full((N, N), 0x7FC0, np.uint16)
+    k32 = np.full((N, N), np.nan, np.float32); v32 = np.full((N, N), np.nan, np.float32)
+    sel, ns = _sel(rows)
+    assert load().oracle_grad_dw(_p(xx), _p(q32), _p(k), _p(v), _p(dqw), _p(dkw), _p(dvw), R, N,
+                                 _p(sel), ns, nthreads, _p(k32), _p(v32)) == 0
+    return dqw, dkw, dvw, k32, v32

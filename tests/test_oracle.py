@@ -193,3 +193,40 @@ def test_oracle_rejects_bad_shapes(oracle_mod):
     rc = lib.oracle_flash_forward(q.ctypes.data, q.ctypes.data, q.ctypes.data, q.ctypes.data,
                                   lse.ctypes.data, 64, 64, 64, 1, 1, 0, 2, 0, 1, None)
     assert rc != 0
+
+
+# ------------------------------------------------ GEMMs around attention
+def test_oracle_gemms_match_numpy(oracle_mod):
+    """The oracle's restatements of attention.metal:301-455 equal dense fp64
+    numpy products of the same bf16/fp32 inputs to fp32 accuracy, and the
+    row-sampled mode computes exactly the requested rows."""
+    from metalllm_b200.inputs import bf16_bits_to_f32, normal_bf16
+    o = oracle_mod
+    B, M, N = 2, 50, 64
+    R = B * M
+    act = lambda s: normal_bf16(R * N, 7, s).reshape(B, M, N)
+    w = lambda s: normal_bf16(N * N, 7, s, 0.02).reshape(N, N)
+    f = bf16_bits_to_f32
+    a, dz, x, dk, dv = act(1), act(2), act(3), act(4), act(5)
+    wp, qw, kw, vw = w(6), w(7), w(8), w(9)
+    dq = np.random.default_rng(0).standard_normal((B, M, N)).astype(np.float32)
+    A64 = lambda t: f(t).reshape(R, N).astype(np.float64)
+    tol = lambda got, want: np.abs(got - want).max() <= 1e-4 * max(1.0, np.abs(want).max())
+    _, o32 = o.proj_forward(a, wp)
+    assert tol(o32, A64(a) @ f(wp).astype(np.float64))
+    _, d32 = o.proj_backward_dx(dz, wp)
+    assert tol(d32, A64(dz) @ f(wp).astype(np.float64).T)
+    _, w32 = o.proj_backward_dw(a, dz)
+    assert tol(w32, A64(a).T @ A64(dz))
+    dx = o.grad_dx(qw, kw, vw, dq, dk, dv)
+    want = (dq.reshape(R, N).astype(np.float64) @ f(qw).astype(np.float64).T
+            + A64(dk) @ f(kw).astype(np.float64).T + A64(dv) @ f(vw).astype(np.float64).T)
+    assert tol(dx, want)
+    dqw, _, _, k32, v32 = o.grad_dw(x, dq, dk, dv)
+    assert tol(dqw, A64(x).T @ dq.reshape(R, N).astype(np.float64))
+    assert tol(k32, A64(x).T @ A64(dk))
+    assert tol(v32, A64(x).T @ A64(dv))
+    rows = np.array([3, 17, 40])
+    dx_s = o.grad_dx(qw, kw, vw, dq, dk, dv, rows=rows)
+    assert np.array_equal(dx_s[rows], dx[rows])
+    assert np.isnan(np.delete(dx_s, rows, axis=0)).all()
