@@ -156,6 +156,55 @@ MA_API int ma_computeGradDw(const ma_bf16* x, const float* dQ, const ma_bf16* dK
                             const ma_bf16* dV, float* dQw, ma_bf16* dKw, ma_bf16* dVw,
                             const AttentionParams* p, uint32_t B, ma_stream_t stream);
 
+/* ---- Training step (config 5): the CUDA counterpart of the reference's
+ * Model (model.h:104-860) for a batch of B sequences: token + positional
+ * embedding, `layers` pre-LayerNorm blocks (attention through the entry
+ * points above, then a ReLU MLP of width E*mlp_scale), a final LayerNorm, the
+ * vocabulary projection, mean cross-entropy, and Adam (beta1 0.9, beta2
+ * 0.999, eps 1e-8, bias-corrected step size, fp32 master weights, bf16
+ * gradients and moments; optimstep.metal, model.h:726-757).  The model
+ * allocates and owns all its buffers at creation (cudaMalloc) and initialises
+ * the weights from `seed` with the reference's distributions
+ * (main.cpp:1594-1620).  forward/backward/step only enqueue work on `stream`.
+ * No counterpart in the attention-only reference ABI: it replaces model.h's
+ * orchestration. */
+typedef struct MaModelConfig {
+  uint32_t B;          /* sequences per step */
+  uint32_t T;          /* sequence length (BLOCK_SIZE) */
+  uint32_t E;          /* embedding width (N_EMBED), a multiple of 64 */
+  uint32_t NH;         /* heads; E/NH must be 64 or 128 */
+  uint32_t layers;     /* N_LAYERS */
+  uint32_t mlp_scale;  /* MLP width = E*mlp_scale (MLP_SCALE) */
+  uint32_t vocab;      /* vocabulary (padded), a multiple of 64 */
+  float lr;            /* LR */
+  uint64_t seed;
+} MaModelConfig;
+
+typedef struct ma_model ma_model;
+
+MA_API int ma_model_create(const MaModelConfig* cfg, ma_model** model);
+MA_API int ma_model_destroy(ma_model* model);
+/* tokens, targets: device int32 [B][T]; they must stay valid until backward
+ * has been enqueued.  The mean loss is the tensor "loss" (device fp32). */
+MA_API int ma_model_forward(ma_model* model, const int32_t* tokens, const int32_t* targets,
+                            ma_stream_t stream);
+MA_API int ma_model_backward(ma_model* model, ma_stream_t stream);
+MA_API int ma_model_step(ma_model* model, ma_stream_t stream);
+/* Device pointer and size of a named buffer: a parameter ("embed", "pos",
+ * "layer<n>.qw" ... "linw"), its gradient ("grad.<name>"), or "logits",
+ * "loss", "loss_rows", "lse_rows", "embed_out", "master", "dstream". */
+MA_API int ma_model_tensor(ma_model* model, const char* name, void** ptr, uint64_t* bytes);
+/* Synchronous copies of a named tensor to / from host memory (bytes must be
+ * its size).  Writing a parameter also resets its fp32 master copy. */
+MA_API int ma_model_read(ma_model* model, const char* name, void* host, uint64_t bytes);
+MA_API int ma_model_write(ma_model* model, const char* name, const void* host, uint64_t bytes);
+MA_API uint32_t ma_model_param_count(ma_model* model);
+MA_API const char* ma_model_param_name(ma_model* model, uint32_t index);
+/* Copies the model's kernel status word (bounded-wait time-outs) to *status. */
+MA_API int ma_model_status(ma_model* model, uint32_t* status);
+/* Text for the last error of a ma_model_* call on the calling thread. */
+MA_API const char* ma_model_last_error(void);
+
 /* Allocation-free backward pass: computeD followed by flashAttentionBackward,
  * for callers that cannot let a library allocate device memory (hosts whose
  * own arena or caching allocator owns all of the GPU's memory, processes under

@@ -65,4 +65,32 @@ cudaError_t launch_grad_dw(const __nv_bfloat16* x, const float* dq, const __nv_b
                            const __nv_bfloat16* dv, float* dqw, __nv_bfloat16* dkw, __nv_bfloat16* dvw,
                            int rows, int n, uint32_t* status, cudaStream_t st);
 
+cudaError_t launch_gemm_bf16(const __nv_bfloat16* A, bool a_mn, const __nv_bfloat16* B, bool b_mn,
+                             __nv_bfloat16* C, int M, int N, int K, uint32_t* status, cudaStream_t st);
+
+// Training-step kernels (train_sm100.cu).
+cudaError_t launch_embed_forward(const int* tok, const __nv_bfloat16* emb, const __nv_bfloat16* pos,
+                                 __nv_bfloat16* out, int rows, int T, int E, cudaStream_t st);
+cudaError_t launch_embed_backward(const int* tok, const __nv_bfloat16* dz, float* demb, __nv_bfloat16* dpos,
+                                  int B, int T, int V, int E, cudaStream_t st);
+cudaError_t launch_layernorm_forward(const __nv_bfloat16* x, __nv_bfloat16* xn, __nv_bfloat16* out,
+                                     const __nv_bfloat16* gamma, const __nv_bfloat16* beta, float* stdev,
+                                     int rows, int cols, float eps, cudaStream_t st);
+cudaError_t launch_layernorm_backward(__nv_bfloat16* dz, const __nv_bfloat16* xn, const __nv_bfloat16* gamma,
+                                      const float* stdev, float* dgamma, float* dbeta, int rows, int cols,
+                                      cudaStream_t st);
+cudaError_t launch_residual_add(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_bfloat16* out, long long n,
+                                cudaStream_t st);
+cudaError_t launch_cast_f32_bf16(const float* in, __nv_bfloat16* out, long long n, cudaStream_t st);
+cudaError_t launch_relu_mask(__nv_bfloat16* v, uint8_t* mask, long long n, cudaStream_t st);
+cudaError_t launch_mask_mul(__nv_bfloat16* dv, const uint8_t* mask, long long n, cudaStream_t st);
+cudaError_t launch_loss_forward(const __nv_bfloat16* x, const int* y, float* out, float* lse, float* mean,
+                                int rows, int cols, cudaStream_t st);
+cudaError_t launch_loss_backward(const __nv_bfloat16* x, const int* y, const float* lse, __nv_bfloat16* dz,
+                                 int rows, int cols, cudaStream_t st);
+cudaError_t launch_adam(float* p, const __nv_bfloat16* g, __nv_bfloat16* m, __nv_bfloat16* v, long long n,
+                        float lr_t, cudaStream_t st);
+cudaError_t launch_gather_f32(const float* src, __nv_bfloat16* dst, long long n, cudaStream_t st);
+cudaError_t launch_scatter(const float* master, __nv_bfloat16* dst, long long n, cudaStream_t st);
+
 }  // namespace ma

@@ -378,6 +378,32 @@ cudaError_t run_gemm(const Operand* A, int na, const Operand* Bop, int nb, void*
 
 }  // namespace
 
+// Generic bf16 GEMM C[M][N] = A . B (bf16 out, fp32 accumulation) for the
+// training step's matmuls (mlp.metal, linear.metal): A is [M][K] (K-major) or
+// [K][M] (a_mn); B is [N][K] (K-major) or [K][N] (b_mn).  64-wide column
+// tiles when 128-wide ones would leave most SMs idle.
+cudaError_t launch_gemm_bf16(const __nv_bfloat16* A, bool a_mn, const __nv_bfloat16* B, bool b_mn,
+                             __nv_bfloat16* C, int M, int N, int K, uint32_t* status, cudaStream_t st) {
+  const Operand a{A, false}, b{B, false};
+  void* c[1] = {C};
+  const bool cf[1] = {false};
+  const bool wide = (long long)((M + 127) / 128) * ((N + 127) / 128) >= 148;
+#define MA_GEMM_CASE(BN_, AM, BMN)                                                               \
+  if (a_mn == AM && b_mn == BMN)                                                                 \
+    return run_gemm<BN_, AM, BMN, false>(&a, 1, &b, 1, c, cf, 1, 1, M, N, K, status, st);
+  if (wide) {
+    MA_GEMM_CASE(128, false, false)
+    MA_GEMM_CASE(128, false, true)
+    MA_GEMM_CASE(128, true, true)
+  } else {
+    MA_GEMM_CASE(64, false, false)
+    MA_GEMM_CASE(64, false, true)
+    MA_GEMM_CASE(64, true, true)
+  }
+#undef MA_GEMM_CASE
+  return cudaErrorInvalidValue;  // A MN-major with B K-major is not needed
+}
+
 // rows = B*M activations rows, n = N (= NH*D)
 cudaError_t launch_proj_forward(const __nv_bfloat16* attn, const __nv_bfloat16* w, __nv_bfloat16* out,
                                 int rows, int n, uint32_t* status, cudaStream_t st) {

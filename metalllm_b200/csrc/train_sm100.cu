@@ -1,0 +1,380 @@
+// train_sm100.cu -- the element-wise, row-wise and optimizer kernels of
+// metalLLM's training step (config 5) around the attention path:
+//   embedForward/Backward  embed.metal:9-34 (+ the positional residualAdd,
+//                          model.h:438; the positional gradient is the batch
+//                          sum of the embedding-output gradient, model.h:284)
+//   layernormForward/Backward  layernorm.metal:10-127
+//   residualAdd, castFloatToBfloat, gather/scatter  elementwise.metal:7-71
+//   ReLU mask of mlpForwardOne / mlpBackwardOne     mlp.metal:20-56, 89-122
+//   lossForward/Backward   loss.metal:9-75 (mean over rows)
+//   MetalStep (Adam)       optimstep.metal:15-42
+// They are memory-bound: 16-byte vector accesses, one warp per row for the
+// row reductions (fp32 math), block partial sums + one atomic per column and
+// block for the LayerNorm parameter gradients.
+#include "common.cuh"
+
+namespace ma {
+namespace {
+
+constexpr int EW_THREADS = 256;
+
+inline int ew_blocks(long long n) {
+  long long b = (n + EW_THREADS - 1) / EW_THREADS;
+  if (b > 148LL * 16) b = 148LL * 16;
+  return (int)(b < 1 ? 1 : b);
+}
+
+__device__ __forceinline__ float bf(__nv_bfloat16 x) { return __bfloat162float(x); }
+__device__ __forceinline__ __nv_bfloat16 tobf(float x) { return __float2bfloat16_rn(x); }
+
+// ---------------------------------------------------------------- embedding
+// out[r] = bf16(E[tok[r]] + P[r % T])   (embedForward then residualAdd)
+__global__ void embed_forward_kernel(const int* __restrict__ tok, const __nv_bfloat16* __restrict__ emb,
+                                     const __nv_bfloat16* __restrict__ pos, __nv_bfloat16* __restrict__ out,
+                                     int rows, int T, int E) {
+  const int r = blockIdx.x;
+  if (r >= rows) return;
+  const __nv_bfloat16* e = emb + (long long)tok[r] * E;
+  const __nv_bfloat16* p = pos + (long long)(r % T) * E;
+  __nv_bfloat16* o = out + (long long)r * E;
+  for (int c = threadIdx.x; c < E; c += blockDim.x) o[c] = tobf(bf(e[c]) + bf(p[c]));
+}
+
+// dEmb[tok[r]] += dZ[r] (fp32 atomics; dEmb zeroed first)
+__global__ void embed_backward_kernel(const int* __restrict__ tok, const __nv_bfloat16* __restrict__ dz,
+                                      float* __restrict__ demb, int rows, int E) {
+  const int r = blockIdx.x;
+  if (r >= rows) return;
+  float* d = demb + (long long)tok[r] * E;
+  const __nv_bfloat16* g = dz + (long long)r * E;
+  for (int c = threadIdx.x; c < E; c += blockDim.x) atomicAdd(d + c, bf(g[c]));
+}
+
+// dPos[t][c] = bf16(sum_b dZ[b*T + t][c])
+__global__ void pos_grad_kernel(const __nv_bfloat16* __restrict__ dz, __nv_bfloat16* __restrict__ dpos,
+                                int B, int T, int E) {
+  const long long n = (long long)T * E;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    float s = 0.0f;
+    for (int b = 0; b < B; ++b) s += bf(dz[(long long)b * n + i]);
+    dpos[i] = tobf(s);
+  }
+}
+
+// ---------------------------------------------------------------- layernorm
+// One warp per row (fp32): mean, variance, stdev = sqrt(var + eps);
+// x_norm = bf16((x - mean) / stdev); out = bf16(gamma * xn + beta) with the
+// unrounded xn (layernorm.metal:10-71).
+__global__ void layernorm_forward_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ xn,
+                                         __nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ gamma,
+                                         const __nv_bfloat16* __restrict__ beta, float* __restrict__ stdev,
+                                         int rows, int cols, float eps) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
+  if (warp >= rows) return;
+  const __nv_bfloat16* xr = x + (long long)warp * cols;
+  float s = 0.0f;
+  for (int c = lane; c < cols; c += 32) s += bf(xr[c]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float mean = s / cols;
+  float v = 0.0f;
+  for (int c = lane; c < cols; c += 32) {
+    const float d = bf(xr[c]) - mean;
+    v += d * d;
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const float sd = sqrtf(v / cols + eps);
+  const float rs = 1.0f / sd;
+  if (lane == 0) stdev[warp] = sd;
+  for (int c = lane; c < cols; c += 32) {
+    const float n = (bf(xr[c]) - mean) * rs;
+    xn[(long long)warp * cols + c] = tobf(n);
+    out[(long long)warp * cols + c] = tobf(bf(gamma[c]) * n + bf(beta[c]));
+  }
+}
+
+// Backward (layernorm.metal:74-127), dZ rewritten in place with dX:
+//   g = dZ * gamma; dX = (g - mean(g) - xn * mean(g * xn)) / stdev;
+//   dGamma += dZ * xn, dBeta += dZ (block partial sums, one atomic per column).
+// One warp per row, WARPS rows per block.
+constexpr int LN_WARPS = 8;
+__global__ void layernorm_backward_kernel(__nv_bfloat16* __restrict__ dz, const __nv_bfloat16* __restrict__ xn,
+                                          const __nv_bfloat16* __restrict__ gamma, const float* __restrict__ stdev,
+                                          float* __restrict__ dgamma, float* __restrict__ dbeta, int rows,
+                                          int cols) {
+  extern __shared__ float red[];  // [2][cols]
+  for (int c = threadIdx.x; c < 2 * cols; c += blockDim.x) red[c] = 0.0f;
+  __syncthreads();
+  const int lane = threadIdx.x % 32, w = threadIdx.x / 32;
+  for (int row = blockIdx.x * LN_WARPS + w; row < rows; row += gridDim.x * LN_WARPS) {
+    __nv_bfloat16* dr = dz + (long long)row * cols;
+    const __nv_bfloat16* nr = xn + (long long)row * cols;
+    float s1 = 0.0f, s2 = 0.0f;
+    for (int c = lane; c < cols; c += 32) {
+      const float d = bf(dr[c]), n = bf(nr[c]), g = d * bf(gamma[c]);
+      s1 += g;
+      s2 += g * n;
+      atomicAdd(&red[c], d * n);
+      atomicAdd(&red[cols + c], d);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+      s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+    }
+    const float m1 = s1 / cols, m2 = s2 / cols, rs = 1.0f / stdev[row];
+    __syncwarp();
+    for (int c = lane; c < cols; c += 32) {
+      const float g = bf(dr[c]) * bf(gamma[c]);
+      dr[c] = tobf(rs * (g - m1 - bf(nr[c]) * m2));
+    }
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+    atomicAdd(dgamma + c, red[c]);
+    atomicAdd(dbeta + c, red[cols + c]);
+  }
+}
+
+// ---------------------------------------------------------------- glue
+__global__ void residual_add_kernel(const uint4* __restrict__ a, const uint4* __restrict__ b,
+                                    uint4* __restrict__ out, long long n8) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8;
+       i += (long long)gridDim.x * blockDim.x) {
+    const uint4 x = a[i], y = b[i];
+    const __nv_bfloat162* xa = reinterpret_cast<const __nv_bfloat162*>(&x);
+    const __nv_bfloat162* ya = reinterpret_cast<const __nv_bfloat162*>(&y);
+    uint4 r;
+    __nv_bfloat162* ra = reinterpret_cast<__nv_bfloat162*>(&r);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 fx = __bfloat1622float2(xa[k]), fy = __bfloat1622float2(ya[k]);
+      ra[k] = __floats2bfloat162_rn(fx.x + fy.x, fx.y + fy.y);
+    }
+    out[i] = r;
+  }
+}
+
+__global__ void cast_kernel(const float4* __restrict__ in, uint2* __restrict__ out, long long n4) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4;
+       i += (long long)gridDim.x * blockDim.x) {
+    const float4 v = in[i];
+    __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+    out[i] = make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+  }
+}
+
+// v = relu(v) in place, mask = (v > 0)   (mlp.metal:45-51)
+__global__ void relu_mask_kernel(__nv_bfloat16* __restrict__ v, uint8_t* __restrict__ mask, long long n) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const float x = bf(v[i]);
+    const bool on = x > 0.0f;
+    mask[i] = on ? 1 : 0;
+    v[i] = on ? v[i] : tobf(0.0f);
+  }
+}
+
+// dV *= mask   (mlp.metal:116-121)
+__global__ void mask_mul_kernel(__nv_bfloat16* __restrict__ dv, const uint8_t* __restrict__ mask, long long n) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x)
+    if (!mask[i]) dv[i] = tobf(0.0f);
+}
+
+// ---------------------------------------------------------------- loss
+// One warp per row: lse = max + ln(sum exp(x - max)); out = lse - x[y]
+// (loss.metal:9-59).
+__global__ void loss_forward_kernel(const __nv_bfloat16* __restrict__ x, const int* __restrict__ y,
+                                    float* __restrict__ out, float* __restrict__ lse, int rows, int cols) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
+  if (warp >= rows) return;
+  const __nv_bfloat16* xr = x + (long long)warp * cols;
+  float m = -INFINITY;
+  for (int c = lane; c < cols; c += 32) m = fmaxf(m, bf(xr[c]));
+#pragma unroll
+  for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  float s = 0.0f;
+  for (int c = lane; c < cols; c += 32) s += expf(bf(xr[c]) - m);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) {
+    const float l = m + logf(s);
+    lse[warp] = l;
+    out[warp] = l - bf(xr[y[warp]]);
+  }
+}
+
+// mean of the per-row losses into *mean (one block, fixed order)
+__global__ void mean_kernel(const float* __restrict__ v, int n, float* __restrict__ mean) {
+  __shared__ float part[32];
+  float s = 0.0f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) s += v[i];
+#pragma unroll
+  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (threadIdx.x % 32 == 0) part[threadIdx.x / 32] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    s = threadIdx.x < (int)(blockDim.x / 32) ? part[threadIdx.x] : 0.0f;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (threadIdx.x == 0) *mean = s / n;
+  }
+}
+
+// dZ = bf16((exp(x - lse) - [c == y]) / rows)   (loss.metal:61-75)
+__global__ void loss_backward_kernel(const __nv_bfloat16* __restrict__ x, const int* __restrict__ y,
+                                     const float* __restrict__ lse, __nv_bfloat16* __restrict__ dz, int rows,
+                                     int cols) {
+  const long long n = (long long)rows * cols;
+  const float inv = 1.0f / rows;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int r = (int)(i / cols), c = (int)(i % cols);
+    const float p = expf(bf(x[i]) - lse[r]);
+    dz[i] = tobf((p - (c == y[r] ? 1.0f : 0.0f)) * inv);
+  }
+}
+
+// ---------------------------------------------------------------- optimizer
+// Adam on the flat fp32 master parameters with bf16 gradients and moments
+// (optimstep.metal:15-42): v = b2 v + (1-b2) g^2; m = b1 m + (1-b1) g;
+// p -= lr_t * m * rsqrt(v + eps).
+__global__ void adam_kernel(float* __restrict__ p, const __nv_bfloat16* __restrict__ g,
+                            __nv_bfloat16* __restrict__ m, __nv_bfloat16* __restrict__ v, long long n,
+                            float b1, float b2, float lr_t, float ob1, float ob2, float eps) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x) {
+    const float gi = bf(g[i]);
+    const float vi = fmaf(b2, bf(v[i]), ob2 * (gi * gi));
+    const float mi = fmaf(b1, bf(m[i]), ob1 * gi);
+    v[i] = tobf(vi);
+    m[i] = tobf(mi);
+    p[i] -= lr_t * mi * rsqrtf(vi + eps);
+  }
+}
+
+__global__ void gather_f32_kernel(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst, long long n) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x)
+    dst[i] = tobf(src[i]);
+}
+
+__global__ void scatter_kernel(const float* __restrict__ master, __nv_bfloat16* __restrict__ dst, long long n) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+       i += (long long)gridDim.x * blockDim.x)
+    dst[i] = tobf(master[i]);
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------- launchers
+cudaError_t launch_embed_forward(const int* tok, const __nv_bfloat16* emb, const __nv_bfloat16* pos,
+                                 __nv_bfloat16* out, int rows, int T, int E, cudaStream_t st) {
+  embed_forward_kernel<<<rows, 128, 0, st>>>(tok, emb, pos, out, rows, T, E);
+  count_launches(1);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_embed_backward(const int* tok, const __nv_bfloat16* dz, float* demb, __nv_bfloat16* dpos,
+                                  int B, int T, int V, int E, cudaStream_t st) {
+  cudaError_t e = cudaMemsetAsync(demb, 0, (size_t)V * E * sizeof(float), st);
+  if (e != cudaSuccess) return e;
+  embed_backward_kernel<<<B * T, 128, 0, st>>>(tok, dz, demb, B * T, E);
+  pos_grad_kernel<<<ew_blocks((long long)T * E), EW_THREADS, 0, st>>>(dz, dpos, B, T, E);
+  count_launches(2);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_layernorm_forward(const __nv_bfloat16* x, __nv_bfloat16* xn, __nv_bfloat16* out,
+                                     const __nv_bfloat16* gamma, const __nv_bfloat16* beta, float* stdev,
+                                     int rows, int cols, float eps, cudaStream_t st) {
+  const int wpb = 8;
+  layernorm_forward_kernel<<<(rows + wpb - 1) / wpb, wpb * 32, 0, st>>>(x, xn, out, gamma, beta, stdev, rows,
+                                                                      cols, eps);
+  count_launches(1);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_layernorm_backward(__nv_bfloat16* dz, const __nv_bfloat16* xn, const __nv_bfloat16* gamma,
+                                      const float* stdev, float* dgamma, float* dbeta, int rows, int cols,
+                                      cudaStream_t st) {
+  cudaError_t e = cudaMemsetAsync(dgamma, 0, (size_t)cols * sizeof(float), st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(dbeta, 0, (size_t)cols * sizeof(float), st);
+  if (e != cudaSuccess) return e;
+  int blocks = (rows + LN_WARPS - 1) / LN_WARPS;
+  if (blocks > 148 * 4) blocks = 148 * 4;
+  layernorm_backward_kernel<<<blocks, LN_WARPS * 32, 2 * cols * sizeof(float), st>>>(dz, xn, gamma, stdev,
+                                                                                       dgamma, dbeta, rows, cols);
+  count_launches(1);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_residual_add(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_bfloat16* out, long long n,
+                                cudaStream_t st) {
+  const long long n8 = n / 8;  // n is a multiple of 64 here
+  residual_add_kernel<<<ew_blocks(n8), EW_THREADS, 0, st>>>(reinterpret_cast<const uint4*>(a),
+                                                            reinterpret_cast<const uint4*>(b),
+                                                            reinterpret_cast<uint4*>(out), n8);
+  count_launches(1);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_cast_f32_bf16(const float* in, __nv_bfloat16* out, long long n, cudaStream_t st) {
+  const long long n4 = n / 4;
+  cast_kernel<<<ew_blocks(n4), EW_THREADS, 0, st>>>(reinterpret_cast<const float4*>(in),
+                                                    reinterpret_cast<uint2*>(out), n4);
+  count_launches(1);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_relu_mask(__nv_bfloat16* v, uint8_t* mask, long long n, cudaStream_t st) {
+  relu_mask_kernel<<<ew_blocks(n), EW_THREADS, 0, st>>>(v, mask, n);
+  count_launches(1);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_mask_mul(__nv_bfloat16* dv, const uint8_t* mask, long long n, cudaStream_t st) {
+  mask_mul_kernel<<<ew_blocks(n), EW_THREADS, 0, st>>>(dv, mask, n);
+  count_launches(1);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_loss_forward(const __nv_bfloat16* x, const int* y, float* out, float* lse, float* mean,
+                                int rows, int cols, cudaStream_t st) {
+  const int wpb = 8;
+  loss_forward_kernel<<<(rows + wpb - 1) / wpb, wpb * 32, 0, st>>>(x, y, out, lse, rows, cols);
+  mean_kernel<<<1, 1024, 0, st>>>(out, rows, mean);
+  count_launches(2);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_loss_backward(const __nv_bfloat16* x, const int* y, const float* lse, __nv_bfloat16* dz,
+                                 int rows, int cols, cudaStream_t st) {
+  loss_backward_kernel<<<ew_blocks((long long)rows * cols), EW_THREADS, 0, st>>>(x, y, lse, dz, rows, cols);
+  count_launches(1);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_adam(float* p, const __nv_bfloat16* g, __nv_bfloat16* m, __nv_bfloat16* v, long long n,
+                        float lr_t, cudaStream_t st) {
+  adam_kernel<<<ew_blocks(n), EW_THREADS, 0, st>>>(p, g, m, v, n, 0.9f, 0.999f, lr_t, 0.1f, 0.001f, 1e-8f);
+  count_launches(1);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gather_f32(const float* src, __nv_bfloat16* dst, long long n, cudaStream_t st) {
+  gather_f32_kernel<<<ew_blocks(n), EW_THREADS, 0, st>>>(src, dst, n);
+  count_launches(1);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_scatter(const float* master, __nv_bfloat16* dst, long long n, cudaStream_t st) {
+  scatter_kernel<<<ew_blocks(n), EW_THREADS, 0, st>>>(master, dst, n);
+  count_launches(1);
+  return cudaGetLastError();
+}
+
+}  // namespace ma

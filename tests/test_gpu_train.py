@@ -1,0 +1,115 @@
+"""GPU training step (config-5 model, model.h's Model on CUDA) against the
+numpy oracle of one step (oracle/train_oracle.py): forward loss and logits,
+every parameter gradient, and the Adam update, on a small 2-layer model;
+then a full config-5 step (B=64, T=256, E=384, 6 heads, 6 layers).
+
+Tolerances: the loss within 2e-2 absolute (about 0.4 % of ln 128); logits
+and gradients within relative-L2 3e-2 (bf16 activations through two layers,
+fp32 atomics in a different order); the Adam update within 1e-6 of the
+oracle's update computed from the GPU's own gradients."""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from metalllm_b200.inputs import bf16_bits_to_f32  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+SMALL = dict(B=2, T=64, E=128, NH=2, layers=2, mlp_scale=2, vocab=128)
+
+
+@pytest.fixture(scope="module")
+def T():
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    from metalllm_b200.build import build_cuda
+    build_cuda()
+    from metalllm_b200 import train
+    return train
+
+
+def _shapes(c):
+    E, H, V, T_ = c["E"], c["E"] * c["mlp_scale"], c["vocab"], c["T"]
+    s = {"embed": (V, E), "pos": (T_, E), "lnf_gamma": (E,), "lnf_beta": (E,), "linw": (E, V)}
+    for n in range(c["layers"]):
+        s.update({f"layer{n}.ln1_gamma": (E,), f"layer{n}.ln1_beta": (E,), f"layer{n}.qw": (E, E),
+                  f"layer{n}.kw": (E, E), f"layer{n}.vw": (E, E), f"layer{n}.projw": (E, E),
+                  f"layer{n}.ln2_gamma": (E,), f"layer{n}.ln2_beta": (E,), f"layer{n}.up": (E, H),
+                  f"layer{n}.dp": (H, E)})
+    return s
+
+
+def _rl2(a, b):
+    a = np.asarray(a, np.float64).ravel()
+    b = np.asarray(b, np.float64).ravel()
+    return np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30)
+
+
+def _grad(model, name):
+    g = model.read("grad." + name)
+    return g if g.dtype == np.float32 else bf16_bits_to_f32(g)
+
+
+def test_small_model_step_matches_oracle(T):
+    from oracle import train_oracle as O
+    c = SMALL
+    model = T.TrainingModel(**c, seed=3)
+    shapes = _shapes(c)
+    assert set(model.param_names()) == set(shapes)
+    W = {n: bf16_bits_to_f32(model.read(n)).reshape(s) for n, s in shapes.items()}
+    rng = np.random.default_rng(0)
+    tok = rng.integers(0, c["vocab"], (c["B"], c["T"])).astype(np.int32)
+    tgt = rng.integers(0, c["vocab"], (c["B"], c["T"])).astype(np.int32)
+    ttok, ttgt = torch.from_numpy(tok).cuda(), torch.from_numpy(tgt).cuda()
+    model.forward(ttok, ttgt)
+    loss = model.loss()
+    # the oracle takes the GPU's ReLU masks: pre-activations within rounding
+    # of zero may take the other sign there and flip whole gradient entries
+    H = c["E"] * c["mlp_scale"]
+    masks = [model.read(f"layer{n}.mask").reshape(-1, H).astype(bool) for n in range(c["layers"])]
+    ref_loss, ref_logits, G = O.forward_backward(W, tok, tgt, c["B"], c["T"], c["NH"], c["layers"],
+                                                 masks=masks)
+    assert abs(loss - ref_loss) <= 2e-2, (loss, ref_loss)
+    logits = bf16_bits_to_f32(model.read("logits")).reshape(ref_logits.shape)
+    assert _rl2(logits, ref_logits) <= 3e-2
+    model.backward()
+    bad = {n: _rl2(_grad(model, n), G[n]) for n in shapes}
+    assert max(bad.values()) <= 3e-2, sorted(bad.items(), key=lambda kv: -kv[1])[:5]
+    # Adam step 1 from the GPU's own gradients (bf16 as gathered)
+    master0 = model.read("master").copy()
+    grads = {n: _grad(model, n) for n in shapes}
+    model.step()
+    master1 = model.read("master")
+    off = 0
+    for n in model.param_names():
+        cnt = int(np.prod(shapes[n]))
+        p, _, _ = O.adam(master0[off:off + cnt], O.r16(grads[n]), np.float32(0), np.float32(0), 1, 0.003)
+        assert np.abs(master1[off:off + cnt] - p).max() <= 1e-6, n
+        w = bf16_bits_to_f32(model.read(n))
+        assert np.array_equal(w, O.r16(master1[off:off + cnt])), n
+        off += (cnt + 7) & ~7
+    assert model.status() == 0
+    # a few more steps on the same batch lower the loss
+    losses = [loss]
+    for _ in range(4):
+        model.train_step(ttok, ttgt)
+        losses.append(model.loss())
+    assert losses[-1] < losses[0] - 0.05, losses
+    model.close()
+
+
+def test_config5_step(T):
+    c = dict(B=64, T=256, E=384, NH=6, layers=6, mlp_scale=2, vocab=128)
+    model = T.TrainingModel(**c, seed=0)
+    rng = np.random.default_rng(1)
+    tok = torch.from_numpy(rng.integers(0, 128, (64, 256)).astype(np.int32)).cuda()
+    tgt = torch.from_numpy(rng.integers(0, 128, (64, 256)).astype(np.int32)).cuda()
+    model.train_step(tok, tgt)
+    l0 = model.loss()
+    assert abs(l0 - np.log(128)) < 0.5, l0
+    for _ in range(3):
+        model.train_step(tok, tgt)
+    assert model.loss() < l0
+    assert model.status() == 0
+    model.close()

@@ -230,3 +230,45 @@ def test_oracle_gemms_match_numpy(oracle_mod):
     dx_s = o.grad_dx(qw, kw, vw, dq, dk, dv, rows=rows)
     assert np.array_equal(dx_s[rows], dx[rows])
     assert np.isnan(np.delete(dx_s, rows, axis=0)).all()
+
+
+def test_train_oracle_gradients_match_finite_differences():
+    """The training-step oracle's backward (oracle/train_oracle.py), with its
+    bf16 rounding switched off and in float64, agrees with central finite
+    differences of its own loss on a tiny model."""
+    from oracle import train_oracle as O
+    saved = O.r16, O.FLOAT
+    O.r16 = lambda x: np.asarray(x, np.float64)
+    O.FLOAT = np.float64
+    try:
+        B, T, E, NH, L, V, H = 2, 8, 16, 2, 1, 12, 32
+        rng = np.random.default_rng(0)
+        W = {"embed": rng.normal(0, 0.5, (V, E)), "pos": rng.normal(0, 0.5, (T, E)),
+             "lnf_gamma": 1 + rng.normal(0, 0.1, E), "lnf_beta": rng.normal(0, 0.1, E),
+             "linw": rng.normal(0, 0.3, (E, V))}
+        for k, s in (("ln1_gamma", E), ("ln2_gamma", E)):
+            W[f"layer0.{k}"] = 1 + rng.normal(0, 0.1, s)
+        for k, s in (("ln1_beta", E), ("ln2_beta", E)):
+            W[f"layer0.{k}"] = rng.normal(0, 0.1, s)
+        for k, s in (("qw", (E, E)), ("kw", (E, E)), ("vw", (E, E)), ("projw", (E, E)),
+                     ("up", (E, H)), ("dp", (H, E))):
+            W[f"layer0.{k}"] = rng.normal(0, 0.3, s)
+        tok = rng.integers(0, V, (B, T))
+        tgt = rng.integers(0, V, (B, T))
+        _, _, G = O.forward_backward(W, tok, tgt, B, T, NH, L)
+        for name in ("layer0.qw", "layer0.up", "layer0.ln1_gamma", "linw", "embed", "pos",
+                     "layer0.kw", "layer0.vw", "layer0.projw", "lnf_beta"):
+            for _ in range(3):
+                idx = tuple(rng.integers(0, d) for d in W[name].shape)
+                if name == "embed":
+                    idx = (int(tok[0, 0]),) + idx[1:]
+                h = 1e-5
+                W[name][idx] += h
+                lp = O.forward_backward(W, tok, tgt, B, T, NH, L)[0]
+                W[name][idx] -= 2 * h
+                lm = O.forward_backward(W, tok, tgt, B, T, NH, L)[0]
+                W[name][idx] += h
+                fd = (lp - lm) / (2 * h)
+                assert abs(fd - G[name][idx]) <= 1e-5 + 1e-4 * abs(fd), (name, idx, fd, G[name][idx])
+    finally:
+        O.r16, O.FLOAT = saved
