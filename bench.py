@@ -463,6 +463,114 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------- config-5 training step
+def run_train(args):
+    """Config 5 (BASELINE): one metalLLM training iteration -- forward,
+    backward and Adam over B=64 sequences of T=256, E=384, 6 heads of 64,
+    6 layers, MLP x2, vocabulary 128 -- in ms/iter, eager (one launch per
+    kernel) and replayed from a CUDA graph, plus the share of the attention
+    kernels measured standalone on the same shapes."""
+    import numpy as np
+    import torch
+    rank = env_int("RANK", 0)
+    if rank != 0:  # a single-GPU workload: replicas only, rank 0 reports
+        return
+    torch.cuda.set_device(env_int("LOCAL_RANK", 0))
+    from metalllm_b200 import attention as A
+    from metalllm_b200 import train as T
+    from metalllm_b200._lib import load
+    B, Tn, E, NH, L, S, V = 64, 256, 384, 6, 6, 2, 128
+    model = T.TrainingModel(B, Tn, E, NH, L, S, V, lr=0.003, seed=args.seed)
+    rng = np.random.default_rng(args.seed)
+    tok = torch.from_numpy(rng.integers(0, V, (B, Tn)).astype(np.int32)).cuda()
+    tgt = torch.from_numpy(rng.integers(0, V, (B, Tn)).astype(np.int32)).cuda()
+    lib = load()
+    for _ in range(args.warmup):
+        model.train_step(tok, tgt)
+    torch.cuda.synchronize()
+    loss0 = model.loss()
+
+    def timed(fn, k):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(k):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / k
+
+    props = torch.cuda.get_device_properties(torch.cuda.current_device())
+    sampler = ClockSampler(f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0")
+    n0 = lib.ma_kernel_launch_count()
+    sampler.start()
+    eager_ms = timed(lambda: model.train_step(tok, tgt), args.steps)
+    clocks = sampler.stop()
+    launches = (lib.ma_kernel_launch_count() - n0) // args.steps
+    loss1 = model.loss()
+    graph = {}
+    try:
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            model.train_step(tok, tgt)
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            model.train_step(tok, tgt)
+        for _ in range(args.warmup):
+            g.replay()
+        graph = {"ms_per_iter": round(timed(g.replay, args.steps), 4),
+                 "note": "whole step captured once and replayed (the Adam bias correction of the "
+                         "captured step is reused)"}
+    except Exception as e:  # capture unsupported by something in the step
+        graph = {"error": str(e)[:200]}
+    # attention share: the attention kernels of one layer, standalone, x layers
+    p = A.make_params(Tn, NH, E // NH)
+    mk = lambda: torch.randn(B, Tn, E, device="cuda").to(torch.bfloat16)
+    q, k, v, do, x = mk(), mk(), mk(), mk(), mk()
+    w = [(torch.randn(E, E, device="cuda") * 0.05).to(torch.bfloat16) for _ in range(4)]
+    out, l = A.flashAttentionForward(q, k, v, p, B)
+    Dv = A.computeD(do, out, p, B)
+    dQ, dK, dV = A.flashAttentionBackward(do, Dv, l, q, k, v, p, B)
+    core = lambda: (A.flashAttentionForward(q, k, v, p, B, out=out, l=l),
+                    A.computeD(do, out, p, B, D=Dv),
+                    A.flashAttentionBackward(do, Dv, l, q, k, v, p, B, dQ=dQ, dK=dK, dV=dV))
+    rest = lambda: (A.computeQKV(x, w[0], w[1], w[2], p, B), A.projForward(out, w[3], p, B),
+                    A.projBackwarddW(out, do, p, B), A.projBackwarddX(do, w[3], p, B),
+                    A.computeGradDx(w[0], w[1], w[2], dQ, dK, dV, p, B),
+                    A.computeGradDw(x, dQ, dK, dV, p, B))
+    for _ in range(3):
+        core(); rest()
+    core_ms = timed(core, 20) * L
+    block_ms = core_ms + timed(rest, 20) * L
+    step_ms = eager_ms
+    flops = L * 7.0 * B * NH * Tn * Tn * (E // NH)   # causal attention core, fwd + bwd
+    line = {
+        "metric": "config-5 training step ms/iter (forward + backward + Adam), attention share",
+        "value": round(eager_ms, 4), "unit": "ms/iter", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(eager_ms, 4), "higher_is_better": False,
+        "scaling": "replicas only", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: tokens and targets uniform in [0, 128), weights initialised as main.cpp",
+        "config": {"workload": "c5: 6-layer metalLLM training step", "B": B, "T": Tn, "E": E,
+                   "heads": NH, "d": E // NH, "layers": L, "mlp_scale": S, "vocab": V},
+        "graph": graph, "gpu_launches": int(launches),
+        "attention_share": {
+            "core_ms": round(core_ms, 4), "core_share": round(core_ms / step_ms, 4),
+            "core_tflops": round(flops / (core_ms * 1e-3) / 1e12, 2),
+            "block_ms": round(block_ms, 4), "block_share": round(block_ms / step_ms, 4),
+            "note": "flashAttentionForward + computeD + flashAttentionBackward (core) and with "
+                    "computeQKV, projForward/BackwarddW/dX, computeGradDx/Dw (block), timed "
+                    "standalone on the step's shapes, times the 6 layers, over the eager step"},
+        "loss": {"after_warmup": round(loss0, 4), "after_timed": round(loss1, 4)},
+        "clocks": clocks,
+        "reference": "published: ~13 ms/iter for this model at B=1 on an M4 MacBook Air "
+                     "(README.md:5,121); not comparable hardware",
+    }
+    print(json.dumps(line), flush=True)
+    model.close()
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -479,10 +587,14 @@ def main():
                          "(batch, head) shards are split over the GPUs")
     ap.add_argument("--batch", type=int, default=0,
                     help="override the config's batch (smaller profiling case)")
+    ap.add_argument("--train", action="store_true",
+                    help="time the config-5 training step instead of an attention config")
     args = ap.parse_args()
     # at least 3 untimed warm-up steps, whatever the caller asks for
     args.warmup = max(args.warmup, 3)
-    if args.impl == "reference":
+    if args.train:
+        run_train(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_gpu(args)
