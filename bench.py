@@ -561,7 +561,9 @@ def run_train(args):
             "block_ms": round(block_ms, 4), "block_share": round(block_ms / step_ms, 4),
             "note": "flashAttentionForward + computeD + flashAttentionBackward (core) and with "
                     "computeQKV, projForward/BackwarddW/dX, computeGradDx/Dw (block), timed "
-                    "standalone on the step's shapes, times the 6 layers, over the eager step"},
+                    "standalone on the step's shapes, times the 6 layers, over the eager step; "
+                    "the block figure uses the public single-pass weight-gradient entry points, "
+                    "slower than the model's split-K path, so it is an upper bound"},
         "loss": {"after_warmup": round(loss0, 4), "after_timed": round(loss1, 4)},
         "clocks": clocks,
         "reference": "published: ~13 ms/iter for this model at B=1 on an M4 MacBook Air "

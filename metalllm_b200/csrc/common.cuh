@@ -67,6 +67,11 @@ cudaError_t launch_grad_dw(const __nv_bfloat16* x, const float* dq, const __nv_b
 
 cudaError_t launch_gemm_bf16(const __nv_bfloat16* A, bool a_mn, const __nv_bfloat16* B, bool b_mn,
                              __nv_bfloat16* C, int M, int N, int K, uint32_t* status, cudaStream_t st);
+cudaError_t launch_gemm_splitk_f32(const __nv_bfloat16* A, const __nv_bfloat16* B, float* C, int M, int N,
+                                   int K, uint32_t* status, cudaStream_t st);
+cudaError_t launch_grad_dw_splitk(const __nv_bfloat16* x, const float* dq, const __nv_bfloat16* dk,
+                                  const __nv_bfloat16* dv, float* dqw, __nv_bfloat16* dkw, __nv_bfloat16* dvw,
+                                  float* ws, int rows, int n, uint32_t* status, cudaStream_t st);
 
 // Training-step kernels (train_sm100.cu).
 cudaError_t launch_embed_forward(const int* tok, const __nv_bfloat16* emb, const __nv_bfloat16* pos,

@@ -55,6 +55,8 @@ struct GemmArgs {
   uint32_t a_f32;     // bit i: a[i] is fp32 (converted to bf16 on chip)
   uint32_t b_f32;
   uint32_t c_f32;     // bit z: output z is fp32 (else bf16)
+  int ksplit;         // split-K: grid.z = outputs * ksplit; partials are added (fp32 outputs)
+  int kchunk;         // K steps per split
   uint32_t* status;
 };
 
@@ -86,8 +88,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t sbase = (raw + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (sbase - raw);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int row0 = blockIdx.x * BM, col0 = blockIdx.y * BN, z = blockIdx.z;
-  const int nk = (args.K + BK - 1) / BK;
+  const int row0 = blockIdx.x * BM, col0 = blockIdx.y * BN;
+  const int z = blockIdx.z / args.ksplit, kz = blockIdx.z % args.ksplit;
+  // split-K: this CTA sweeps K steps [kbeg, kbeg + nk) of its output (nseg == 1)
+  const int nk_all = (args.K + BK - 1) / BK;
+  const int kbeg = kz * args.kchunk;
+  const int nk = args.ksplit > 1 ? min(args.kchunk, nk_all - kbeg) : nk_all;
   const int nsteps = args.nseg * nk;
 
   const uint32_t bar0 = sbase + C::OFF_BAR;
@@ -129,7 +135,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int s = 0; s < nsteps; ++s) {
         const int st = s % C::STAGES;
         if (s >= C::STAGES && !mbar_wait(BAR_E(st), ((s / C::STAGES) - 1) & 1, abort_p)) break;
-        const int ai = a_index(s), bi = b_index(s), k0 = (s % nk) * BK;
+        const int ai = a_index(s), bi = b_index(s), k0 = (kbeg * (args.ksplit > 1) + s % nk) * BK;
         const bool af = HAS_F32 && bit_of(args.a_f32, ai), bf = HAS_F32 && bit_of(args.b_f32, bi);
         const uint32_t sa = sbase + st * C::STAGE_BYTES;
         const uint32_t sb = sa + C::A_BYTES;
@@ -291,7 +297,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     ok = bar_red_and(1, 128, ok);
     if (ok && leader) {
       const CUtensorMap* cm = &maps.c[z];
-      if (out_f32) {
+      if (args.ksplit > 1) {  // fp32 partial sums added into the (zeroed) output
+        for (int b = 0; b < BN / 32; ++b) tma_reduce_add_2d(cm, sbase + b * (BM * 128), col0 + 32 * b, row0);
+      } else if (out_f32) {
         for (int b = 0; b < BN / 32; ++b) tma_store_2d(cm, sbase + b * (BM * 128), col0 + 32 * b, row0);
       } else {
         for (int b = 0; b < BN / 64; ++b) tma_store_2d(cm, sbase + b * (BM * 128), col0 + 64 * b, row0);
@@ -333,7 +341,7 @@ bool make_operand_map(CUtensorMap* m, const Operand& o, bool mn_major, uint64_t 
 template <int BN, bool A_MN, bool B_MN, bool HAS_F32>
 cudaError_t run_gemm(const Operand* A, int na, const Operand* Bop, int nb, void* const* Cptr,
                      const bool* c_f32, int nz, int nseg, int M, int N, int K, uint32_t* status,
-                     cudaStream_t st) {
+                     cudaStream_t st, int ksplit = 1) {
   using Cfg = GemmCfg<BN, HAS_F32>;
   GemmMaps maps;
   memset(&maps, 0, sizeof(maps));
@@ -345,6 +353,16 @@ cudaError_t run_gemm(const Operand* A, int na, const Operand* Bop, int nb, void*
   args.na = na;
   args.nb = nb;
   args.status = status;
+  // split-K only for single-segment products with fp32 outputs (the partial
+  // sums are added by TMA reductions into outputs the caller has zeroed)
+  const int nk_all = (K + BK - 1) / BK;
+  if (ksplit < 1 || nseg > 1) ksplit = 1;
+  if (ksplit > nk_all) ksplit = nk_all;
+  args.kchunk = (nk_all + ksplit - 1) / ksplit;
+  args.ksplit = (nk_all + args.kchunk - 1) / args.kchunk;
+  if (args.ksplit > 1)
+    for (int i = 0; i < nz; ++i)
+      if (!c_f32[i]) return cudaErrorInvalidValue;
   for (int i = 0; i < na; ++i) {
     if (A[i].f32) args.a_f32 |= 1u << i;
     if (!make_operand_map(&maps.a[i], A[i], A_MN, M, K, BM)) return cudaErrorInvalidValue;
@@ -370,7 +388,7 @@ cudaError_t run_gemm(const Operand* A, int na, const Operand* Bop, int nb, void*
   auto kern = gemm_kernel<BN, A_MN, B_MN, HAS_F32>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
   if (e != cudaSuccess) return e;
-  const dim3 grid((M + BM - 1) / BM, (N + BN - 1) / BN, nz);
+  const dim3 grid((M + BM - 1) / BM, (N + BN - 1) / BN, nz * args.ksplit);
   kern<<<grid, NUM_THREADS, Cfg::SMEM_BYTES, st>>>(maps, args);
   count_launches(1);
   return cudaGetLastError();
@@ -402,6 +420,48 @@ cudaError_t launch_gemm_bf16(const __nv_bfloat16* A, bool a_mn, const __nv_bfloa
   }
 #undef MA_GEMM_CASE
   return cudaErrorInvalidValue;  // A MN-major with B K-major is not needed
+}
+
+// Split-K GEMM into an fp32 output (zeroed here): C[M][N] = A . B with both
+// operands MN-major ([K][M], [K][N]); used for weight gradients, whose K (the
+// B*T activation rows) is long and whose M x N is small.  Enough K chunks to
+// give about two CTAs per SM.
+int pick_ksplit(int tiles, int K) {
+  const int nk = (K + BK - 1) / BK;
+  int s = (296 + tiles - 1) / tiles;
+  if (s > nk / 4) s = nk / 4;  // at least 4 K steps per chunk
+  return s < 1 ? 1 : s;
+}
+
+cudaError_t launch_gemm_splitk_f32(const __nv_bfloat16* A, const __nv_bfloat16* B, float* C, int M, int N,
+                                   int K, uint32_t* status, cudaStream_t st) {
+  cudaError_t e = cudaMemsetAsync(C, 0, (size_t)M * N * sizeof(float), st);
+  if (e != cudaSuccess) return e;
+  const Operand a{A, false}, b{B, false};
+  void* c[1] = {C};
+  const bool cf[1] = {true};
+  const int tiles = ((M + 127) / 128) * ((N + 63) / 64);
+  return run_gemm<64, true, true, false>(&a, 1, &b, 1, c, cf, 1, 1, M, N, K, status, st,
+                                         pick_ksplit(tiles, K));
+}
+
+// computeGradDw with split-K: dQw (fp32) and the two bf16 gradients, the
+// latter accumulated in an fp32 workspace of 2*n*n floats and then rounded.
+cudaError_t launch_grad_dw_splitk(const __nv_bfloat16* x, const float* dq, const __nv_bfloat16* dk,
+                                  const __nv_bfloat16* dv, float* dqw, __nv_bfloat16* dkw, __nv_bfloat16* dvw,
+                                  float* ws, int rows, int n, uint32_t* status, cudaStream_t st) {
+  cudaError_t e = cudaMemsetAsync(dqw, 0, (size_t)n * n * sizeof(float), st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(ws, 0, (size_t)2 * n * n * sizeof(float), st);
+  if (e != cudaSuccess) return e;
+  const Operand a{x, false};
+  const Operand b[3] = {{dq, true}, {dk, false}, {dv, false}};
+  void* c[3] = {dqw, ws, ws + (size_t)n * n};
+  const bool cf[3] = {true, true, true};
+  const int tiles = 3 * ((n + 127) / 128) * ((n + 63) / 64);
+  e = run_gemm<64, true, true, true>(&a, 1, b, 3, c, cf, 3, 1, n, n, rows, status, st, pick_ksplit(tiles, rows));
+  if (e == cudaSuccess) e = launch_cast_f32_bf16(ws, dkw, (long long)n * n, st);
+  if (e == cudaSuccess) e = launch_cast_f32_bf16(ws + (size_t)n * n, dvw, (long long)n * n, st);
+  return e;
 }
 
 // rows = B*M activations rows, n = N (= NH*D)

@@ -8,6 +8,7 @@
 // element-wise kernels and the tcgen05 GEMM for the MLP and the vocabulary
 // projection.  Nothing synchronises the host, so a whole step can be captured
 // into a CUDA graph once the model has run one step.
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <random>
@@ -60,6 +61,7 @@ struct ma_model {
   __nv_bfloat16 *dstream = nullptr, *dbranch = nullptr, *dzattn = nullptr, *dattnd = nullptr;
   __nv_bfloat16 *dk = nullptr, *dv = nullptr, *dmlpv = nullptr, *dpos = nullptr, *dlinw = nullptr;
   float *dq = nullptr, *dxattn = nullptr, *demb = nullptr;
+  float* ws = nullptr;  // fp32 workspace of the split-K weight-gradient GEMMs
   float *loss_rows = nullptr, *lse_rows = nullptr, *loss_mean = nullptr;
   const int* tokens = nullptr;   // last forward's inputs (device)
   const int* targets = nullptr;
@@ -241,6 +243,7 @@ int ma_model_create(const MaModelConfig* c, ma_model** out) {
   ALLOC(m->dv, R * E);
   ALLOC(m->dxattn, R * E);
   ALLOC(m->dmlpv, R * H);
+  ALLOC(m->ws, std::max(std::max(E * H, 2 * E * E), E * V));
   ALLOC(m->loss_rows, R);
   ALLOC(m->lse_rows, R);
   ALLOC(m->loss_mean, 1);
@@ -314,6 +317,15 @@ int ma_model_forward(ma_model* m, const int32_t* tokens, const int32_t* targets,
   return MA_OK;
 }
 
+// Weight gradient G[M][N] = X^T . Y over all B*T rows (X [rows][M], Y
+// [rows][N], bf16): split-K into the fp32 workspace, then rounded to bf16.
+static cudaError_t wgrad(ma_model* m, const __nv_bfloat16* X, const __nv_bfloat16* Y, __nv_bfloat16* G, int M,
+                         int N, cudaStream_t st) {
+  cudaError_t e = ma::launch_gemm_splitk_f32(X, Y, m->ws, M, N, m->R, m->status, st);
+  if (e == cudaSuccess) e = ma::launch_cast_f32_bf16(m->ws, G, (long long)M * N, st);
+  return e;
+}
+
 int ma_model_backward(ma_model* m, ma_stream_t stream) {
   using namespace ma;
   if (!m || !m->tokens) return merr(MA_ERR_NULL, "backward before forward");
@@ -324,8 +336,7 @@ int ma_model_backward(ma_model* m, ma_stream_t stream) {
   // linearBackward: dStream = dLogits . W^T ; dW = lnf.out^T . dLogits
   MA_M_CUDA(launch_gemm_bf16(m->dlogits, false, m->linw, false, m->dstream, R, E, V, m->status, st),
             "linearBackward dX");
-  MA_M_CUDA(launch_gemm_bf16(m->lnf.out, true, m->dlogits, true, m->dlinw, E, V, R, m->status, st),
-            "linearBackward dW");
+  MA_M_CUDA(wgrad(m, m->lnf.out, m->dlogits, m->dlinw, E, V, st), "linearBackward dW");
   MA_M_CUDA(launch_layernorm_backward(m->dstream, m->lnf.xn, m->lnf.gamma, m->lnf.stdev, m->lnf.dgamma,
                                       m->lnf.dbeta, R, E, st), "layernormBackward");
   for (int n = m->L - 1; n >= 0; --n) {
@@ -335,25 +346,23 @@ int ma_model_backward(ma_model* m, ma_stream_t stream) {
     MA_M_CUDA(launch_gemm_bf16(m->dstream, false, y.dp, false, m->dmlpv, R, H, E, m->status, st),
               "mlpBackwardOne");
     MA_M_CUDA(launch_mask_mul(m->dmlpv, y.mask, (long long)R * H, st), "mlpBackwardOne mask");
-    MA_M_CUDA(launch_gemm_bf16(y.ln2.out, true, m->dmlpv, true, y.dup, E, H, R, m->status, st),
-              "mlpBackwardTwo dUp");
-    MA_M_CUDA(launch_gemm_bf16(y.mlp_v, true, m->dstream, true, y.ddp, H, E, R, m->status, st),
-              "mlpBackwardTwo dDp");
+    MA_M_CUDA(wgrad(m, y.ln2.out, m->dmlpv, y.dup, E, H, st), "mlpBackwardTwo dUp");
+    MA_M_CUDA(wgrad(m, y.mlp_v, m->dstream, y.ddp, H, E, st), "mlpBackwardTwo dDp");
     MA_M_CUDA(launch_gemm_bf16(m->dmlpv, false, y.up, false, m->dbranch, R, E, H, m->status, st),
               "mlpBackwardTwo dX");
     MA_M_CUDA(launch_layernorm_backward(m->dbranch, y.ln2.xn, y.ln2.gamma, y.ln2.stdev, y.ln2.dgamma,
                                         y.ln2.dbeta, R, E, st), "layernormBackward");
     MA_M_CUDA(launch_residual_add(m->dbranch, m->dstream, m->dbranch, (long long)R * E, st), "residualAdd");
     // attention block
-    MA_M_CUDA(launch_proj_backward_dw(y.attn, m->dbranch, y.dprojw, R, E, m->status, st), "projBackwarddW");
+    MA_M_CUDA(wgrad(m, y.attn, m->dbranch, y.dprojw, E, E, st), "projBackwarddW");
     MA_M_CUDA(launch_proj_backward_dx(m->dbranch, y.projw, m->dzattn, R, E, m->status, st), "projBackwarddX");
     MA_M_CUDA(launch_compute_d(m->dzattn, y.attn, m->dattnd, s, st), "computeD");
     MA_M_CUDA(launch_flash_bwd(m->dzattn, m->dattnd, y.l, y.q, y.k, y.v, m->dq, m->dk, m->dv, s, m->status, st),
               "flashAttentionBackward");
     MA_M_CUDA(launch_grad_dx(m->dxattn, y.qw, y.kw, y.vw, m->dq, m->dk, m->dv, R, E, m->status, st),
               "computeGradDx");
-    MA_M_CUDA(launch_grad_dw(y.ln1.out, m->dq, m->dk, m->dv, y.dqw, y.dkw, y.dvw, R, E, m->status, st),
-              "computeGradDw");
+    MA_M_CUDA(launch_grad_dw_splitk(y.ln1.out, m->dq, m->dk, m->dv, y.dqw, y.dkw, y.dvw, m->ws, R, E,
+                                    m->status, st), "computeGradDw");
     MA_M_CUDA(launch_cast_f32_bf16(m->dxattn, m->dstream, (long long)R * E, st), "castFloatToBfloat");
     MA_M_CUDA(launch_layernorm_backward(m->dstream, y.ln1.xn, y.ln1.gamma, y.ln1.stdev, y.ln1.dgamma,
                                         y.ln1.dbeta, R, E, st), "layernormBackward");
