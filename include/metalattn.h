@@ -142,6 +142,16 @@ MA_API int ma_projBackwarddW(const ma_bf16* attn_out, const ma_bf16* dZ, ma_bf16
 MA_API int ma_projBackwarddX(const ma_bf16* dZ, const ma_bf16* proj_w, ma_bf16* dAttn,
                              const AttentionParams* p, uint32_t B, ma_stream_t stream);
 
+/* projBackwarddX with computeD fused into the GEMM epilogue: dAttn as
+ * ma_projBackwarddX, and D as ma_computeD(dAttn, attn_out) computed from the
+ * tile while it is on chip (the bf16-rounded dAttn values, fp32 sums, one
+ * bf16 rounding), which saves computeD's launch and its read of dAttn.
+ * Needs the attention shape (D in {64, 128}).  Replaces the pair of
+ * dispatches at model.h:629-647 (attention.metal:432-455 then 166-195). */
+MA_API int ma_projBackwarddXComputeD(const ma_bf16* dZ, const ma_bf16* proj_w, ma_bf16* dAttn,
+                                     const ma_bf16* attn_out, ma_bf16* D, const AttentionParams* p,
+                                     uint32_t B, ma_stream_t stream);
+
 /* computeGradDx: dX = dQ * Wq^T + dK * Wk^T + dV * Wv^T, fp32 (dQ fp32, the
  * rest bf16; dQ enters the tensor core rounded to bf16).  Replaces
  * attention.metal:301-342 (buffers 0..7) dispatched at model.h:666-678. */

@@ -53,6 +53,7 @@ SIGNATURES = {
     "ma_projForward": [_P, _P, _P, _PP, _U32, _P],
     "ma_projBackwarddW": [_P, _P, _P, _PP, _U32, _P],
     "ma_projBackwarddX": [_P, _P, _P, _PP, _U32, _P],
+    "ma_projBackwarddXComputeD": [_P, _P, _P, _P, _P, _PP, _U32, _P],
     "ma_computeGradDx": [_P, _P, _P, _P, _P, _P, _P, _PP, _U32, _P],
     "ma_computeGradDw": [_P, _P, _P, _P, _P, _P, _P, _PP, _U32, _P],
     "ma_device_status": [ctypes.POINTER(ctypes.c_uint32), _P],

@@ -121,6 +121,23 @@ def projBackwarddX(dZ: torch.Tensor, proj_w: torch.Tensor, p: AttentionParams, B
     return dAttn
 
 
+def projBackwarddXComputeD(dZ: torch.Tensor, proj_w: torch.Tensor, attn_out: torch.Tensor,
+                           p: AttentionParams, B: int, dAttn: Optional[torch.Tensor] = None,
+                           D: Optional[torch.Tensor] = None,
+                           stream: Optional[torch.cuda.Stream] = None):
+    """dAttn = dZ . proj_w^T and D = computeD(dAttn, attn_out) in one launch
+    (the D sums formed in the GEMM epilogue)."""
+    act = (B, p.M, p.N)
+    _check(dZ, "dZ", torch.bfloat16, act)
+    _check(proj_w, "proj_w", torch.bfloat16, (p.N, p.N))
+    _check(attn_out, "attn_out", torch.bfloat16, act)
+    dAttn = _out(dAttn, dZ, act, torch.bfloat16, "dAttn")
+    D = _out(D, dZ, (B, p.M, p.NH), torch.bfloat16, "D")
+    _lib.call("ma_projBackwarddXComputeD", _ptr(dZ), _ptr(proj_w), _ptr(dAttn), _ptr(attn_out), _ptr(D),
+              ctypes.byref(p), B, _stream(stream))
+    return dAttn, D
+
+
 def computeGradDx(q_w: torch.Tensor, k_w: torch.Tensor, v_w: torch.Tensor, dQ: torch.Tensor,
                   dK: torch.Tensor, dV: torch.Tensor, p: AttentionParams, B: int,
                   dX: Optional[torch.Tensor] = None, stream: Optional[torch.cuda.Stream] = None):

@@ -318,6 +318,32 @@ int ma_projBackwarddX(const ma_bf16* dZ, const ma_bf16* proj_w, ma_bf16* dAttn,
   return ok();
 }
 
+int ma_projBackwarddXComputeD(const ma_bf16* dZ, const ma_bf16* proj_w, ma_bf16* dAttn,
+                              const ma_bf16* attn_out, ma_bf16* D, const AttentionParams* p, uint32_t B,
+                              ma_stream_t stream) {
+  ma::AttnShape s;
+  int rc = check_shape(p, B, 0, 0, false, &s);
+  if (rc) return rc;
+  int rows = 0, n = 0;
+  rc = gemm_shape(p, B, &rows, &n);
+  if (rc) return rc;
+  MA_REQUIRE_PTR(dZ);
+  MA_REQUIRE_PTR(proj_w);
+  MA_REQUIRE_PTR(dAttn);
+  MA_REQUIRE_PTR(attn_out);
+  if (!D) return fail(MA_ERR_NULL, "pointer 'D' is NULL");
+  if (reinterpret_cast<uintptr_t>(D) & 1u) return fail(MA_ERR_ALIGN, "pointer 'D' is not 2-byte aligned");
+  uint32_t* status = nullptr;
+  rc = device_status_word(&status);
+  if (rc) return rc;
+  cudaError_t e = ma::launch_proj_backward_dx_d(reinterpret_cast<bf16p>(dZ), reinterpret_cast<bf16p>(proj_w),
+                                                reinterpret_cast<bf16m>(dAttn), reinterpret_cast<bf16p>(attn_out),
+                                                reinterpret_cast<bf16m>(D), rows, n, (int)p->D, status,
+                                                reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "projBackwarddX+computeD launch");
+  return ok();
+}
+
 int ma_computeGradDx(float* dX, const ma_bf16* qw, const ma_bf16* kw, const ma_bf16* vw,
                      const float* dQ, const ma_bf16* dK, const ma_bf16* dV,
                      const AttentionParams* p, uint32_t B, ma_stream_t stream) {

@@ -58,6 +58,9 @@ cudaError_t launch_proj_backward_dx(const __nv_bfloat16* dz, const __nv_bfloat16
 cudaError_t launch_proj_backward_dw(const __nv_bfloat16* attn, const __nv_bfloat16* dz,
                                     __nv_bfloat16* dw, int rows, int n, uint32_t* status,
                                     cudaStream_t st);
+cudaError_t launch_proj_backward_dx_d(const __nv_bfloat16* dz, const __nv_bfloat16* w, __nv_bfloat16* dattn,
+                                      const __nv_bfloat16* attn, __nv_bfloat16* d, int rows, int n, int head_dim,
+                                      uint32_t* status, cudaStream_t st);
 cudaError_t launch_grad_dx(float* dx, const __nv_bfloat16* qw, const __nv_bfloat16* kw,
                            const __nv_bfloat16* vw, const float* dq, const __nv_bfloat16* dk,
                            const __nv_bfloat16* dv, int rows, int n, uint32_t* status, cudaStream_t st);

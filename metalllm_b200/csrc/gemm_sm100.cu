@@ -57,6 +57,11 @@ struct GemmArgs {
   uint32_t c_f32;     // bit z: output z is fp32 (else bf16)
   int ksplit;         // split-K: grid.z = outputs * ksplit; partials are added (fp32 outputs)
   int kchunk;         // K steps per split
+  // fused computeD (FUSE_D): D[row][h] = bf16(sum over head h's columns of
+  // bf16(C) * O), O [M][N] bf16, D [M][N / head_dim] bf16
+  const __nv_bfloat16* o_in;
+  __nv_bfloat16* d_out;
+  int head_dim;
   uint32_t* status;
 };
 
@@ -78,7 +83,20 @@ struct GemmCfg {
 
 __device__ __forceinline__ int bit_of(uint32_t m, int i) { return (m >> i) & 1u; }
 
-template <int BN, bool A_MN, bool B_MN, bool HAS_F32>
+__device__ __forceinline__ float dot_bf16x8(uint4 a, uint4 b) {
+  const __nv_bfloat162* x = reinterpret_cast<const __nv_bfloat162*>(&a);
+  const __nv_bfloat162* y = reinterpret_cast<const __nv_bfloat162*>(&b);
+  float s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 fx = __bfloat1622float2(x[i]), fy = __bfloat1622float2(y[i]);
+    s = fmaf(fx.x, fy.x, s);
+    s = fmaf(fx.y, fy.y, s);
+  }
+  return s;
+}
+
+template <int BN, bool A_MN, bool B_MN, bool HAS_F32, bool FUSE_D = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_kernel(const __grid_constant__ GemmMaps maps, const GemmArgs args) {
   using C = GemmCfg<BN, HAS_F32>;
@@ -260,6 +278,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (ok) ok = mbar_wait_warp(BAR_DONE, 0, abort_p);
     ok = bar_red_and(1, 128, ok);
     const bool out_f32 = (args.c_f32 >> z) & 1u;
+    const int grow = row0 + row;
+    float dsum = 0.0f;  // FUSE_D: this row's partial dot for the current head
     if (ok) {
       tc_fence_after();
       uint8_t* stage = gbase;  // the ring is idle now
@@ -290,6 +310,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const int ch = (cc % 64) / 8;
           *reinterpret_cast<uint4*>(rowp + ((ch ^ (row & 7)) * 16)) = v0;
           *reinterpret_cast<uint4*>(rowp + (((ch + 1) ^ (row & 7)) * 16)) = v1;
+          if constexpr (FUSE_D) {  // D from the rounded bf16 values, as computeD reads them
+            if (grow < args.M) {
+              const uint4* op = reinterpret_cast<const uint4*>(args.o_in + (size_t)grow * args.N + col0 + cc);
+              dsum += dot_bf16x8(v0, __ldg(op)) + dot_bf16x8(v1, __ldg(op + 1));
+              if ((col0 + cc + 16) % args.head_dim == 0) {
+                const int nh = args.N / args.head_dim;
+                args.d_out[(size_t)grow * nh + (col0 + cc) / args.head_dim] = __float2bfloat16_rn(dsum);
+                dsum = 0.0f;
+              }
+            }
+          }
         }
       }
       fence_proxy_async_smem();
@@ -338,10 +369,11 @@ bool make_operand_map(CUtensorMap* m, const Operand& o, bool mn_major, uint64_t 
   return make_tmap_2d(m, o.ptr, t, eb, outer, K, inner_box, BK, sw);
 }
 
-template <int BN, bool A_MN, bool B_MN, bool HAS_F32>
+template <int BN, bool A_MN, bool B_MN, bool HAS_F32, bool FUSE_D = false>
 cudaError_t run_gemm(const Operand* A, int na, const Operand* Bop, int nb, void* const* Cptr,
                      const bool* c_f32, int nz, int nseg, int M, int N, int K, uint32_t* status,
-                     cudaStream_t st, int ksplit = 1) {
+                     cudaStream_t st, int ksplit = 1, const __nv_bfloat16* o_in = nullptr,
+                     __nv_bfloat16* d_out = nullptr, int head_dim = 0) {
   using Cfg = GemmCfg<BN, HAS_F32>;
   GemmMaps maps;
   memset(&maps, 0, sizeof(maps));
@@ -353,6 +385,12 @@ cudaError_t run_gemm(const Operand* A, int na, const Operand* Bop, int nb, void*
   args.na = na;
   args.nb = nb;
   args.status = status;
+  args.o_in = o_in;
+  args.d_out = d_out;
+  args.head_dim = head_dim;
+  if (FUSE_D && (!o_in || !d_out || head_dim <= 0 || BN % 16 || N % head_dim || head_dim % 16 ||
+                 nz != 1 || c_f32[0]))
+    return cudaErrorInvalidValue;
   // split-K only for single-segment products with fp32 outputs (the partial
   // sums are added by TMA reductions into outputs the caller has zeroed)
   const int nk_all = (K + BK - 1) / BK;
@@ -385,7 +423,7 @@ cudaError_t run_gemm(const Operand* A, int na, const Operand* Bop, int nb, void*
                                        CU_TENSOR_MAP_SWIZZLE_128B);
     if (!ok) return cudaErrorInvalidValue;
   }
-  auto kern = gemm_kernel<BN, A_MN, B_MN, HAS_F32>;
+  auto kern = gemm_kernel<BN, A_MN, B_MN, HAS_F32, FUSE_D>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
   if (e != cudaSuccess) return e;
   const dim3 grid((M + BM - 1) / BM, (N + BN - 1) / BN, nz * args.ksplit);
@@ -479,6 +517,18 @@ cudaError_t launch_proj_backward_dx(const __nv_bfloat16* dz, const __nv_bfloat16
   void* c[1] = {dattn};
   const bool cf[1] = {false};
   return run_gemm<128, false, false, false>(&a, 1, &b, 1, c, cf, 1, 1, rows, n, n, status, st);
+}
+
+// projBackwarddX with computeD fused into its epilogue: dAttn = dZ . W^T and
+// D[row][h] = bf16(sum_c bf16(dAttn[row][h*hd + c]) * attn[row][h*hd + c]).
+cudaError_t launch_proj_backward_dx_d(const __nv_bfloat16* dz, const __nv_bfloat16* w, __nv_bfloat16* dattn,
+                                      const __nv_bfloat16* attn, __nv_bfloat16* d, int rows, int n, int head_dim,
+                                      uint32_t* status, cudaStream_t st) {
+  const Operand a{dz, false}, b{w, false};
+  void* c[1] = {dattn};
+  const bool cf[1] = {false};
+  return run_gemm<128, false, false, false, true>(&a, 1, &b, 1, c, cf, 1, 1, rows, n, n, status, st, 1, attn,
+                                                  d, head_dim);
 }
 
 cudaError_t launch_proj_backward_dw(const __nv_bfloat16* attn, const __nv_bfloat16* dz, __nv_bfloat16* dw,

@@ -355,8 +355,9 @@ int ma_model_backward(ma_model* m, ma_stream_t stream) {
     MA_M_CUDA(launch_residual_add(m->dbranch, m->dstream, m->dbranch, (long long)R * E, st), "residualAdd");
     // attention block
     MA_M_CUDA(wgrad(m, y.attn, m->dbranch, y.dprojw, E, E, st), "projBackwarddW");
-    MA_M_CUDA(launch_proj_backward_dx(m->dbranch, y.projw, m->dzattn, R, E, m->status, st), "projBackwarddX");
-    MA_M_CUDA(launch_compute_d(m->dzattn, y.attn, m->dattnd, s, st), "computeD");
+    // projBackwarddX with computeD fused into its epilogue
+    MA_M_CUDA(launch_proj_backward_dx_d(m->dbranch, y.projw, m->dzattn, y.attn, m->dattnd, R, E, m->D, m->status,
+                                        st), "projBackwarddX + computeD");
     MA_M_CUDA(launch_flash_bwd(m->dzattn, m->dattnd, y.l, y.q, y.k, y.v, m->dq, m->dk, m->dv, s, m->status, st),
               "flashAttentionBackward");
     MA_M_CUDA(launch_grad_dx(m->dxattn, y.qw, y.kw, y.vw, m->dq, m->dk, m->dv, R, E, m->status, st),

@@ -148,3 +148,22 @@ def test_gemm_rejects_bad_n(A):
     wt = torch.zeros(96, 96, dtype=torch.bfloat16, device="cuda")
     with pytest.raises(A.MetalAttnError, match="MA_ERR_SHAPE"):
         A.projForward(x, wt, p, 1)
+
+
+@pytest.mark.parametrize("B,M,H,D", [(2, 100, 2, 64), (4, 256, 6, 64), (2, 130, 3, 128)])
+def test_proj_backward_dx_with_fused_compute_d(A, B, M, H, D):
+    """projBackwarddX + computeD in one launch (D formed in the GEMM epilogue)
+    equals the two separate entry points: dAttn bit for bit, D to one bf16
+    rounding step (the fp32 sum runs in another order)."""
+    N = H * D
+    act, w, _ = _data(B, M, N, 61)
+    dz, o, wp = up(act(1)), up(act(2)), up(w(3))
+    p = A.make_params(M, H, D)
+    dattn, Dv = A.projBackwarddXComputeD(dz, wp, o, p, B)
+    ref_dattn = A.projBackwarddX(dz, wp, p, B)
+    ref_D = A.computeD(ref_dattn, o, p, B)
+    torch.cuda.synchronize()
+    assert A.device_status() == 0
+    assert torch.equal(dattn, ref_dattn)
+    got, want = Dv.float().cpu().numpy(), ref_D.float().cpu().numpy()
+    assert np.abs(got - want).max() <= 2 ** -7 * max(1.0, np.abs(want).max())
