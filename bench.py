@@ -259,7 +259,21 @@ def run_gpu(args):
     h2d = sum(t.numel() * t.element_size() for t in (h_q, h_k, h_v, h_do))
     d2h = sum(t.numel() * t.element_size() for t in (h_out, h_l, h_dQ, h_dK, h_dV))
 
+    # whole local sequences: the public host-buffer entry point, which
+    # pipelines copies in, kernels and copies out over chunks of the batch;
+    # a shard that splits a sequence's heads copies whole tensors around the
+    # shard kernels instead
+    whole = shard is None or tuple(shard) == (0, Bl * H)
+    pipeline = None
+    if whole and not args.no_e2e:
+        e2e_chunk = max(1, -(-Bl // args.e2e_chunks))
+        pipeline = A.HostPipeline(T, H, D, e2e_chunk, device=dev)
+
     def e2e_step():
+        if pipeline is not None:
+            pipeline.forward_backward(h_q, h_k, h_v, h_do, Bl, out=h_out, l=h_l, dQ=h_dQ, dK=h_dK, dV=h_dV,
+                                      stream=stream)
+            return
         with torch.cuda.stream(stream):
             for dst, src in ((q, h_q), (k, h_k), (v, h_v), (do, h_do)):
                 dst.copy_(src, non_blocking=True)
@@ -356,7 +370,10 @@ def run_gpu(args):
         "clocks": clocks,
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
-                "note": "pinned host Q,K,V,dO -> device, fwd+computeD+bwd, O,l,dQ,dK,dV -> host"},
+                "note": ("pinned host Q,K,V,dO -> device, fwd+computeD+bwd, O,l,dQ,dK,dV -> host; "
+                         + (f"ma_attentionForwardBackward_host, chunks of {pipeline.chunk_B} sequences, "
+                            "copies in / kernels / copies out overlapped" if pipeline is not None
+                            else "whole-tensor copies around the shard kernels on one stream"))},
         "gpu_launches": int(launches),
         "roofline": roofline,
         "kernels": extra_kernels,
@@ -584,6 +601,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) leg")
+    ap.add_argument("--e2e-chunks", type=int, default=8,
+                    help="chunks the host-buffer pipeline splits the local batch into")
     ap.add_argument("--mode", default="weak", choices=["weak", "strong"],
                     help="weak: each GPU runs a whole config batch; strong: the config's "
                          "(batch, head) shards are split over the GPUs")

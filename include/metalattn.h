@@ -254,6 +254,38 @@ MA_API int ma_device_status(uint32_t* status, ma_stream_t stream);
  * no counterpart in the reference. */
 MA_API uint64_t ma_kernel_launch_count(void);
 
+/* ---- Host-resident batches.  The reference's buffers are shared CPU/GPU
+ * memory (MTLResourceStorageModeShared, model.h:236-253): its host writes
+ * inputs and reads results in place.  On a discrete GPU the batch must cross
+ * PCIe, so a pipeline splits the batch into chunks of `chunk_B` sequences
+ * and overlaps, on three internal streams, the host->device copy of chunk
+ * c+1, the kernels of chunk c and the device->host copy of chunk c-1 (the
+ * copy engines of the two directions run concurrently).  Results equal the
+ * device entry points bit for bit (every (batch, head) is independent).
+ *   - Host pointers should be page-locked (cudaHostAlloc / cudaHostRegister);
+ *     pageable memory gives the same results without the overlap.
+ *   - A pipeline belongs to the device current at create and owns three
+ *     chunk-sized sets of device buffers (allocated once, at create).
+ *   - Calls are stream-ordered: the copies start after the work already on
+ *     `stream` and `stream` waits for the last copy back; the host buffers
+ *     must stay valid until then.  Calls that use one pipeline must be
+ *     ordered (same stream, or synchronised).
+ * No counterpart in the reference. */
+typedef struct ma_host_pipeline ma_host_pipeline;
+MA_API int ma_host_pipeline_create(const AttentionParams* p, uint32_t chunk_B, ma_host_pipeline** out);
+MA_API int ma_host_pipeline_destroy(ma_host_pipeline* pl);
+/* flashAttentionForward over B host-resident sequences: q, k, v -> out, l. */
+MA_API int ma_flashAttentionForward_host(ma_host_pipeline* pl, const ma_bf16* q, const ma_bf16* k,
+                                         const ma_bf16* v, ma_bf16* out, float* l, uint32_t B,
+                                         ma_stream_t stream);
+/* forward, computeD and backward over B host-resident sequences:
+ * q, k, v, dO -> out, l, dQ, dK, dV (the attention core of one training step,
+ * model.h:459-473 then model.h:639-665). */
+MA_API int ma_attentionForwardBackward_host(ma_host_pipeline* pl, const ma_bf16* q, const ma_bf16* k,
+                                            const ma_bf16* v, const ma_bf16* dO, ma_bf16* out, float* l,
+                                            float* dQ, ma_bf16* dK, ma_bf16* dV, uint32_t B,
+                                            ma_stream_t stream);
+
 /* Library version as major*10000 + minor*100 + patch. */
 MA_API int ma_version(void);
 

@@ -56,6 +56,10 @@ SIGNATURES = {
     "ma_projBackwarddXComputeD": [_P, _P, _P, _P, _P, _PP, _U32, _P],
     "ma_computeGradDx": [_P, _P, _P, _P, _P, _P, _P, _PP, _U32, _P],
     "ma_computeGradDw": [_P, _P, _P, _P, _P, _P, _P, _PP, _U32, _P],
+    "ma_host_pipeline_create": [_PP, _U32, ctypes.POINTER(_P)],
+    "ma_host_pipeline_destroy": [_P],
+    "ma_flashAttentionForward_host": [_P, _P, _P, _P, _P, _P, _U32, _P],
+    "ma_attentionForwardBackward_host": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _U32, _P],
     "ma_device_status": [ctypes.POINTER(ctypes.c_uint32), _P],
     "ma_version": [],
 }

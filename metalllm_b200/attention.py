@@ -273,3 +273,83 @@ class CudaAttention:
         computeD(dO, self.out, self.p, self.B, D=self.Dvec, stream=stream)
         return flashAttentionBackward(dO, self.Dvec, self.l, self.q, self.k, self.v, self.p,
                                       self.B, dQ=self.dQ, dK=self.dK, dV=self.dV, stream=stream)
+
+
+def _check_host(t: torch.Tensor, name: str, dtype: torch.dtype, shape: tuple) -> None:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if t.is_cuda:
+        raise ValueError(f"{name} must be a host (CPU) tensor; use the device entry points for CUDA tensors")
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if t.numel() != _numel(shape):
+        raise ValueError(f"{name} has shape {tuple(t.shape)}, expected {tuple(shape)}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+class HostPipeline:
+    """Attention over host-resident batches (ma_host_pipeline_*): the batch is
+    split into chunks of `chunk_B` sequences whose host->device copies,
+    kernels and device->host copies overlap on three internal streams.  The
+    reference needs no such step (its Metal buffers are shared CPU/GPU memory,
+    model.h:236-253); the results equal the device entry points bit for bit.
+    Host tensors should be pinned (`tensor.pin_memory()`) for the overlap."""
+
+    def __init__(self, T: int, NH: int, D: int, chunk_B: int, device=None):
+        self.p = make_params(T, NH, D)
+        self.T, self.NH, self.D, self.chunk_B = T, NH, D, chunk_B
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        h = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _lib.call("ma_host_pipeline_create", ctypes.byref(self.p), chunk_B, ctypes.byref(h))
+        self._h = h
+
+    def close(self) -> None:
+        if getattr(self, "_h", None) is not None and self._h.value:
+            _lib.call("ma_host_pipeline_destroy", self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _shapes(self, B: int):
+        act = (B, self.T, self.NH * self.D)
+        return act, (B, self.T, self.NH)
+
+    def forward(self, q, k, v, B: int, out=None, l=None, stream=None):
+        """flashAttentionForward of B host sequences -> (out bf16, l fp32), host."""
+        act, rows = self._shapes(B)
+        for t, n in ((q, "q"), (k, "k"), (v, "v")):
+            _check_host(t, n, torch.bfloat16, act)
+        out = torch.empty(act, dtype=torch.bfloat16).pin_memory() if out is None else out
+        l = torch.empty(rows, dtype=torch.float32).pin_memory() if l is None else l
+        _check_host(out, "out", torch.bfloat16, act)
+        _check_host(l, "l", torch.float32, rows)
+        with torch.cuda.device(self.device):
+            _lib.call("ma_flashAttentionForward_host", self._h, q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                      out.data_ptr(), l.data_ptr(), B, _stream(stream))
+        return out, l
+
+    def forward_backward(self, q, k, v, dO, B: int, out=None, l=None, dQ=None, dK=None, dV=None,
+                         stream=None):
+        """forward + computeD + backward of B host sequences ->
+        (out, l, dQ, dK, dV), host tensors, ready when `stream` is."""
+        act, rows = self._shapes(B)
+        for t, n in ((q, "q"), (k, "k"), (v, "v"), (dO, "dO")):
+            _check_host(t, n, torch.bfloat16, act)
+        mk = lambda t, shape, dt: torch.empty(shape, dtype=dt).pin_memory() if t is None else t
+        out, l = mk(out, act, torch.bfloat16), mk(l, rows, torch.float32)
+        dQ, dK, dV = mk(dQ, act, torch.float32), mk(dK, act, torch.bfloat16), mk(dV, act, torch.bfloat16)
+        for t, n, dt, shp in ((out, "out", torch.bfloat16, act), (l, "l", torch.float32, rows),
+                              (dQ, "dQ", torch.float32, act), (dK, "dK", torch.bfloat16, act),
+                              (dV, "dV", torch.bfloat16, act)):
+            _check_host(t, n, dt, shp)
+        with torch.cuda.device(self.device):
+            _lib.call("ma_attentionForwardBackward_host", self._h, q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                      dO.data_ptr(), out.data_ptr(), l.data_ptr(), dQ.data_ptr(), dK.data_ptr(),
+                      dV.data_ptr(), B, _stream(stream))
+        return out, l, dQ, dK, dV

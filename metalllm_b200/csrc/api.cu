@@ -509,3 +509,215 @@ extern "C" int ma_flashAttentionBackward_noalloc(const ma_bf16* dZ, const ma_bf1
   if (e != cudaSuccess) return cuda_fail(e, "flashAttentionBackward launch (no-alloc)");
   return ok();
 }
+
+// ---------------------------------------------------------------------------
+// Host-resident batches: chunked copy / compute / copy-back pipeline.
+// Chunk c uses buffer slot c % kSlots.  Stream order per chunk:
+//   h2d : [wait compute(c - kSlots) done: its inputs are consumed] copy in -> in_ready
+//   comp: wait in_ready, [wait d2h(c - kSlots) done: outputs read] kernels -> comp_done
+//   d2h : wait comp_done, copy out -> out_done
+// so copies in, kernels and copies out of neighbouring chunks overlap.
+struct ma_host_pipeline {
+  static constexpr int kSlots = 3;
+  int device = -1;
+  AttentionParams p{};
+  uint32_t chunk_B = 0;
+  size_t act_elems = 0, row_elems = 0;  // per chunk: chunk_B*M*N, chunk_B*M*NH
+  struct Slot {
+    __nv_bfloat16 *q = nullptr, *k = nullptr, *v = nullptr, *dO = nullptr, *out = nullptr, *dK = nullptr,
+                  *dV = nullptr, *D = nullptr;
+    float *l = nullptr, *dQ = nullptr;
+    cudaEvent_t in_ready = nullptr, comp_done = nullptr, out_done = nullptr;
+  } slot[kSlots];
+  cudaStream_t h2d = nullptr, comp = nullptr, d2h = nullptr;
+  cudaEvent_t start = nullptr;
+  void* block = nullptr;  // one allocation holds every slot's buffers
+};
+
+namespace {
+
+void pipeline_free(ma_host_pipeline* pl) {
+  for (auto& s : pl->slot) {
+    if (s.in_ready) cudaEventDestroy(s.in_ready);
+    if (s.comp_done) cudaEventDestroy(s.comp_done);
+    if (s.out_done) cudaEventDestroy(s.out_done);
+  }
+  if (pl->start) cudaEventDestroy(pl->start);
+  if (pl->h2d) cudaStreamDestroy(pl->h2d);
+  if (pl->comp) cudaStreamDestroy(pl->comp);
+  if (pl->d2h) cudaStreamDestroy(pl->d2h);
+  if (pl->block) cudaFree(pl->block);
+  delete pl;
+}
+
+size_t round256(size_t n) { return (n + 255) & ~size_t(255); }
+
+// One chunk of rows [b0, b0 + bc) of a host batch through the pipeline.
+int pipeline_chunk(ma_host_pipeline* pl, int c, uint32_t b0, uint32_t bc, bool backward, const ma_bf16* q,
+                   const ma_bf16* k, const ma_bf16* v, const ma_bf16* dO, ma_bf16* out, float* l, float* dQ,
+                   ma_bf16* dK, ma_bf16* dV) {
+  auto& s = pl->slot[c % ma_host_pipeline::kSlots];
+  const bool reuse = c >= ma_host_pipeline::kSlots;
+  const size_t per_seq = (size_t)pl->p.M * pl->p.N, per_seq_rows = (size_t)pl->p.M * pl->p.NH;
+  const size_t off = (size_t)b0 * per_seq, off_rows = (size_t)b0 * per_seq_rows;
+  const size_t n = (size_t)bc * per_seq, n_rows = (size_t)bc * per_seq_rows;
+  cudaError_t e = cudaSuccess;
+  auto h2d = [&](void* dst, const void* src, size_t bytes) {
+    if (e == cudaSuccess) e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, pl->h2d);
+  };
+  auto d2h = [&](void* dst, const void* src, size_t bytes) {
+    if (e == cudaSuccess) e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, pl->d2h);
+  };
+  if (reuse) e = cudaStreamWaitEvent(pl->h2d, s.comp_done, 0);
+  h2d(s.q, q + off, n * 2);
+  h2d(s.k, k + off, n * 2);
+  h2d(s.v, v + off, n * 2);
+  if (backward) h2d(s.dO, dO + off, n * 2);
+  if (e == cudaSuccess) e = cudaEventRecord(s.in_ready, pl->h2d);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(pl->comp, s.in_ready, 0);
+  if (e == cudaSuccess && reuse) e = cudaStreamWaitEvent(pl->comp, s.out_done, 0);
+  if (e != cudaSuccess) return cuda_fail(e, "host pipeline: copy in");
+
+  ma::AttnShape sh;
+  int rc = check_shape(&pl->p, bc, 0, 0, false, &sh);
+  if (rc) return rc;
+  uint32_t* status = nullptr;
+  rc = device_status_word(&status);
+  if (rc) return rc;
+  e = ma::launch_flash_fwd(s.q, s.k, s.v, s.out, s.l, sh, status, pl->comp);
+  if (e != cudaSuccess) return cuda_fail(e, "host pipeline: flashAttentionForward launch");
+  if (backward) {
+    e = ma::launch_compute_d(s.dO, s.out, s.D, sh, pl->comp);
+    if (e != cudaSuccess) return cuda_fail(e, "host pipeline: computeD launch");
+    e = ma::launch_flash_bwd(s.dO, s.D, s.l, s.q, s.k, s.v, s.dQ, s.dK, s.dV, sh, status, pl->comp);
+    if (e != cudaSuccess) return cuda_fail(e, "host pipeline: flashAttentionBackward launch");
+  }
+  e = cudaEventRecord(s.comp_done, pl->comp);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(pl->d2h, s.comp_done, 0);
+  d2h(out + off, s.out, n * 2);
+  d2h(l + off_rows, s.l, n_rows * 4);
+  if (backward) {
+    d2h(dQ + off, s.dQ, n * 4);
+    d2h(dK + off, s.dK, n * 2);
+    d2h(dV + off, s.dV, n * 2);
+  }
+  if (e == cudaSuccess) e = cudaEventRecord(s.out_done, pl->d2h);
+  if (e != cudaSuccess) return cuda_fail(e, "host pipeline: copy out");
+  return MA_OK;
+}
+
+int pipeline_run(ma_host_pipeline* pl, bool backward, const ma_bf16* q, const ma_bf16* k, const ma_bf16* v,
+                 const ma_bf16* dO, ma_bf16* out, float* l, float* dQ, ma_bf16* dK, ma_bf16* dV, uint32_t B,
+                 ma_stream_t stream) {
+  if (!pl) return fail(MA_ERR_NULL, "host pipeline is NULL");
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev != pl->device)
+    return fail(MA_ERR_NO_DEVICE, "host pipeline belongs to device %d, current device is %d", pl->device, dev);
+  ma::AttnShape sh;
+  int rc = check_shape(&pl->p, B, 0, 0, false, &sh);
+  if (rc) return rc;
+  if (!q || !k || !v || !out || !l || (backward && (!dO || !dQ || !dK || !dV)))
+    return fail(MA_ERR_NULL, "a host buffer pointer is NULL");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  e = cudaEventRecord(pl->start, st);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(pl->h2d, pl->start, 0);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(pl->comp, pl->start, 0);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(pl->d2h, pl->start, 0);
+  if (e != cudaSuccess) return cuda_fail(e, "host pipeline: start");
+  const uint32_t nchunks = (B + pl->chunk_B - 1) / pl->chunk_B;
+  for (uint32_t c = 0; c < nchunks; ++c) {
+    const uint32_t b0 = c * pl->chunk_B;
+    const uint32_t bc = B - b0 < pl->chunk_B ? B - b0 : pl->chunk_B;
+    rc = pipeline_chunk(pl, (int)c, b0, bc, backward, q, k, v, dO, out, l, dQ, dK, dV);
+    if (rc) return rc;
+  }
+  // the d2h stream is in order, so its last record covers every chunk (and,
+  // through the waits, every kernel and copy in)
+  e = cudaStreamWaitEvent(st, pl->slot[(nchunks - 1) % ma_host_pipeline::kSlots].out_done, 0);
+  if (e != cudaSuccess) return cuda_fail(e, "host pipeline: finish");
+  return ok();
+}
+
+}  // namespace
+
+extern "C" int ma_host_pipeline_create(const AttentionParams* p, uint32_t chunk_B, ma_host_pipeline** out) {
+  if (!out) return fail(MA_ERR_NULL, "output pointer is NULL");
+  *out = nullptr;
+  ma::AttnShape sh;
+  int rc = check_shape(p, chunk_B, 0, 0, false, &sh);
+  if (rc) return rc;
+  uint32_t* status = nullptr;
+  rc = device_status_word(&status);  // also checks for an sm_100 device
+  if (rc) return rc;
+  auto* pl = new ma_host_pipeline();
+  cudaGetDevice(&pl->device);
+  pl->p = *p;
+  pl->chunk_B = chunk_B;
+  pl->act_elems = (size_t)chunk_B * p->M * p->N;
+  pl->row_elems = (size_t)chunk_B * p->M * p->NH;
+  const size_t a2 = round256(pl->act_elems * 2), a4 = round256(pl->act_elems * 4);
+  const size_t r2 = round256(pl->row_elems * 2), r4 = round256(pl->row_elems * 4);
+  const size_t per_slot = 7 * a2 + a4 + r2 + r4;
+  cudaError_t e = cudaMalloc(&pl->block, per_slot * ma_host_pipeline::kSlots);
+  if (e != cudaSuccess) {
+    pipeline_free(pl);
+    return cuda_fail(e, "cudaMalloc(host pipeline buffers)");
+  }
+  unsigned char* base = static_cast<unsigned char*>(pl->block);
+  for (auto& s : pl->slot) {
+    auto take = [&](size_t bytes) {
+      void* r = base;
+      base += bytes;
+      return r;
+    };
+    s.q = static_cast<__nv_bfloat16*>(take(a2));
+    s.k = static_cast<__nv_bfloat16*>(take(a2));
+    s.v = static_cast<__nv_bfloat16*>(take(a2));
+    s.dO = static_cast<__nv_bfloat16*>(take(a2));
+    s.out = static_cast<__nv_bfloat16*>(take(a2));
+    s.dK = static_cast<__nv_bfloat16*>(take(a2));
+    s.dV = static_cast<__nv_bfloat16*>(take(a2));
+    s.dQ = static_cast<float*>(take(a4));
+    s.D = static_cast<__nv_bfloat16*>(take(r2));
+    s.l = static_cast<float*>(take(r4));
+    for (cudaEvent_t* ev : {&s.in_ready, &s.comp_done, &s.out_done})
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(ev, cudaEventDisableTiming);
+  }
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&pl->start, cudaEventDisableTiming);
+  for (cudaStream_t* st : {&pl->h2d, &pl->comp, &pl->d2h})
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(st, cudaStreamNonBlocking);
+  if (e != cudaSuccess) {
+    pipeline_free(pl);
+    return cuda_fail(e, "host pipeline streams/events");
+  }
+  *out = pl;
+  return ok();
+}
+
+extern "C" int ma_host_pipeline_destroy(ma_host_pipeline* pl) {
+  if (!pl) return ok();
+  int prev = -1;
+  cudaGetDevice(&prev);
+  cudaSetDevice(pl->device);
+  cudaStreamSynchronize(pl->h2d);
+  cudaStreamSynchronize(pl->comp);
+  cudaStreamSynchronize(pl->d2h);
+  pipeline_free(pl);
+  if (prev >= 0) cudaSetDevice(prev);
+  return ok();
+}
+
+extern "C" int ma_flashAttentionForward_host(ma_host_pipeline* pl, const ma_bf16* q, const ma_bf16* k,
+                                             const ma_bf16* v, ma_bf16* out, float* l, uint32_t B,
+                                             ma_stream_t stream) {
+  return pipeline_run(pl, false, q, k, v, nullptr, out, l, nullptr, nullptr, nullptr, B, stream);
+}
+
+extern "C" int ma_attentionForwardBackward_host(ma_host_pipeline* pl, const ma_bf16* q, const ma_bf16* k,
+                                                const ma_bf16* v, const ma_bf16* dO, ma_bf16* out, float* l,
+                                                float* dQ, ma_bf16* dK, ma_bf16* dV, uint32_t B,
+                                                ma_stream_t stream) {
+  return pipeline_run(pl, true, q, k, v, dO, out, l, dQ, dK, dV, B, stream);
+}
