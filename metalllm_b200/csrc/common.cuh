@@ -75,6 +75,13 @@ cudaError_t launch_gemm_splitk_f32(const __nv_bfloat16* A, const __nv_bfloat16* 
 cudaError_t launch_grad_dw_splitk(const __nv_bfloat16* x, const float* dq, const __nv_bfloat16* dk,
                                   const __nv_bfloat16* dv, float* dqw, __nv_bfloat16* dkw, __nv_bfloat16* dvw,
                                   float* ws, int rows, int n, uint32_t* status, cudaStream_t st);
+cudaError_t launch_grad_dx_bf16(float* dx, const __nv_bfloat16* qw, const __nv_bfloat16* kw,
+                                const __nv_bfloat16* vw, const __nv_bfloat16* dq16, const __nv_bfloat16* dk,
+                                const __nv_bfloat16* dv, int rows, int n, uint32_t* status, cudaStream_t st);
+cudaError_t launch_grad_dw_splitk_bf16(const __nv_bfloat16* x, const __nv_bfloat16* dq16, const __nv_bfloat16* dk,
+                                       const __nv_bfloat16* dv, float* dqw, __nv_bfloat16* dkw,
+                                       __nv_bfloat16* dvw, float* ws, int rows, int n, uint32_t* status,
+                                       cudaStream_t st);
 
 // Training-step kernels (train_sm100.cu).
 cudaError_t launch_embed_forward(const int* tok, const __nv_bfloat16* emb, const __nv_bfloat16* pos,
@@ -96,9 +103,17 @@ cudaError_t launch_loss_forward(const __nv_bfloat16* x, const int* y, float* out
                                 int rows, int cols, cudaStream_t st);
 cudaError_t launch_loss_backward(const __nv_bfloat16* x, const int* y, const float* lse, __nv_bfloat16* dz,
                                  int rows, int cols, cudaStream_t st);
-cudaError_t launch_adam(float* p, const __nv_bfloat16* g, __nv_bfloat16* m, __nv_bfloat16* v, long long n,
-                        float lr_t, cudaStream_t st);
-cudaError_t launch_gather_f32(const float* src, __nv_bfloat16* dst, long long n, cudaStream_t st);
-cudaError_t launch_scatter(const float* master, __nv_bfloat16* dst, long long n, cudaStream_t st);
 
+
+// One optimizer segment per parameter: its gradient (fp32 or bf16), its bf16
+// weight, its element count and its offset into the flat master/moment arrays.
+struct AdamSegment {
+  const void* grad;
+  __nv_bfloat16* weight;
+  long long count;
+  long long offset;
+  int grad_f32;
+};
+cudaError_t launch_adam_fused(const AdamSegment* segs, int nsegs, long long max_count, float* p,
+                              __nv_bfloat16* m, __nv_bfloat16* v, float lr_t, cudaStream_t st);
 }  // namespace ma

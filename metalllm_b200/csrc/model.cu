@@ -60,13 +60,16 @@ struct ma_model {
   __nv_bfloat16 *embed_out = nullptr, *logits = nullptr, *dlogits = nullptr;
   __nv_bfloat16 *dstream = nullptr, *dbranch = nullptr, *dzattn = nullptr, *dattnd = nullptr;
   __nv_bfloat16 *dk = nullptr, *dv = nullptr, *dmlpv = nullptr, *dpos = nullptr, *dlinw = nullptr;
+  __nv_bfloat16* dq16 = nullptr;  // dQ rounded to bf16 for computeGradDx/Dw
   float *dq = nullptr, *dxattn = nullptr, *demb = nullptr;
   float* ws = nullptr;  // fp32 workspace of the split-K weight-gradient GEMMs
   float *loss_rows = nullptr, *lse_rows = nullptr, *loss_mean = nullptr;
   const int* tokens = nullptr;   // last forward's inputs (device)
   const int* targets = nullptr;
   float* master = nullptr;
-  __nv_bfloat16 *gflat = nullptr, *mom = nullptr, *var = nullptr;
+  __nv_bfloat16 *mom = nullptr, *var = nullptr;
+  ma::AdamSegment* segs = nullptr;  // device table, one entry per parameter
+  long long max_count = 0;
   size_t nparam = 0;
   float step_count = 0.0f;
   uint32_t* status = nullptr;
@@ -239,6 +242,7 @@ int ma_model_create(const MaModelConfig* c, ma_model** out) {
   ALLOC(m->dzattn, R * E);
   ALLOC(m->dattnd, R * m->NH);
   ALLOC(m->dq, R * E);
+  ALLOC(m->dq16, R * E);
   ALLOC(m->dk, R * E);
   ALLOC(m->dv, R * E);
   ALLOC(m->dxattn, R * E);
@@ -249,7 +253,8 @@ int ma_model_create(const MaModelConfig* c, ma_model** out) {
   ALLOC(m->loss_mean, 1);
   ALLOC(m->status, 1);
   // flat optimizer state (model.h:300-325): fp32 master copy of the bf16
-  // weights, bf16 gradients and moments
+  // weights and bf16 moments (the gradients are read where the backward
+  // wrote them)
   size_t off = 0;
   for (auto& p : m->params) {
     p.offset = off;
@@ -257,7 +262,7 @@ int ma_model_create(const MaModelConfig* c, ma_model** out) {
   }
   m->nparam = off;
   ALLOC(m->master, off);
-  ALLOC(m->gflat, off);
+
   ALLOC(m->mom, off);
   ALLOC(m->var, off);
   for (auto& p : m->params) {
@@ -271,6 +276,15 @@ int ma_model_create(const MaModelConfig* c, ma_model** out) {
     if ((e = cudaMemcpy(m->master + p.offset, f.data(), p.count * 4, cudaMemcpyHostToDevice)))
       return fail(e, "cudaMemcpy");
   }
+  // the optimizer's segment table (one fused launch per step)
+  std::vector<ma::AdamSegment> segs;
+  for (const auto& p : m->params) {
+    segs.push_back({p.grad, p.weight, (long long)p.count, (long long)p.offset, p.grad_f32 ? 1 : 0});
+    m->max_count = std::max(m->max_count, (long long)p.count);
+  }
+  ALLOC(m->segs, segs.size());
+  if ((e = cudaMemcpy(m->segs, segs.data(), segs.size() * sizeof(ma::AdamSegment), cudaMemcpyHostToDevice)))
+    return fail(e, "cudaMemcpy");
 #undef ALLOC
   *out = m;
   return MA_OK;
@@ -360,10 +374,13 @@ int ma_model_backward(ma_model* m, ma_stream_t stream) {
                                         st), "projBackwarddX + computeD");
     MA_M_CUDA(launch_flash_bwd(m->dzattn, m->dattnd, y.l, y.q, y.k, y.v, m->dq, m->dk, m->dv, s, m->status, st),
               "flashAttentionBackward");
-    MA_M_CUDA(launch_grad_dx(m->dxattn, y.qw, y.kw, y.vw, m->dq, m->dk, m->dv, R, E, m->status, st),
+    // dQ rounded to bf16 once for both products (their fp32-operand kernels
+    // apply the same rounding on chip)
+    MA_M_CUDA(launch_cast_f32_bf16(m->dq, m->dq16, (long long)R * E, st), "castFloatToBfloat dQ");
+    MA_M_CUDA(launch_grad_dx_bf16(m->dxattn, y.qw, y.kw, y.vw, m->dq16, m->dk, m->dv, R, E, m->status, st),
               "computeGradDx");
-    MA_M_CUDA(launch_grad_dw_splitk(y.ln1.out, m->dq, m->dk, m->dv, y.dqw, y.dkw, y.dvw, m->ws, R, E,
-                                    m->status, st), "computeGradDw");
+    MA_M_CUDA(launch_grad_dw_splitk_bf16(y.ln1.out, m->dq16, m->dk, m->dv, y.dqw, y.dkw, y.dvw, m->ws, R, E,
+                                         m->status, st), "computeGradDw");
     MA_M_CUDA(launch_cast_f32_bf16(m->dxattn, m->dstream, (long long)R * E, st), "castFloatToBfloat");
     MA_M_CUDA(launch_layernorm_backward(m->dstream, y.ln1.xn, y.ln1.gamma, y.ln1.stdev, y.ln1.dgamma,
                                         y.ln1.dbeta, R, E, st), "layernormBackward");
@@ -381,18 +398,8 @@ int ma_model_step(ma_model* m, ma_stream_t stream) {
   m->step_count += 1.0f;
   const float t = m->step_count;
   const float lr_t = m->cfg.lr * std::sqrt(1.0f - std::pow(0.999f, t)) / (1.0f - std::pow(0.9f, t));
-  for (const Param& p : m->params) {
-    if (p.grad_f32) {
-      MA_M_CUDA(launch_gather_f32(static_cast<const float*>(p.grad), m->gflat + p.offset, (long long)p.count, st),
-                "gatherGradFloat");
-    } else {
-      MA_M_CUDA(cudaMemcpyAsync(m->gflat + p.offset, p.grad, p.count * 2, cudaMemcpyDeviceToDevice, st),
-                "gatherGradBfloat");
-    }
-  }
-  MA_M_CUDA(launch_adam(m->master, m->gflat, m->mom, m->var, (long long)m->nparam, lr_t, st), "MetalStep");
-  for (const Param& p : m->params)
-    MA_M_CUDA(launch_scatter(m->master + p.offset, p.weight, (long long)p.count, st), "scatterWeight");
+  MA_M_CUDA(launch_adam_fused(m->segs, (int)m->params.size(), m->max_count, m->master, m->mom, m->var, lr_t, st),
+            "MetalStep");
   return MA_OK;
 }
 

@@ -138,6 +138,156 @@ __global__ void layernorm_backward_kernel(__nv_bfloat16* __restrict__ dz, const 
   }
 }
 
+// Row kernels for cols <= 256*NCH (cols a multiple of 8): one warp per row,
+// lane l holding the 8-column chunks l, l+32, ... (16-byte loads and stores),
+// the row kept in registers between its passes.
+__device__ __forceinline__ void unpack8(const uint4 u, float (&f)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __bfloat1622float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  uint4 u;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+  return u;
+}
+
+template <int NCH>
+__global__ void layernorm_forward_vec_kernel(const uint4* __restrict__ x, uint4* __restrict__ xn,
+                                             uint4* __restrict__ out, const uint4* __restrict__ gamma,
+                                             const uint4* __restrict__ beta, float* __restrict__ stdev, int rows,
+                                             int cols, float eps) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
+  if (warp >= rows) return;
+  const int c8 = cols / 8;
+  const long long rb = (long long)warp * c8;
+  float v[NCH][8];
+  float s = 0.0f;
+#pragma unroll
+  for (int k = 0; k < NCH; ++k) {
+    const int c = lane + 32 * k;
+    if (c < c8) {
+      unpack8(x[rb + c], v[k]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s += v[k][i];
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float mean = s / cols;
+  float q = 0.0f;
+#pragma unroll
+  for (int k = 0; k < NCH; ++k)
+    if (lane + 32 * k < c8)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float d = v[k][i] - mean;
+        q += d * d;
+      }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+  const float sd = sqrtf(q / cols + eps);
+  const float rs = 1.0f / sd;
+  if (lane == 0) stdev[warp] = sd;
+#pragma unroll
+  for (int k = 0; k < NCH; ++k) {
+    const int c = lane + 32 * k;
+    if (c < c8) {
+      float g[8], b[8], n[8], o[8];
+      unpack8(gamma[c], g);
+      unpack8(beta[c], b);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        n[i] = (v[k][i] - mean) * rs;
+        o[i] = g[i] * n[i] + b[i];
+      }
+      xn[rb + c] = pack8(n);
+      out[rb + c] = pack8(o);
+    }
+  }
+}
+
+// Backward, dZ rewritten in place with dX (layernorm.metal:74-127); each
+// lane keeps its columns' dGamma/dBeta partial sums in registers over the
+// rows its warp visits, then the block reduces them in shared memory and adds
+// one value per column into the fp32 outputs.
+template <int NCH>
+__global__ void layernorm_backward_vec_kernel(uint4* __restrict__ dz, const uint4* __restrict__ xn,
+                                              const uint4* __restrict__ gamma, const float* __restrict__ stdev,
+                                              float* __restrict__ dgamma, float* __restrict__ dbeta, int rows,
+                                              int cols) {
+  extern __shared__ float red[];  // [2][cols]
+  for (int c = threadIdx.x; c < 2 * cols; c += blockDim.x) red[c] = 0.0f;
+  const int lane = threadIdx.x % 32, w = threadIdx.x / 32, nw = blockDim.x / 32;
+  const int c8 = cols / 8;
+  float gm[NCH][8], pg[NCH][8], pb[NCH][8];
+#pragma unroll
+  for (int k = 0; k < NCH; ++k) {
+    if (lane + 32 * k < c8) unpack8(gamma[lane + 32 * k], gm[k]);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) pg[k][i] = pb[k][i] = 0.0f;
+  }
+  for (int row = blockIdx.x * nw + w; row < rows; row += gridDim.x * nw) {
+    const long long rb = (long long)row * c8;
+    float d[NCH][8], n[NCH][8];
+    float s1 = 0.0f, s2 = 0.0f;
+#pragma unroll
+    for (int k = 0; k < NCH; ++k) {
+      const int c = lane + 32 * k;
+      if (c < c8) {
+        unpack8(dz[rb + c], d[k]);
+        unpack8(xn[rb + c], n[k]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float g = d[k][i] * gm[k][i];
+          s1 += g;
+          s2 += g * n[k][i];
+          pg[k][i] += d[k][i] * n[k][i];
+          pb[k][i] += d[k][i];
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+      s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+    }
+    const float m1 = s1 / cols, m2 = s2 / cols, rs = 1.0f / stdev[row];
+#pragma unroll
+    for (int k = 0; k < NCH; ++k) {
+      const int c = lane + 32 * k;
+      if (c < c8) {
+        float r[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) r[i] = rs * (d[k][i] * gm[k][i] - m1 - n[k][i] * m2);
+        dz[rb + c] = pack8(r);
+      }
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < NCH; ++k) {
+    const int c = lane + 32 * k;
+    if (c < c8)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        atomicAdd(&red[c * 8 + i], pg[k][i]);
+        atomicAdd(&red[cols + c * 8 + i], pb[k][i]);
+      }
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+    atomicAdd(dgamma + c, red[c]);
+    atomicAdd(dbeta + c, red[cols + c]);
+  }
+}
+
 // ---------------------------------------------------------------- glue
 __global__ void residual_add_kernel(const uint4* __restrict__ a, const uint4* __restrict__ b,
                                     uint4* __restrict__ out, long long n8) {
@@ -242,30 +392,29 @@ __global__ void loss_backward_kernel(const __nv_bfloat16* __restrict__ x, const 
 // Adam on the flat fp32 master parameters with bf16 gradients and moments
 // (optimstep.metal:15-42): v = b2 v + (1-b2) g^2; m = b1 m + (1-b1) g;
 // p -= lr_t * m * rsqrt(v + eps).
-__global__ void adam_kernel(float* __restrict__ p, const __nv_bfloat16* __restrict__ g,
-                            __nv_bfloat16* __restrict__ m, __nv_bfloat16* __restrict__ v, long long n,
-                            float b1, float b2, float lr_t, float ob1, float ob2, float eps) {
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+// The whole optimizer step in one pass: for parameter blockIdx.y, each
+// element's gradient is rounded to bf16 (the gather into the flat gradient
+// array of model.h:726-742), Adam updates the fp32 master and bf16 moments at
+// the parameter's flat offset (optimstep.metal:15-42), and the rounded master
+// is written back to the bf16 weight (the scatter) -- the same values as
+// gather, adam_kernel and scatter in sequence, in one launch.
+__global__ void adam_fused_kernel(const AdamSegment* __restrict__ segs, float* __restrict__ p,
+                                  __nv_bfloat16* __restrict__ m, __nv_bfloat16* __restrict__ v, float b1,
+                                  float b2, float lr_t, float ob1, float ob2, float eps) {
+  const AdamSegment sg = segs[blockIdx.y];
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < sg.count;
        i += (long long)gridDim.x * blockDim.x) {
-    const float gi = bf(g[i]);
-    const float vi = fmaf(b2, bf(v[i]), ob2 * (gi * gi));
-    const float mi = fmaf(b1, bf(m[i]), ob1 * gi);
-    v[i] = tobf(vi);
-    m[i] = tobf(mi);
-    p[i] -= lr_t * mi * rsqrtf(vi + eps);
+    const float gi = sg.grad_f32 ? bf(tobf(static_cast<const float*>(sg.grad)[i]))
+                                 : bf(static_cast<const __nv_bfloat16*>(sg.grad)[i]);
+    const long long j = sg.offset + i;
+    const float vi = fmaf(b2, bf(v[j]), ob2 * (gi * gi));
+    const float mi = fmaf(b1, bf(m[j]), ob1 * gi);
+    v[j] = tobf(vi);
+    m[j] = tobf(mi);
+    const float pj = p[j] - lr_t * mi * rsqrtf(vi + eps);
+    p[j] = pj;
+    sg.weight[i] = tobf(pj);
   }
-}
-
-__global__ void gather_f32_kernel(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst, long long n) {
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
-       i += (long long)gridDim.x * blockDim.x)
-    dst[i] = tobf(src[i]);
-}
-
-__global__ void scatter_kernel(const float* __restrict__ master, __nv_bfloat16* __restrict__ dst, long long n) {
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
-       i += (long long)gridDim.x * blockDim.x)
-    dst[i] = tobf(master[i]);
 }
 
 }  // namespace
@@ -292,8 +441,20 @@ cudaError_t launch_layernorm_forward(const __nv_bfloat16* x, __nv_bfloat16* xn, 
                                      const __nv_bfloat16* gamma, const __nv_bfloat16* beta, float* stdev,
                                      int rows, int cols, float eps, cudaStream_t st) {
   const int wpb = 8;
-  layernorm_forward_kernel<<<(rows + wpb - 1) / wpb, wpb * 32, 0, st>>>(x, xn, out, gamma, beta, stdev, rows,
-                                                                      cols, eps);
+  const dim3 grid((rows + wpb - 1) / wpb), block(wpb * 32);
+  const int nch = (cols + 255) / 256;
+  auto u = [](const void* p) { return reinterpret_cast<const uint4*>(p); };
+  auto um = [](void* p) { return reinterpret_cast<uint4*>(p); };
+  if (cols % 8 == 0 && nch <= 4) {
+    switch (nch) {
+      case 1: layernorm_forward_vec_kernel<1><<<grid, block, 0, st>>>(u(x), um(xn), um(out), u(gamma), u(beta), stdev, rows, cols, eps); break;
+      case 2: layernorm_forward_vec_kernel<2><<<grid, block, 0, st>>>(u(x), um(xn), um(out), u(gamma), u(beta), stdev, rows, cols, eps); break;
+      case 3: layernorm_forward_vec_kernel<3><<<grid, block, 0, st>>>(u(x), um(xn), um(out), u(gamma), u(beta), stdev, rows, cols, eps); break;
+      default: layernorm_forward_vec_kernel<4><<<grid, block, 0, st>>>(u(x), um(xn), um(out), u(gamma), u(beta), stdev, rows, cols, eps); break;
+    }
+  } else {
+    layernorm_forward_kernel<<<grid, block, 0, st>>>(x, xn, out, gamma, beta, stdev, rows, cols, eps);
+  }
   count_launches(1);
   return cudaGetLastError();
 }
@@ -304,10 +465,28 @@ cudaError_t launch_layernorm_backward(__nv_bfloat16* dz, const __nv_bfloat16* xn
   cudaError_t e = cudaMemsetAsync(dgamma, 0, (size_t)cols * sizeof(float), st);
   if (e == cudaSuccess) e = cudaMemsetAsync(dbeta, 0, (size_t)cols * sizeof(float), st);
   if (e != cudaSuccess) return e;
-  int blocks = (rows + LN_WARPS - 1) / LN_WARPS;
-  if (blocks > 148 * 4) blocks = 148 * 4;
-  layernorm_backward_kernel<<<blocks, LN_WARPS * 32, 2 * cols * sizeof(float), st>>>(dz, xn, gamma, stdev,
-                                                                                       dgamma, dbeta, rows, cols);
+  const int nch = (cols + 255) / 256;
+  if (cols % 8 == 0 && nch <= 4) {
+    // two blocks per SM (the register use allows two): enough rows in
+    // flight, few column atomics at the end
+    int blocks = (rows + LN_WARPS - 1) / LN_WARPS;
+    if (blocks > 2 * 148) blocks = 2 * 148;
+    const size_t sm = 2 * cols * sizeof(float);
+    uint4* d = reinterpret_cast<uint4*>(dz);
+    const uint4* n = reinterpret_cast<const uint4*>(xn);
+    const uint4* g = reinterpret_cast<const uint4*>(gamma);
+    switch (nch) {
+      case 1: layernorm_backward_vec_kernel<1><<<blocks, LN_WARPS * 32, sm, st>>>(d, n, g, stdev, dgamma, dbeta, rows, cols); break;
+      case 2: layernorm_backward_vec_kernel<2><<<blocks, LN_WARPS * 32, sm, st>>>(d, n, g, stdev, dgamma, dbeta, rows, cols); break;
+      case 3: layernorm_backward_vec_kernel<3><<<blocks, LN_WARPS * 32, sm, st>>>(d, n, g, stdev, dgamma, dbeta, rows, cols); break;
+      default: layernorm_backward_vec_kernel<4><<<blocks, LN_WARPS * 32, sm, st>>>(d, n, g, stdev, dgamma, dbeta, rows, cols); break;
+    }
+  } else {
+    int blocks = (rows + LN_WARPS - 1) / LN_WARPS;
+    if (blocks > 148 * 4) blocks = 148 * 4;
+    layernorm_backward_kernel<<<blocks, LN_WARPS * 32, 2 * cols * sizeof(float), st>>>(dz, xn, gamma, stdev,
+                                                                                         dgamma, dbeta, rows, cols);
+  }
   count_launches(1);
   return cudaGetLastError();
 }
@@ -358,23 +537,14 @@ cudaError_t launch_loss_backward(const __nv_bfloat16* x, const int* y, const flo
   return cudaGetLastError();
 }
 
-cudaError_t launch_adam(float* p, const __nv_bfloat16* g, __nv_bfloat16* m, __nv_bfloat16* v, long long n,
-                        float lr_t, cudaStream_t st) {
-  adam_kernel<<<ew_blocks(n), EW_THREADS, 0, st>>>(p, g, m, v, n, 0.9f, 0.999f, lr_t, 0.1f, 0.001f, 1e-8f);
+cudaError_t launch_adam_fused(const AdamSegment* segs, int nsegs, long long max_count, float* p,
+                              __nv_bfloat16* m, __nv_bfloat16* v, float lr_t, cudaStream_t st) {
+  if (nsegs <= 0) return cudaSuccess;
+  long long bx = (max_count + 4 * EW_THREADS - 1) / (4 * EW_THREADS);
+  if (bx < 1) bx = 1;
+  adam_fused_kernel<<<dim3((unsigned)bx, (unsigned)nsegs), EW_THREADS, 0, st>>>(segs, p, m, v, 0.9f, 0.999f, lr_t,
+                                                                             0.1f, 0.001f, 1e-8f);
   count_launches(1);
   return cudaGetLastError();
 }
-
-cudaError_t launch_gather_f32(const float* src, __nv_bfloat16* dst, long long n, cudaStream_t st) {
-  gather_f32_kernel<<<ew_blocks(n), EW_THREADS, 0, st>>>(src, dst, n);
-  count_launches(1);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_scatter(const float* master, __nv_bfloat16* dst, long long n, cudaStream_t st) {
-  scatter_kernel<<<ew_blocks(n), EW_THREADS, 0, st>>>(master, dst, n);
-  count_launches(1);
-  return cudaGetLastError();
-}
-
 }  // namespace ma
