@@ -70,6 +70,8 @@ cudaError_t launch_grad_dw(const __nv_bfloat16* x, const float* dq, const __nv_b
 
 cudaError_t launch_gemm_bf16(const __nv_bfloat16* A, bool a_mn, const __nv_bfloat16* B, bool b_mn,
                              __nv_bfloat16* C, int M, int N, int K, uint32_t* status, cudaStream_t st);
+cudaError_t launch_gemm_bf16_act(const __nv_bfloat16* A, const __nv_bfloat16* B, bool b_mn, __nv_bfloat16* C,
+                                 uint8_t* mask, int act, int M, int N, int K, uint32_t* status, cudaStream_t st);
 cudaError_t launch_gemm_splitk_f32(const __nv_bfloat16* A, const __nv_bfloat16* B, float* C, int M, int N,
                                    int K, uint32_t* status, cudaStream_t st);
 cudaError_t launch_grad_dw_splitk(const __nv_bfloat16* x, const float* dq, const __nv_bfloat16* dk,
@@ -97,8 +99,8 @@ cudaError_t launch_layernorm_backward(__nv_bfloat16* dz, const __nv_bfloat16* xn
 cudaError_t launch_residual_add(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_bfloat16* out, long long n,
                                 cudaStream_t st);
 cudaError_t launch_cast_f32_bf16(const float* in, __nv_bfloat16* out, long long n, cudaStream_t st);
-cudaError_t launch_relu_mask(__nv_bfloat16* v, uint8_t* mask, long long n, cudaStream_t st);
-cudaError_t launch_mask_mul(__nv_bfloat16* dv, const uint8_t* mask, long long n, cudaStream_t st);
+
+
 cudaError_t launch_loss_forward(const __nv_bfloat16* x, const int* y, float* out, float* lse, float* mean,
                                 int rows, int cols, cudaStream_t st);
 cudaError_t launch_loss_backward(const __nv_bfloat16* x, const int* y, const float* lse, __nv_bfloat16* dz,

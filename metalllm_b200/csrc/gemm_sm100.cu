@@ -62,6 +62,10 @@ struct GemmArgs {
   const __nv_bfloat16* o_in;
   __nv_bfloat16* d_out;
   int head_dim;
+  // ReLU epilogue (ACT 1): mask [M][N] uint8 written, 1 where the rounded
+  // output is > 0 (mlp.metal:45-51); mask-multiply epilogue (ACT 2): the
+  // rounded output is zeroed where the mask is 0
+  uint8_t* mask;
   uint32_t* status;
 };
 
@@ -96,7 +100,7 @@ __device__ __forceinline__ float dot_bf16x8(uint4 a, uint4 b) {
   return s;
 }
 
-template <int BN, bool A_MN, bool B_MN, bool HAS_F32, bool FUSE_D = false>
+template <int BN, bool A_MN, bool B_MN, bool HAS_F32, bool FUSE_D = false, int ACT = 0>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_kernel(const __grid_constant__ GemmMaps maps, const GemmArgs args) {
   using C = GemmCfg<BN, HAS_F32>;
@@ -307,6 +311,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           v1.y = pack_bf16(__uint_as_float(r[10]), __uint_as_float(r[11]));
           v1.z = pack_bf16(__uint_as_float(r[12]), __uint_as_float(r[13]));
           v1.w = pack_bf16(__uint_as_float(r[14]), __uint_as_float(r[15]));
+          if constexpr (ACT != 0) {  // on the rounded values, as the separate kernels do
+            if (grow < args.M) {
+              uint8_t* mp = args.mask + (size_t)grow * args.N + col0 + cc;
+              uint4 mk = ACT == 2 ? *reinterpret_cast<const uint4*>(mp) : make_uint4(0, 0, 0, 0);
+              uint32_t* w = reinterpret_cast<uint32_t*>(&v0);  // v0, v1: 8 words, 16 values
+              uint32_t* wb = reinterpret_cast<uint32_t*>(&v1);
+              uint8_t* mb = reinterpret_cast<uint8_t*>(&mk);
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                uint32_t& word = j < 8 ? w[j / 2] : wb[(j - 8) / 2];
+                const int sh = 16 * (j & 1);
+                const uint32_t h = (word >> sh) & 0xFFFFu;
+                // ACT 1: x > 0 (not negative, not zero, not NaN); ACT 2: mask set
+                const bool on = ACT == 1 ? (!(h & 0x8000u) && (h & 0x7FFFu) != 0 && (h & 0x7FFFu) <= 0x7F80u)
+                                         : mb[j] != 0;
+                if (!on) word &= ~(0xFFFFu << sh);
+                if (ACT == 1) mb[j] = on ? 1 : 0;
+              }
+              if (ACT == 1) *reinterpret_cast<uint4*>(mp) = mk;
+            }
+          }
           const int ch = (cc % 64) / 8;
           *reinterpret_cast<uint4*>(rowp + ((ch ^ (row & 7)) * 16)) = v0;
           *reinterpret_cast<uint4*>(rowp + (((ch + 1) ^ (row & 7)) * 16)) = v1;
@@ -369,11 +394,11 @@ bool make_operand_map(CUtensorMap* m, const Operand& o, bool mn_major, uint64_t 
   return make_tmap_2d(m, o.ptr, t, eb, outer, K, inner_box, BK, sw);
 }
 
-template <int BN, bool A_MN, bool B_MN, bool HAS_F32, bool FUSE_D = false>
+template <int BN, bool A_MN, bool B_MN, bool HAS_F32, bool FUSE_D = false, int ACT = 0>
 cudaError_t run_gemm(const Operand* A, int na, const Operand* Bop, int nb, void* const* Cptr,
                      const bool* c_f32, int nz, int nseg, int M, int N, int K, uint32_t* status,
                      cudaStream_t st, int ksplit = 1, const __nv_bfloat16* o_in = nullptr,
-                     __nv_bfloat16* d_out = nullptr, int head_dim = 0) {
+                     __nv_bfloat16* d_out = nullptr, int head_dim = 0, uint8_t* mask = nullptr) {
   using Cfg = GemmCfg<BN, HAS_F32>;
   GemmMaps maps;
   memset(&maps, 0, sizeof(maps));
@@ -388,6 +413,9 @@ cudaError_t run_gemm(const Operand* A, int na, const Operand* Bop, int nb, void*
   args.o_in = o_in;
   args.d_out = d_out;
   args.head_dim = head_dim;
+  args.mask = mask;
+  if (ACT != 0 && (!mask || nz != 1 || c_f32[0] || ksplit > 1 || N % 16 || (reinterpret_cast<uintptr_t>(mask) & 15)))
+    return cudaErrorInvalidValue;
   if (FUSE_D && (!o_in || !d_out || head_dim <= 0 || BN % 16 || N % head_dim || head_dim % 16 ||
                  nz != 1 || c_f32[0]))
     return cudaErrorInvalidValue;
@@ -423,7 +451,7 @@ cudaError_t run_gemm(const Operand* A, int na, const Operand* Bop, int nb, void*
                                        CU_TENSOR_MAP_SWIZZLE_128B);
     if (!ok) return cudaErrorInvalidValue;
   }
-  auto kern = gemm_kernel<BN, A_MN, B_MN, HAS_F32, FUSE_D>;
+  auto kern = gemm_kernel<BN, A_MN, B_MN, HAS_F32, FUSE_D, ACT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
   if (e != cudaSuccess) return e;
   const dim3 grid((M + BM - 1) / BM, (N + BN - 1) / BN, nz * args.ksplit);
@@ -458,6 +486,32 @@ cudaError_t launch_gemm_bf16(const __nv_bfloat16* A, bool a_mn, const __nv_bfloa
   }
 #undef MA_GEMM_CASE
   return cudaErrorInvalidValue;  // A MN-major with B K-major is not needed
+}
+
+// The training step's MLP GEMMs with their element-wise step in the epilogue
+// (A K-major, B MN-major): act = 1, C = relu(A . B) and mask = (C > 0)
+// (mlp.metal:45-51); act = 2, C = (A . B) where mask is set, else 0 (the
+// backward's mask multiply).  Same values as launch_gemm_bf16 followed by
+// the separate relu / mask kernels.
+cudaError_t launch_gemm_bf16_act(const __nv_bfloat16* A, const __nv_bfloat16* B, bool b_mn, __nv_bfloat16* C,
+                                 uint8_t* mask, int act, int M, int N, int K, uint32_t* status, cudaStream_t st) {
+  const Operand a{A, false}, b{B, false};
+  void* c[1] = {C};
+  const bool cf[1] = {false};
+  const bool wide = (long long)((M + 127) / 128) * ((N + 127) / 128) >= 148;
+#define MA_GEMM_ACT(BN_, BMN, ACT_)                                                                         \
+  if (b_mn == BMN && act == ACT_)                                                                          \
+    return run_gemm<BN_, false, BMN, false, false, ACT_>(&a, 1, &b, 1, c, cf, 1, 1, M, N, K, status, st, 1, \
+                                                         nullptr, nullptr, 0, mask);
+  if (wide) {
+    MA_GEMM_ACT(128, true, 1)
+    MA_GEMM_ACT(128, false, 2)
+  } else {
+    MA_GEMM_ACT(64, true, 1)
+    MA_GEMM_ACT(64, false, 2)
+  }
+#undef MA_GEMM_ACT
+  return cudaErrorInvalidValue;
 }
 
 // Split-K GEMM into an fp32 output (zeroed here): C[M][N] = A . B with both

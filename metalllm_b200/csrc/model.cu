@@ -316,8 +316,8 @@ int ma_model_forward(ma_model* m, const int32_t* tokens, const int32_t* targets,
     MA_M_CUDA(launch_residual_add(hidden, y.proj_out, y.res1, (long long)R * E, st), "residualAdd");
     MA_M_CUDA(launch_layernorm_forward(y.res1, y.ln2.xn, y.ln2.out, y.ln2.gamma, y.ln2.beta, y.ln2.stdev, R, E,
                                        1e-5f, st), "layernormForward");
-    MA_M_CUDA(launch_gemm_bf16(y.ln2.out, false, y.up, true, y.mlp_v, R, H, E, m->status, st), "mlpForwardOne");
-    MA_M_CUDA(launch_relu_mask(y.mlp_v, y.mask, (long long)R * H, st), "mlpForwardOne relu");
+    MA_M_CUDA(launch_gemm_bf16_act(y.ln2.out, y.up, true, y.mlp_v, y.mask, 1, R, H, E, m->status, st),
+              "mlpForwardOne + relu");
     MA_M_CUDA(launch_gemm_bf16(y.mlp_v, false, y.dp, true, y.mlp_out, R, E, H, m->status, st), "mlpForwardTwo");
     MA_M_CUDA(launch_residual_add(y.res1, y.mlp_out, y.res2, (long long)R * E, st), "residualAdd");
     hidden = y.res2;
@@ -357,9 +357,8 @@ int ma_model_backward(ma_model* m, ma_stream_t stream) {
     Layer& y = m->layers[n];
     // MLP: dV = (dStream . Dp^T) * mask; dUp = ln2.out^T . dV; dDp = V^T . dStream;
     // dBranch = dV . Up^T
-    MA_M_CUDA(launch_gemm_bf16(m->dstream, false, y.dp, false, m->dmlpv, R, H, E, m->status, st),
-              "mlpBackwardOne");
-    MA_M_CUDA(launch_mask_mul(m->dmlpv, y.mask, (long long)R * H, st), "mlpBackwardOne mask");
+    MA_M_CUDA(launch_gemm_bf16_act(m->dstream, y.dp, false, m->dmlpv, y.mask, 2, R, H, E, m->status, st),
+              "mlpBackwardOne + mask");
     MA_M_CUDA(wgrad(m, y.ln2.out, m->dmlpv, y.dup, E, H, st), "mlpBackwardTwo dUp");
     MA_M_CUDA(wgrad(m, y.mlp_v, m->dstream, y.ddp, H, E, st), "mlpBackwardTwo dDp");
     MA_M_CUDA(launch_gemm_bf16(m->dmlpv, false, y.up, false, m->dbranch, R, E, H, m->status, st),

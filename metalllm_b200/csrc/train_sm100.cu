@@ -4,10 +4,11 @@
 //                          model.h:438; the positional gradient is the batch
 //                          sum of the embedding-output gradient, model.h:284)
 //   layernormForward/Backward  layernorm.metal:10-127
-//   residualAdd, castFloatToBfloat, gather/scatter  elementwise.metal:7-71
-//   ReLU mask of mlpForwardOne / mlpBackwardOne     mlp.metal:20-56, 89-122
+//   residualAdd, castFloatToBfloat  elementwise.metal:7-71
 //   lossForward/Backward   loss.metal:9-75 (mean over rows)
-//   MetalStep (Adam)       optimstep.metal:15-42
+//   MetalStep (Adam) with the gradient gather and weight scatter of
+//   model.h:726-757 in one pass   optimstep.metal:15-42
+// (the ReLU and mask multiply of mlp.metal:45-51, 116-121 are GEMM epilogues).
 // They are memory-bound: 16-byte vector accesses, one warp per row for the
 // row reductions (fp32 math), block partial sums + one atomic per column and
 // block for the LayerNorm parameter gradients.
@@ -316,24 +317,6 @@ __global__ void cast_kernel(const float4* __restrict__ in, uint2* __restrict__ o
   }
 }
 
-// v = relu(v) in place, mask = (v > 0)   (mlp.metal:45-51)
-__global__ void relu_mask_kernel(__nv_bfloat16* __restrict__ v, uint8_t* __restrict__ mask, long long n) {
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
-       i += (long long)gridDim.x * blockDim.x) {
-    const float x = bf(v[i]);
-    const bool on = x > 0.0f;
-    mask[i] = on ? 1 : 0;
-    v[i] = on ? v[i] : tobf(0.0f);
-  }
-}
-
-// dV *= mask   (mlp.metal:116-121)
-__global__ void mask_mul_kernel(__nv_bfloat16* __restrict__ dv, const uint8_t* __restrict__ mask, long long n) {
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
-       i += (long long)gridDim.x * blockDim.x)
-    if (!mask[i]) dv[i] = tobf(0.0f);
-}
-
 // ---------------------------------------------------------------- loss
 // One warp per row: lse = max + ln(sum exp(x - max)); out = lse - x[y]
 // (loss.metal:9-59).
@@ -505,18 +488,6 @@ cudaError_t launch_cast_f32_bf16(const float* in, __nv_bfloat16* out, long long 
   const long long n4 = n / 4;
   cast_kernel<<<ew_blocks(n4), EW_THREADS, 0, st>>>(reinterpret_cast<const float4*>(in),
                                                     reinterpret_cast<uint2*>(out), n4);
-  count_launches(1);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_relu_mask(__nv_bfloat16* v, uint8_t* mask, long long n, cudaStream_t st) {
-  relu_mask_kernel<<<ew_blocks(n), EW_THREADS, 0, st>>>(v, mask, n);
-  count_launches(1);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_mask_mul(__nv_bfloat16* dv, const uint8_t* mask, long long n, cudaStream_t st) {
-  mask_mul_kernel<<<ew_blocks(n), EW_THREADS, 0, st>>>(dv, mask, n);
   count_launches(1);
   return cudaGetLastError();
 }
