@@ -75,9 +75,10 @@ struct GemmCfg {
   static constexpr uint32_t B_BYTES = BN * BK * 2;             // 8 / 16 KB
   static constexpr uint32_t F32_BYTES = HAS_F32 ? 2 * (BM > BN ? BM : BN) * 128 : 0;  // 32 KB
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES + F32_BYTES;
-  // three stages of 32 KB at BN = 128 leave room for two CTAs per SM, so one
-  // CTA's epilogue overlaps the other's main loop
-  static constexpr int STAGES = (HAS_F32 || BN == 128) ? 3 : 4;
+  // three stages leave room for two CTAs per SM at BN = 128 (32 KB stages)
+  // and three at BN = 64 (24 KB), so one CTA's epilogue overlaps another's
+  // main loop
+  static constexpr int STAGES = 3;
   static constexpr uint32_t OFF_BAR = STAGES * STAGE_BYTES;
   // full[S], empty[S], converted[S], done
   static constexpr uint32_t OFF_TSLOT = OFF_BAR + (3 * STAGES + 1) * 8;
