@@ -71,13 +71,14 @@ cudaError_t launch_grad_dw(const __nv_bfloat16* x, const float* dq, const __nv_b
 cudaError_t launch_gemm_bf16(const __nv_bfloat16* A, bool a_mn, const __nv_bfloat16* B, bool b_mn,
                              __nv_bfloat16* C, int M, int N, int K, uint32_t* status, cudaStream_t st);
 cudaError_t launch_gemm_bf16_act(const __nv_bfloat16* A, const __nv_bfloat16* B, bool b_mn, __nv_bfloat16* C,
-                                 uint8_t* mask, int act, int M, int N, int K, uint32_t* status, cudaStream_t st);
+                                 uint8_t* mask, const __nv_bfloat16* res, int act, int M, int N, int K,
+                                 uint32_t* status, cudaStream_t st);
 cudaError_t launch_gemm_splitk_f32(const __nv_bfloat16* A, const __nv_bfloat16* B, float* C, int M, int N,
                                    int K, uint32_t* status, cudaStream_t st);
 cudaError_t launch_grad_dw_splitk(const __nv_bfloat16* x, const float* dq, const __nv_bfloat16* dk,
                                   const __nv_bfloat16* dv, float* dqw, __nv_bfloat16* dkw, __nv_bfloat16* dvw,
                                   float* ws, int rows, int n, uint32_t* status, cudaStream_t st);
-cudaError_t launch_grad_dx_bf16(float* dx, const __nv_bfloat16* qw, const __nv_bfloat16* kw,
+cudaError_t launch_grad_dx_bf16(void* dx, bool dx_f32, const __nv_bfloat16* qw, const __nv_bfloat16* kw,
                                 const __nv_bfloat16* vw, const __nv_bfloat16* dq16, const __nv_bfloat16* dk,
                                 const __nv_bfloat16* dv, int rows, int n, uint32_t* status, cudaStream_t st);
 cudaError_t launch_grad_dw_splitk_bf16(const __nv_bfloat16* x, const __nv_bfloat16* dq16, const __nv_bfloat16* dk,
@@ -93,11 +94,12 @@ cudaError_t launch_embed_backward(const int* tok, const __nv_bfloat16* dz, float
 cudaError_t launch_layernorm_forward(const __nv_bfloat16* x, __nv_bfloat16* xn, __nv_bfloat16* out,
                                      const __nv_bfloat16* gamma, const __nv_bfloat16* beta, float* stdev,
                                      int rows, int cols, float eps, cudaStream_t st);
+// res (optional): dX is rounded to bf16 and res added (the residualAdd that
+// follows the LayerNorm backward in model.h), one more rounding.
 cudaError_t launch_layernorm_backward(__nv_bfloat16* dz, const __nv_bfloat16* xn, const __nv_bfloat16* gamma,
                                       const float* stdev, float* dgamma, float* dbeta, int rows, int cols,
-                                      cudaStream_t st);
-cudaError_t launch_residual_add(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_bfloat16* out, long long n,
-                                cudaStream_t st);
+                                      cudaStream_t st, const __nv_bfloat16* res = nullptr);
+
 cudaError_t launch_cast_f32_bf16(const float* in, __nv_bfloat16* out, long long n, cudaStream_t st);
 
 

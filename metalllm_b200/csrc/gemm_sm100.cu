@@ -64,8 +64,11 @@ struct GemmArgs {
   int head_dim;
   // ReLU epilogue (ACT 1): mask [M][N] uint8 written, 1 where the rounded
   // output is > 0 (mlp.metal:45-51); mask-multiply epilogue (ACT 2): the
-  // rounded output is zeroed where the mask is 0
+  // rounded output is zeroed where the mask is 0; residual epilogue (ACT 3):
+  // C = bf16(res + bf16(A . B)), res [M][N] bf16 (elementwise.metal's
+  // residualAdd after the GEMM)
   uint8_t* mask;
+  const __nv_bfloat16* res;
   uint32_t* status;
 };
 
@@ -89,6 +92,20 @@ struct GemmCfg {
 };
 
 __device__ __forceinline__ int bit_of(uint32_t m, int i) { return (m >> i) & 1u; }
+
+// bf16(float(a) + float(b)) elementwise over 8 bf16 values (round to nearest even)
+__device__ __forceinline__ uint4 add_bf16x8(uint4 a, uint4 b) {
+  const __nv_bfloat162* x = reinterpret_cast<const __nv_bfloat162*>(&a);
+  const __nv_bfloat162* y = reinterpret_cast<const __nv_bfloat162*>(&b);
+  uint4 r;
+  __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(&r);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 fx = __bfloat1622float2(x[i]), fy = __bfloat1622float2(y[i]);
+    o[i] = __floats2bfloat162_rn(fy.x + fx.x, fy.y + fx.y);
+  }
+  return r;
+}
 
 __device__ __forceinline__ float dot_bf16x8(uint4 a, uint4 b) {
   const __nv_bfloat162* x = reinterpret_cast<const __nv_bfloat162*>(&a);
@@ -314,7 +331,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           v1.y = pack_bf16(__uint_as_float(r[10]), __uint_as_float(r[11]));
           v1.z = pack_bf16(__uint_as_float(r[12]), __uint_as_float(r[13]));
           v1.w = pack_bf16(__uint_as_float(r[14]), __uint_as_float(r[15]));
-          if constexpr (ACT != 0) {  // on the rounded values, as the separate kernels do
+          if constexpr (ACT == 3) {  // residual add on the rounded values
+            if (grow < args.M) {
+              const uint4* rp = reinterpret_cast<const uint4*>(args.res + (size_t)grow * args.N + col0 + cc);
+              const uint4 ra = __ldg(rp), rb = __ldg(rp + 1);
+              v0 = add_bf16x8(v0, ra);
+              v1 = add_bf16x8(v1, rb);
+            }
+          }
+          if constexpr (ACT == 1 || ACT == 2) {  // on the rounded values, as the separate kernels do
             if (grow < args.M) {
               uint8_t* mp = args.mask + (size_t)grow * args.N + col0 + cc;
               uint4 mk = ACT == 2 ? *reinterpret_cast<const uint4*>(mp) : make_uint4(0, 0, 0, 0);
@@ -401,7 +426,8 @@ template <int BN, bool A_MN, bool B_MN, bool HAS_F32, bool FUSE_D = false, int A
 cudaError_t run_gemm(const Operand* A, int na, const Operand* Bop, int nb, void* const* Cptr,
                      const bool* c_f32, int nz, int nseg, int M, int N, int K, uint32_t* status,
                      cudaStream_t st, int ksplit = 1, const __nv_bfloat16* o_in = nullptr,
-                     __nv_bfloat16* d_out = nullptr, int head_dim = 0, uint8_t* mask = nullptr) {
+                     __nv_bfloat16* d_out = nullptr, int head_dim = 0, uint8_t* mask = nullptr,
+                     const __nv_bfloat16* res = nullptr) {
   using Cfg = GemmCfg<BN, HAS_F32>;
   GemmMaps maps;
   memset(&maps, 0, sizeof(maps));
@@ -417,7 +443,10 @@ cudaError_t run_gemm(const Operand* A, int na, const Operand* Bop, int nb, void*
   args.d_out = d_out;
   args.head_dim = head_dim;
   args.mask = mask;
-  if (ACT != 0 && (!mask || nz != 1 || c_f32[0] || ksplit > 1 || N % 16 || (reinterpret_cast<uintptr_t>(mask) & 15)))
+  args.res = res;
+  if (ACT == 3 && (!res || nz != 1 || c_f32[0] || ksplit > 1 || N % 16 || (reinterpret_cast<uintptr_t>(res) & 15)))
+    return cudaErrorInvalidValue;
+  if ((ACT == 1 || ACT == 2) && (!mask || nz != 1 || c_f32[0] || ksplit > 1 || N % 16 || (reinterpret_cast<uintptr_t>(mask) & 15)))
     return cudaErrorInvalidValue;
   if (FUSE_D && (!o_in || !d_out || head_dim <= 0 || BN % 16 || N % head_dim || head_dim % 16 ||
                  nz != 1 || c_f32[0]))
@@ -492,12 +521,14 @@ cudaError_t launch_gemm_bf16(const __nv_bfloat16* A, bool a_mn, const __nv_bfloa
 }
 
 // The training step's MLP GEMMs with their element-wise step in the epilogue
-// (A K-major, B MN-major): act = 1, C = relu(A . B) and mask = (C > 0)
-// (mlp.metal:45-51); act = 2, C = (A . B) where mask is set, else 0 (the
-// backward's mask multiply).  Same values as launch_gemm_bf16 followed by
-// the separate relu / mask kernels.
+// (A K-major): act = 1, C = relu(A . B) and mask = (C > 0) (mlp.metal:45-51,
+// B MN-major); act = 2, C = (A . B) where mask is set, else 0 (the backward's
+// mask multiply, B K-major); act = 3, C = res + A . B (the residual add after
+// projForward / mlpForwardTwo, B MN-major).  Same values as launch_gemm_bf16
+// followed by the separate element-wise kernels.
 cudaError_t launch_gemm_bf16_act(const __nv_bfloat16* A, const __nv_bfloat16* B, bool b_mn, __nv_bfloat16* C,
-                                 uint8_t* mask, int act, int M, int N, int K, uint32_t* status, cudaStream_t st) {
+                                 uint8_t* mask, const __nv_bfloat16* res, int act, int M, int N, int K,
+                                 uint32_t* status, cudaStream_t st) {
   const Operand a{A, false}, b{B, false};
   void* c[1] = {C};
   const bool cf[1] = {false};
@@ -505,13 +536,15 @@ cudaError_t launch_gemm_bf16_act(const __nv_bfloat16* A, const __nv_bfloat16* B,
 #define MA_GEMM_ACT(BN_, BMN, ACT_)                                                                         \
   if (b_mn == BMN && act == ACT_)                                                                          \
     return run_gemm<BN_, false, BMN, false, false, ACT_>(&a, 1, &b, 1, c, cf, 1, 1, M, N, K, status, st, 1, \
-                                                         nullptr, nullptr, 0, mask);
+                                                         nullptr, nullptr, 0, mask, res);
   if (wide) {
     MA_GEMM_ACT(128, true, 1)
     MA_GEMM_ACT(128, false, 2)
+    MA_GEMM_ACT(128, true, 3)
   } else {
     MA_GEMM_ACT(64, true, 1)
     MA_GEMM_ACT(64, false, 2)
+    MA_GEMM_ACT(64, true, 3)
   }
 #undef MA_GEMM_ACT
   return cudaErrorInvalidValue;
@@ -619,13 +652,13 @@ cudaError_t launch_grad_dw(const __nv_bfloat16* x, const float* dq, const __nv_b
 // The same two products with dQ already rounded to bf16 (the rounding the
 // fp32-operand path applies in shared memory, so the results are identical):
 // the all-bf16 kernel without the in-kernel conversion.
-cudaError_t launch_grad_dx_bf16(float* dx, const __nv_bfloat16* qw, const __nv_bfloat16* kw,
+cudaError_t launch_grad_dx_bf16(void* dx, bool dx_f32, const __nv_bfloat16* qw, const __nv_bfloat16* kw,
                                 const __nv_bfloat16* vw, const __nv_bfloat16* dq16, const __nv_bfloat16* dk,
                                 const __nv_bfloat16* dv, int rows, int n, uint32_t* status, cudaStream_t st) {
   const Operand a[3] = {{dq16, false}, {dk, false}, {dv, false}};
   const Operand b[3] = {{qw, false}, {kw, false}, {vw, false}};
   void* c[1] = {dx};
-  const bool cf[1] = {true};
+  const bool cf[1] = {dx_f32};
   return run_gemm<128, false, false, false>(a, 3, b, 3, c, cf, 1, 3, rows, n, n, status, st);
 }
 

@@ -39,7 +39,7 @@ struct LayerNormBufs {
 struct Layer {
   LayerNormBufs ln1, ln2;
   bf16 *qw, *kw, *vw, *projw, *up, *dp;
-  bf16 *q, *k, *v, *attn, *proj_out, *res1, *mlp_v, *mlp_out, *res2;
+  bf16 *q, *k, *v, *attn, *res1, *mlp_v, *res2;
   float* l;
   uint8_t* mask;
   float* dqw;
@@ -61,7 +61,7 @@ struct ma_model {
   __nv_bfloat16 *dstream = nullptr, *dbranch = nullptr, *dzattn = nullptr, *dattnd = nullptr;
   __nv_bfloat16 *dk = nullptr, *dv = nullptr, *dmlpv = nullptr, *dpos = nullptr, *dlinw = nullptr;
   __nv_bfloat16* dq16 = nullptr;  // dQ rounded to bf16 for computeGradDx/Dw
-  float *dq = nullptr, *dxattn = nullptr, *demb = nullptr;
+  float *dq = nullptr, *demb = nullptr;
   float* ws = nullptr;  // fp32 workspace of the split-K weight-gradient GEMMs
   float *loss_rows = nullptr, *lse_rows = nullptr, *loss_mean = nullptr;
   const int* tokens = nullptr;   // last forward's inputs (device)
@@ -221,11 +221,9 @@ int ma_model_create(const MaModelConfig* c, ma_model** out) {
     ALLOC(y.v, R * E);
     ALLOC(y.attn, R * E);
     ALLOC(y.l, R * m->NH);
-    ALLOC(y.proj_out, R * E);
     ALLOC(y.res1, R * E);
     ALLOC(y.mlp_v, R * H);
     ALLOC(y.mask, R * H);
-    ALLOC(y.mlp_out, R * E);
     ALLOC(y.res2, R * E);
   }
   if ((e = ln_bufs(m->lnf))) return fail(e, "cudaMalloc");
@@ -245,7 +243,6 @@ int ma_model_create(const MaModelConfig* c, ma_model** out) {
   ALLOC(m->dq16, R * E);
   ALLOC(m->dk, R * E);
   ALLOC(m->dv, R * E);
-  ALLOC(m->dxattn, R * E);
   ALLOC(m->dmlpv, R * H);
   ALLOC(m->ws, std::max(std::max(E * H, 2 * E * E), E * V));
   ALLOC(m->loss_rows, R);
@@ -312,14 +309,15 @@ int ma_model_forward(ma_model* m, const int32_t* tokens, const int32_t* targets,
                                        1e-5f, st), "layernormForward");
     MA_M_CUDA(launch_qkv(y.ln1.out, y.q, y.k, y.v, y.qw, y.kw, y.vw, R, E, m->status, st), "computeQKV");
     MA_M_CUDA(launch_flash_fwd(y.q, y.k, y.v, y.attn, y.l, s, m->status, st), "flashAttentionForward");
-    MA_M_CUDA(launch_proj_forward(y.attn, y.projw, y.proj_out, R, E, m->status, st), "projForward");
-    MA_M_CUDA(launch_residual_add(hidden, y.proj_out, y.res1, (long long)R * E, st), "residualAdd");
+    // projForward with the residual add in its epilogue: res1 = hidden + attn . projw
+    MA_M_CUDA(launch_gemm_bf16_act(y.attn, y.projw, true, y.res1, nullptr, hidden, 3, R, E, E, m->status, st),
+              "projForward + residualAdd");
     MA_M_CUDA(launch_layernorm_forward(y.res1, y.ln2.xn, y.ln2.out, y.ln2.gamma, y.ln2.beta, y.ln2.stdev, R, E,
                                        1e-5f, st), "layernormForward");
-    MA_M_CUDA(launch_gemm_bf16_act(y.ln2.out, y.up, true, y.mlp_v, y.mask, 1, R, H, E, m->status, st),
+    MA_M_CUDA(launch_gemm_bf16_act(y.ln2.out, y.up, true, y.mlp_v, y.mask, nullptr, 1, R, H, E, m->status, st),
               "mlpForwardOne + relu");
-    MA_M_CUDA(launch_gemm_bf16(y.mlp_v, false, y.dp, true, y.mlp_out, R, E, H, m->status, st), "mlpForwardTwo");
-    MA_M_CUDA(launch_residual_add(y.res1, y.mlp_out, y.res2, (long long)R * E, st), "residualAdd");
+    MA_M_CUDA(launch_gemm_bf16_act(y.mlp_v, y.dp, true, y.res2, nullptr, y.res1, 3, R, E, H, m->status, st),
+              "mlpForwardTwo + residualAdd");
     hidden = y.res2;
   }
   MA_M_CUDA(launch_layernorm_forward(hidden, m->lnf.xn, m->lnf.out, m->lnf.gamma, m->lnf.beta, m->lnf.stdev, R,
@@ -357,15 +355,15 @@ int ma_model_backward(ma_model* m, ma_stream_t stream) {
     Layer& y = m->layers[n];
     // MLP: dV = (dStream . Dp^T) * mask; dUp = ln2.out^T . dV; dDp = V^T . dStream;
     // dBranch = dV . Up^T
-    MA_M_CUDA(launch_gemm_bf16_act(m->dstream, y.dp, false, m->dmlpv, y.mask, 2, R, H, E, m->status, st),
+    MA_M_CUDA(launch_gemm_bf16_act(m->dstream, y.dp, false, m->dmlpv, y.mask, nullptr, 2, R, H, E, m->status, st),
               "mlpBackwardOne + mask");
     MA_M_CUDA(wgrad(m, y.ln2.out, m->dmlpv, y.dup, E, H, st), "mlpBackwardTwo dUp");
     MA_M_CUDA(wgrad(m, y.mlp_v, m->dstream, y.ddp, H, E, st), "mlpBackwardTwo dDp");
     MA_M_CUDA(launch_gemm_bf16(m->dmlpv, false, y.up, false, m->dbranch, R, E, H, m->status, st),
               "mlpBackwardTwo dX");
+    // LayerNorm backward with the residual add: dbranch = dLN2 + dstream
     MA_M_CUDA(launch_layernorm_backward(m->dbranch, y.ln2.xn, y.ln2.gamma, y.ln2.stdev, y.ln2.dgamma,
-                                        y.ln2.dbeta, R, E, st), "layernormBackward");
-    MA_M_CUDA(launch_residual_add(m->dbranch, m->dstream, m->dbranch, (long long)R * E, st), "residualAdd");
+                                        y.ln2.dbeta, R, E, st, m->dstream), "layernormBackward + residualAdd");
     // attention block
     MA_M_CUDA(wgrad(m, y.attn, m->dbranch, y.dprojw, E, E, st), "projBackwarddW");
     // projBackwarddX with computeD fused into its epilogue
@@ -376,14 +374,13 @@ int ma_model_backward(ma_model* m, ma_stream_t stream) {
     // dQ rounded to bf16 once for both products (their fp32-operand kernels
     // apply the same rounding on chip)
     MA_M_CUDA(launch_cast_f32_bf16(m->dq, m->dq16, (long long)R * E, st), "castFloatToBfloat dQ");
-    MA_M_CUDA(launch_grad_dx_bf16(m->dxattn, y.qw, y.kw, y.vw, m->dq16, m->dk, m->dv, R, E, m->status, st),
-              "computeGradDx");
+    // dX straight to bf16 (the fp32 dX rounded by castFloatToBfloat gives the same values)
+    MA_M_CUDA(launch_grad_dx_bf16(m->dstream, false, y.qw, y.kw, y.vw, m->dq16, m->dk, m->dv, R, E, m->status, st),
+              "computeGradDx + castFloatToBfloat");
     MA_M_CUDA(launch_grad_dw_splitk_bf16(y.ln1.out, m->dq16, m->dk, m->dv, y.dqw, y.dkw, y.dvw, m->ws, R, E,
                                          m->status, st), "computeGradDw");
-    MA_M_CUDA(launch_cast_f32_bf16(m->dxattn, m->dstream, (long long)R * E, st), "castFloatToBfloat");
     MA_M_CUDA(launch_layernorm_backward(m->dstream, y.ln1.xn, y.ln1.gamma, y.ln1.stdev, y.ln1.dgamma,
-                                        y.ln1.dbeta, R, E, st), "layernormBackward");
-    MA_M_CUDA(launch_residual_add(m->dstream, m->dbranch, m->dstream, (long long)R * E, st), "residualAdd");
+                                        y.ln1.dbeta, R, E, st, m->dbranch), "layernormBackward + residualAdd");
   }
   MA_M_CUDA(launch_embed_backward(m->tokens, m->dstream, m->demb, m->dpos, m->Bt, m->T, V, E, st),
             "embedBackward");
@@ -439,7 +436,7 @@ int ma_model_tensor(ma_model* m, const char* name, void** ptr, uint64_t* bytes) 
     void* p;
     size_t bytes;
   } scratch[] = {{"dmlpv", m->dmlpv, R * H * 2}, {"dbranch", m->dbranch, R * E * 2},
-                 {"dzattn", m->dzattn, R * E * 2}, {"dxattn", m->dxattn, R * E * 4},
+                 {"dzattn", m->dzattn, R * E * 2},
                  {"dlogits", m->dlogits, R * V * 2}};
   for (const auto& x : scratch) {
     if (n == x.name) {

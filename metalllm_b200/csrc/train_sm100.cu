@@ -4,7 +4,8 @@
 //                          model.h:438; the positional gradient is the batch
 //                          sum of the embedding-output gradient, model.h:284)
 //   layernormForward/Backward  layernorm.metal:10-127
-//   residualAdd, castFloatToBfloat  elementwise.metal:7-71
+//   castFloatToBfloat      elementwise.metal:7-71 (residualAdd is fused into
+//                          the GEMM and LayerNorm-backward epilogues)
 //   lossForward/Backward   loss.metal:9-75 (mean over rows)
 //   MetalStep (Adam) with the gradient gather and weight scatter of
 //   model.h:726-757 in one pass   optimstep.metal:15-42
@@ -104,7 +105,7 @@ constexpr int LN_WARPS = 8;
 __global__ void layernorm_backward_kernel(__nv_bfloat16* __restrict__ dz, const __nv_bfloat16* __restrict__ xn,
                                           const __nv_bfloat16* __restrict__ gamma, const float* __restrict__ stdev,
                                           float* __restrict__ dgamma, float* __restrict__ dbeta, int rows,
-                                          int cols) {
+                                          int cols, const __nv_bfloat16* __restrict__ res) {
   extern __shared__ float red[];  // [2][cols]
   for (int c = threadIdx.x; c < 2 * cols; c += blockDim.x) red[c] = 0.0f;
   __syncthreads();
@@ -129,7 +130,8 @@ __global__ void layernorm_backward_kernel(__nv_bfloat16* __restrict__ dz, const 
     __syncwarp();
     for (int c = lane; c < cols; c += 32) {
       const float g = bf(dr[c]) * bf(gamma[c]);
-      dr[c] = tobf(rs * (g - m1 - bf(nr[c]) * m2));
+      const __nv_bfloat16 x = tobf(rs * (g - m1 - bf(nr[c]) * m2));
+      dr[c] = res ? tobf(bf(x) + bf(res[(long long)row * cols + c])) : x;
     }
   }
   __syncthreads();
@@ -222,7 +224,7 @@ template <int NCH>
 __global__ void layernorm_backward_vec_kernel(uint4* __restrict__ dz, const uint4* __restrict__ xn,
                                               const uint4* __restrict__ gamma, const float* __restrict__ stdev,
                                               float* __restrict__ dgamma, float* __restrict__ dbeta, int rows,
-                                              int cols) {
+                                              int cols, const uint4* __restrict__ res) {
   extern __shared__ float red[];  // [2][cols]
   for (int c = threadIdx.x; c < 2 * cols; c += blockDim.x) red[c] = 0.0f;
   const int lane = threadIdx.x % 32, w = threadIdx.x / 32, nw = blockDim.x / 32;
@@ -267,6 +269,12 @@ __global__ void layernorm_backward_vec_kernel(uint4* __restrict__ dz, const uint
         float r[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) r[i] = rs * (d[k][i] * gm[k][i] - m1 - n[k][i] * m2);
+        if (res) {  // the following residual add, on the rounded dX
+          float q[8];
+          unpack8(res[rb + c], q);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) r[i] = __bfloat162float(__float2bfloat16_rn(r[i])) + q[i];
+        }
         dz[rb + c] = pack8(r);
       }
     }
@@ -290,23 +298,6 @@ __global__ void layernorm_backward_vec_kernel(uint4* __restrict__ dz, const uint
 }
 
 // ---------------------------------------------------------------- glue
-__global__ void residual_add_kernel(const uint4* __restrict__ a, const uint4* __restrict__ b,
-                                    uint4* __restrict__ out, long long n8) {
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8;
-       i += (long long)gridDim.x * blockDim.x) {
-    const uint4 x = a[i], y = b[i];
-    const __nv_bfloat162* xa = reinterpret_cast<const __nv_bfloat162*>(&x);
-    const __nv_bfloat162* ya = reinterpret_cast<const __nv_bfloat162*>(&y);
-    uint4 r;
-    __nv_bfloat162* ra = reinterpret_cast<__nv_bfloat162*>(&r);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float2 fx = __bfloat1622float2(xa[k]), fy = __bfloat1622float2(ya[k]);
-      ra[k] = __floats2bfloat162_rn(fx.x + fy.x, fx.y + fy.y);
-    }
-    out[i] = r;
-  }
-}
 
 __global__ void cast_kernel(const float4* __restrict__ in, uint2* __restrict__ out, long long n4) {
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4;
@@ -444,7 +435,7 @@ cudaError_t launch_layernorm_forward(const __nv_bfloat16* x, __nv_bfloat16* xn, 
 
 cudaError_t launch_layernorm_backward(__nv_bfloat16* dz, const __nv_bfloat16* xn, const __nv_bfloat16* gamma,
                                       const float* stdev, float* dgamma, float* dbeta, int rows, int cols,
-                                      cudaStream_t st) {
+                                      cudaStream_t st, const __nv_bfloat16* res) {
   cudaError_t e = cudaMemsetAsync(dgamma, 0, (size_t)cols * sizeof(float), st);
   if (e == cudaSuccess) e = cudaMemsetAsync(dbeta, 0, (size_t)cols * sizeof(float), st);
   if (e != cudaSuccess) return e;
@@ -458,28 +449,20 @@ cudaError_t launch_layernorm_backward(__nv_bfloat16* dz, const __nv_bfloat16* xn
     uint4* d = reinterpret_cast<uint4*>(dz);
     const uint4* n = reinterpret_cast<const uint4*>(xn);
     const uint4* g = reinterpret_cast<const uint4*>(gamma);
+    const uint4* rv = reinterpret_cast<const uint4*>(res);
     switch (nch) {
-      case 1: layernorm_backward_vec_kernel<1><<<blocks, LN_WARPS * 32, sm, st>>>(d, n, g, stdev, dgamma, dbeta, rows, cols); break;
-      case 2: layernorm_backward_vec_kernel<2><<<blocks, LN_WARPS * 32, sm, st>>>(d, n, g, stdev, dgamma, dbeta, rows, cols); break;
-      case 3: layernorm_backward_vec_kernel<3><<<blocks, LN_WARPS * 32, sm, st>>>(d, n, g, stdev, dgamma, dbeta, rows, cols); break;
-      default: layernorm_backward_vec_kernel<4><<<blocks, LN_WARPS * 32, sm, st>>>(d, n, g, stdev, dgamma, dbeta, rows, cols); break;
+      case 1: layernorm_backward_vec_kernel<1><<<blocks, LN_WARPS * 32, sm, st>>>(d, n, g, stdev, dgamma, dbeta, rows, cols, rv); break;
+      case 2: layernorm_backward_vec_kernel<2><<<blocks, LN_WARPS * 32, sm, st>>>(d, n, g, stdev, dgamma, dbeta, rows, cols, rv); break;
+      case 3: layernorm_backward_vec_kernel<3><<<blocks, LN_WARPS * 32, sm, st>>>(d, n, g, stdev, dgamma, dbeta, rows, cols, rv); break;
+      default: layernorm_backward_vec_kernel<4><<<blocks, LN_WARPS * 32, sm, st>>>(d, n, g, stdev, dgamma, dbeta, rows, cols, rv); break;
     }
   } else {
     int blocks = (rows + LN_WARPS - 1) / LN_WARPS;
     if (blocks > 148 * 4) blocks = 148 * 4;
     layernorm_backward_kernel<<<blocks, LN_WARPS * 32, 2 * cols * sizeof(float), st>>>(dz, xn, gamma, stdev,
-                                                                                         dgamma, dbeta, rows, cols);
+                                                                                         dgamma, dbeta, rows, cols,
+                                                                                         res);
   }
-  count_launches(1);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_residual_add(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_bfloat16* out, long long n,
-                                cudaStream_t st) {
-  const long long n8 = n / 8;  // n is a multiple of 64 here
-  residual_add_kernel<<<ew_blocks(n8), EW_THREADS, 0, st>>>(reinterpret_cast<const uint4*>(a),
-                                                            reinterpret_cast<const uint4*>(b),
-                                                            reinterpret_cast<uint4*>(out), n8);
   count_launches(1);
   return cudaGetLastError();
 }

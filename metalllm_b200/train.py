@@ -128,7 +128,7 @@ class TrainingModel:
         nbytes = self.tensor_bytes(name)
         if name.startswith("grad."):
             dt = np.float32 if _grad_is_f32(name[5:]) else np.uint16
-        elif name in ("loss", "loss_rows", "lse_rows", "master", "dxattn"):
+        elif name in ("loss", "loss_rows", "lse_rows", "master"):
             dt = np.float32
         elif name.endswith(".mask"):
             dt = np.uint8
