@@ -221,7 +221,7 @@ __global__ void layernorm_forward_vec_kernel(const uint4* __restrict__ x, uint4*
 // rows its warp visits, then the block reduces them in shared memory and adds
 // one value per column into the fp32 outputs.
 template <int NCH>
-__global__ void layernorm_backward_vec_kernel(uint4* __restrict__ dz, const uint4* __restrict__ xn,
+__global__ void __launch_bounds__(LN_WARPS * 32, 2) layernorm_backward_vec_kernel(uint4* __restrict__ dz, const uint4* __restrict__ xn,
                                               const uint4* __restrict__ gamma, const float* __restrict__ stdev,
                                               float* __restrict__ dgamma, float* __restrict__ dbeta, int rows,
                                               int cols, const uint4* __restrict__ res) {
@@ -236,16 +236,44 @@ __global__ void layernorm_backward_vec_kernel(uint4* __restrict__ dz, const uint
 #pragma unroll
     for (int i = 0; i < 8; ++i) pg[k][i] = pb[k][i] = 0.0f;
   }
-  for (int row = blockIdx.x * nw + w; row < rows; row += gridDim.x * nw) {
+  // rows of this warp; the next row's loads are issued before the current
+  // row is computed, so each warp keeps two rows in flight
+  const int stride = gridDim.x * nw;
+  uint4 ld[NCH], ln[NCH], lr[NCH];
+  float lsd = 1.0f;
+  auto load_row = [&](int row) {
     const long long rb = (long long)row * c8;
-    float d[NCH][8], n[NCH][8];
-    float s1 = 0.0f, s2 = 0.0f;
 #pragma unroll
     for (int k = 0; k < NCH; ++k) {
       const int c = lane + 32 * k;
       if (c < c8) {
-        unpack8(dz[rb + c], d[k]);
-        unpack8(xn[rb + c], n[k]);
+        ld[k] = dz[rb + c];
+        ln[k] = __ldg(xn + rb + c);
+        if (res) lr[k] = __ldg(res + rb + c);
+      }
+    }
+    lsd = __ldg(stdev + row);
+  };
+  int row = blockIdx.x * nw + w;
+  if (row < rows) load_row(row);
+  for (; row < rows; row += stride) {
+    const long long rb = (long long)row * c8;
+    float d[NCH][8], n[NCH][8];
+    uint4 qr[NCH];  // the residual, unpacked at the store
+#pragma unroll
+    for (int k = 0; k < NCH; ++k) {
+      if (lane + 32 * k < c8) {
+        unpack8(ld[k], d[k]);
+        unpack8(ln[k], n[k]);
+        qr[k] = lr[k];
+      }
+    }
+    const float rs = 1.0f / lsd;
+    if (row + stride < rows) load_row(row + stride);
+    float s1 = 0.0f, s2 = 0.0f;
+#pragma unroll
+    for (int k = 0; k < NCH; ++k) {
+      if (lane + 32 * k < c8) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const float g = d[k][i] * gm[k][i];
@@ -261,7 +289,7 @@ __global__ void layernorm_backward_vec_kernel(uint4* __restrict__ dz, const uint
       s1 += __shfl_xor_sync(0xffffffffu, s1, o);
       s2 += __shfl_xor_sync(0xffffffffu, s2, o);
     }
-    const float m1 = s1 / cols, m2 = s2 / cols, rs = 1.0f / stdev[row];
+    const float m1 = s1 / cols, m2 = s2 / cols;
 #pragma unroll
     for (int k = 0; k < NCH; ++k) {
       const int c = lane + 32 * k;
@@ -271,7 +299,7 @@ __global__ void layernorm_backward_vec_kernel(uint4* __restrict__ dz, const uint
         for (int i = 0; i < 8; ++i) r[i] = rs * (d[k][i] * gm[k][i] - m1 - n[k][i] * m2);
         if (res) {  // the following residual add, on the rounded dX
           float q[8];
-          unpack8(res[rb + c], q);
+          unpack8(qr[k], q);
 #pragma unroll
           for (int i = 0; i < 8; ++i) r[i] = __bfloat162float(__float2bfloat16_rn(r[i])) + q[i];
         }
