@@ -74,17 +74,15 @@ cudaError_t launch_gemm_bf16_act(const __nv_bfloat16* A, const __nv_bfloat16* B,
                                  uint8_t* mask, const __nv_bfloat16* res, int act, int M, int N, int K,
                                  uint32_t* status, cudaStream_t st);
 cudaError_t launch_gemm_splitk_f32(const __nv_bfloat16* A, const __nv_bfloat16* B, float* C, int M, int N,
-                                   int K, uint32_t* status, cudaStream_t st);
-cudaError_t launch_grad_dw_splitk(const __nv_bfloat16* x, const float* dq, const __nv_bfloat16* dk,
-                                  const __nv_bfloat16* dv, float* dqw, __nv_bfloat16* dkw, __nv_bfloat16* dvw,
-                                  float* ws, int rows, int n, uint32_t* status, cudaStream_t st);
+                                   int K, uint32_t* status, cudaStream_t st, bool zero = true);
+// The training step's computeGradDx/Dw on a bf16 copy of dQ; the weight
+// gradients are fp32, split along K and added into zeroed outputs.
+cudaError_t launch_grad_dw_splitk_f32(const __nv_bfloat16* x, const __nv_bfloat16* dq16, const __nv_bfloat16* dk,
+                                      const __nv_bfloat16* dv, float* dqw, float* dkw, float* dvw, int rows, int n,
+                                      uint32_t* status, cudaStream_t st);
 cudaError_t launch_grad_dx_bf16(void* dx, bool dx_f32, const __nv_bfloat16* qw, const __nv_bfloat16* kw,
                                 const __nv_bfloat16* vw, const __nv_bfloat16* dq16, const __nv_bfloat16* dk,
                                 const __nv_bfloat16* dv, int rows, int n, uint32_t* status, cudaStream_t st);
-cudaError_t launch_grad_dw_splitk_bf16(const __nv_bfloat16* x, const __nv_bfloat16* dq16, const __nv_bfloat16* dk,
-                                       const __nv_bfloat16* dv, float* dqw, __nv_bfloat16* dkw,
-                                       __nv_bfloat16* dvw, float* ws, int rows, int n, uint32_t* status,
-                                       cudaStream_t st);
 
 // Training-step kernels (train_sm100.cu).
 cudaError_t launch_embed_forward(const int* tok, const __nv_bfloat16* emb, const __nv_bfloat16* pos,

@@ -562,34 +562,17 @@ int pick_ksplit(int tiles, int K) {
 }
 
 cudaError_t launch_gemm_splitk_f32(const __nv_bfloat16* A, const __nv_bfloat16* B, float* C, int M, int N,
-                                   int K, uint32_t* status, cudaStream_t st) {
-  cudaError_t e = cudaMemsetAsync(C, 0, (size_t)M * N * sizeof(float), st);
-  if (e != cudaSuccess) return e;
+                                   int K, uint32_t* status, cudaStream_t st, bool zero) {
+  if (zero) {
+    cudaError_t e = cudaMemsetAsync(C, 0, (size_t)M * N * sizeof(float), st);
+    if (e != cudaSuccess) return e;
+  }
   const Operand a{A, false}, b{B, false};
   void* c[1] = {C};
   const bool cf[1] = {true};
   const int tiles = ((M + 127) / 128) * ((N + 63) / 64);
   return run_gemm<64, true, true, false>(&a, 1, &b, 1, c, cf, 1, 1, M, N, K, status, st,
                                          pick_ksplit(tiles, K));
-}
-
-// computeGradDw with split-K: dQw (fp32) and the two bf16 gradients, the
-// latter accumulated in an fp32 workspace of 2*n*n floats and then rounded.
-cudaError_t launch_grad_dw_splitk(const __nv_bfloat16* x, const float* dq, const __nv_bfloat16* dk,
-                                  const __nv_bfloat16* dv, float* dqw, __nv_bfloat16* dkw, __nv_bfloat16* dvw,
-                                  float* ws, int rows, int n, uint32_t* status, cudaStream_t st) {
-  cudaError_t e = cudaMemsetAsync(dqw, 0, (size_t)n * n * sizeof(float), st);
-  if (e == cudaSuccess) e = cudaMemsetAsync(ws, 0, (size_t)2 * n * n * sizeof(float), st);
-  if (e != cudaSuccess) return e;
-  const Operand a{x, false};
-  const Operand b[3] = {{dq, true}, {dk, false}, {dv, false}};
-  void* c[3] = {dqw, ws, ws + (size_t)n * n};
-  const bool cf[3] = {true, true, true};
-  const int tiles = 3 * ((n + 127) / 128) * ((n + 63) / 64);
-  e = run_gemm<64, true, true, true>(&a, 1, b, 3, c, cf, 3, 1, n, n, rows, status, st, pick_ksplit(tiles, rows));
-  if (e == cudaSuccess) e = launch_cast_f32_bf16(ws, dkw, (long long)n * n, st);
-  if (e == cudaSuccess) e = launch_cast_f32_bf16(ws + (size_t)n * n, dvw, (long long)n * n, st);
-  return e;
 }
 
 // rows = B*M activations rows, n = N (= NH*D)
@@ -651,7 +634,20 @@ cudaError_t launch_grad_dw(const __nv_bfloat16* x, const float* dq, const __nv_b
 
 // The same two products with dQ already rounded to bf16 (the rounding the
 // fp32-operand path applies in shared memory, so the results are identical):
-// the all-bf16 kernel without the in-kernel conversion.
+// the all-bf16 kernel without the in-kernel conversion.  The weight
+// gradients are split along K and added (TMA reductions) into fp32 outputs
+// the caller has zeroed.
+cudaError_t launch_grad_dw_splitk_f32(const __nv_bfloat16* x, const __nv_bfloat16* dq16, const __nv_bfloat16* dk,
+                                      const __nv_bfloat16* dv, float* dqw, float* dkw, float* dvw, int rows, int n,
+                                      uint32_t* status, cudaStream_t st) {
+  const Operand a{x, false};
+  const Operand b[3] = {{dq16, false}, {dk, false}, {dv, false}};
+  void* c[3] = {dqw, dkw, dvw};
+  const bool cf[3] = {true, true, true};
+  const int tiles = 3 * ((n + 127) / 128) * ((n + 63) / 64);
+  return run_gemm<64, true, true, false>(&a, 1, b, 3, c, cf, 3, 1, n, n, rows, status, st, pick_ksplit(tiles, rows));
+}
+
 cudaError_t launch_grad_dx_bf16(void* dx, bool dx_f32, const __nv_bfloat16* qw, const __nv_bfloat16* kw,
                                 const __nv_bfloat16* vw, const __nv_bfloat16* dq16, const __nv_bfloat16* dk,
                                 const __nv_bfloat16* dv, int rows, int n, uint32_t* status, cudaStream_t st) {
@@ -660,24 +656,6 @@ cudaError_t launch_grad_dx_bf16(void* dx, bool dx_f32, const __nv_bfloat16* qw, 
   void* c[1] = {dx};
   const bool cf[1] = {dx_f32};
   return run_gemm<128, false, false, false>(a, 3, b, 3, c, cf, 1, 3, rows, n, n, status, st);
-}
-
-cudaError_t launch_grad_dw_splitk_bf16(const __nv_bfloat16* x, const __nv_bfloat16* dq16, const __nv_bfloat16* dk,
-                                       const __nv_bfloat16* dv, float* dqw, __nv_bfloat16* dkw,
-                                       __nv_bfloat16* dvw, float* ws, int rows, int n, uint32_t* status,
-                                       cudaStream_t st) {
-  cudaError_t e = cudaMemsetAsync(dqw, 0, (size_t)n * n * sizeof(float), st);
-  if (e == cudaSuccess) e = cudaMemsetAsync(ws, 0, (size_t)2 * n * n * sizeof(float), st);
-  if (e != cudaSuccess) return e;
-  const Operand a{x, false};
-  const Operand b[3] = {{dq16, false}, {dk, false}, {dv, false}};
-  void* c[3] = {dqw, ws, ws + (size_t)n * n};
-  const bool cf[3] = {true, true, true};
-  const int tiles = 3 * ((n + 127) / 128) * ((n + 63) / 64);
-  e = run_gemm<64, true, true, false>(&a, 1, b, 3, c, cf, 3, 1, n, n, rows, status, st, pick_ksplit(tiles, rows));
-  if (e == cudaSuccess) e = launch_cast_f32_bf16(ws, dkw, (long long)n * n, st);
-  if (e == cudaSuccess) e = launch_cast_f32_bf16(ws + (size_t)n * n, dvw, (long long)n * n, st);
-  return e;
 }
 
 }  // namespace ma

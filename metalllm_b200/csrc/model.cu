@@ -42,8 +42,8 @@ struct Layer {
   bf16 *q, *k, *v, *attn, *res1, *mlp_v, *res2;
   float* l;
   uint8_t* mask;
-  float* dqw;
-  bf16 *dkw, *dvw, *dprojw, *dup, *ddp;
+  // fp32 weight gradients (parts of the model's zeroed-per-step block)
+  float *dqw, *dkw, *dvw, *dprojw, *dup, *ddp;
 };
 
 }  // namespace
@@ -59,10 +59,13 @@ struct ma_model {
   __nv_bfloat16 *embed = nullptr, *pos = nullptr, *linw = nullptr;
   __nv_bfloat16 *embed_out = nullptr, *logits = nullptr, *dlogits = nullptr;
   __nv_bfloat16 *dstream = nullptr, *dbranch = nullptr, *dzattn = nullptr, *dattnd = nullptr;
-  __nv_bfloat16 *dk = nullptr, *dv = nullptr, *dmlpv = nullptr, *dpos = nullptr, *dlinw = nullptr;
+  __nv_bfloat16 *dk = nullptr, *dv = nullptr, *dmlpv = nullptr, *dpos = nullptr;
+  float* dlinw = nullptr;
+  // every split-K weight gradient, contiguous, zeroed by one memset per backward
+  float* wgrads = nullptr;
+  size_t wgrads_count = 0;
   __nv_bfloat16* dq16 = nullptr;  // dQ rounded to bf16 for computeGradDx/Dw
   float *dq = nullptr, *demb = nullptr;
-  float* ws = nullptr;  // fp32 workspace of the split-K weight-gradient GEMMs
   float *loss_rows = nullptr, *lse_rows = nullptr, *loss_mean = nullptr;
   const int* tokens = nullptr;   // last forward's inputs (device)
   const int* targets = nullptr;
@@ -186,6 +189,15 @@ int ma_model_create(const MaModelConfig* c, ma_model** out) {
   if ((e = param("embed", &m->embed, V, E, 0.02f, false, m->demb, true)) != cudaSuccess) return fail(e, "param");
   if ((e = param("pos", &m->pos, T, E, 0.02f, false, m->dpos, false)) != cudaSuccess) return fail(e, "param");
   m->layers.resize(m->L);
+  // the weight gradients that split-K GEMMs add into, in one block
+  m->wgrads_count = (size_t)m->L * (4 * (size_t)E * E + 2 * (size_t)E * H) + (size_t)E * V;
+  ALLOC(m->wgrads, m->wgrads_count);
+  float* wg_next = m->wgrads;
+  auto wg_take = [&](size_t n) {
+    float* p = wg_next;
+    wg_next += n;
+    return p;
+  };
   const float small = 0.02f / std::sqrt(2.0f * m->L);
   auto ln_bufs = [&](LayerNormBufs& ln) -> cudaError_t {
     cudaError_t e2;
@@ -198,23 +210,23 @@ int ma_model_create(const MaModelConfig* c, ma_model** out) {
     Layer& y = m->layers[n];
     const std::string pre = "layer" + std::to_string(n) + ".";
     if ((e = ln_bufs(y.ln1)) || (e = ln_bufs(y.ln2))) return fail(e, "cudaMalloc");
-    ALLOC(y.dqw, E * E);
-    ALLOC(y.dkw, E * E);
-    ALLOC(y.dvw, E * E);
-    ALLOC(y.dprojw, E * E);
-    ALLOC(y.dup, E * H);
-    ALLOC(y.ddp, H * E);
+    y.dqw = wg_take(E * E);
+    y.dkw = wg_take(E * E);
+    y.dvw = wg_take(E * E);
+    y.dprojw = wg_take(E * E);
+    y.dup = wg_take(E * H);
+    y.ddp = wg_take(H * E);
     const float xav = std::sqrt(2.0f / (float)(E + E)), kai = std::sqrt(2.0f / (float)E);
     if ((e = param((pre + "ln1_gamma").c_str(), &y.ln1.gamma, 1, E, 0.0f, true, y.ln1.dgamma, true)) ||
         (e = param((pre + "ln1_beta").c_str(), &y.ln1.beta, 1, E, 0.0f, false, y.ln1.dbeta, true)) ||
         (e = param((pre + "qw").c_str(), &y.qw, E, E, xav, false, y.dqw, true)) ||
-        (e = param((pre + "kw").c_str(), &y.kw, E, E, xav, false, y.dkw, false)) ||
-        (e = param((pre + "vw").c_str(), &y.vw, E, E, xav, false, y.dvw, false)) ||
-        (e = param((pre + "projw").c_str(), &y.projw, E, E, small, false, y.dprojw, false)) ||
+        (e = param((pre + "kw").c_str(), &y.kw, E, E, xav, false, y.dkw, true)) ||
+        (e = param((pre + "vw").c_str(), &y.vw, E, E, xav, false, y.dvw, true)) ||
+        (e = param((pre + "projw").c_str(), &y.projw, E, E, small, false, y.dprojw, true)) ||
         (e = param((pre + "ln2_gamma").c_str(), &y.ln2.gamma, 1, E, 0.0f, true, y.ln2.dgamma, true)) ||
         (e = param((pre + "ln2_beta").c_str(), &y.ln2.beta, 1, E, 0.0f, false, y.ln2.dbeta, true)) ||
-        (e = param((pre + "up").c_str(), &y.up, E, H, kai, false, y.dup, false)) ||
-        (e = param((pre + "dp").c_str(), &y.dp, H, E, small, false, y.ddp, false)))
+        (e = param((pre + "up").c_str(), &y.up, E, H, kai, false, y.dup, true)) ||
+        (e = param((pre + "dp").c_str(), &y.dp, H, E, small, false, y.ddp, true)))
       return fail(e, "param");
     ALLOC(y.q, R * E);
     ALLOC(y.k, R * E);
@@ -227,10 +239,10 @@ int ma_model_create(const MaModelConfig* c, ma_model** out) {
     ALLOC(y.res2, R * E);
   }
   if ((e = ln_bufs(m->lnf))) return fail(e, "cudaMalloc");
-  ALLOC(m->dlinw, E * V);
+  m->dlinw = wg_take(E * V);
   if ((e = param("lnf_gamma", &m->lnf.gamma, 1, E, 0.0f, true, m->lnf.dgamma, true)) ||
       (e = param("lnf_beta", &m->lnf.beta, 1, E, 0.0f, false, m->lnf.dbeta, true)) ||
-      (e = param("linw", &m->linw, E, V, 0.02f, false, m->dlinw, false)))
+      (e = param("linw", &m->linw, E, V, 0.02f, false, m->dlinw, true)))
     return fail(e, "param");
   ALLOC(m->embed_out, R * E);
   ALLOC(m->logits, R * V);
@@ -244,7 +256,6 @@ int ma_model_create(const MaModelConfig* c, ma_model** out) {
   ALLOC(m->dk, R * E);
   ALLOC(m->dv, R * E);
   ALLOC(m->dmlpv, R * H);
-  ALLOC(m->ws, std::max(std::max(E * H, 2 * E * E), E * V));
   ALLOC(m->loss_rows, R);
   ALLOC(m->lse_rows, R);
   ALLOC(m->loss_mean, 1);
@@ -329,13 +340,13 @@ int ma_model_forward(ma_model* m, const int32_t* tokens, const int32_t* targets,
   return MA_OK;
 }
 
-// Weight gradient G[M][N] = X^T . Y over all B*T rows (X [rows][M], Y
-// [rows][N], bf16): split-K into the fp32 workspace, then rounded to bf16.
-static cudaError_t wgrad(ma_model* m, const __nv_bfloat16* X, const __nv_bfloat16* Y, __nv_bfloat16* G, int M,
-                         int N, cudaStream_t st) {
-  cudaError_t e = ma::launch_gemm_splitk_f32(X, Y, m->ws, M, N, m->R, m->status, st);
-  if (e == cudaSuccess) e = ma::launch_cast_f32_bf16(m->ws, G, (long long)M * N, st);
-  return e;
+// Weight gradient G[M][N] (fp32, zeroed at the start of the backward) =
+// X^T . Y over all B*T rows (X [rows][M], Y [rows][N], bf16), split along K
+// with the partial sums added by TMA reductions; Adam rounds it to bf16, as
+// the reference's bf16 gradient buffers hold it.
+static cudaError_t wgrad(ma_model* m, const __nv_bfloat16* X, const __nv_bfloat16* Y, float* G, int M, int N,
+                         cudaStream_t st) {
+  return ma::launch_gemm_splitk_f32(X, Y, G, M, N, m->R, m->status, st, /*zero=*/false);
 }
 
 int ma_model_backward(ma_model* m, ma_stream_t stream) {
@@ -344,6 +355,7 @@ int ma_model_backward(ma_model* m, ma_stream_t stream) {
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int R = m->R, E = m->E, H = m->H, V = m->V;
   AttnShape s{m->T, E, m->D, m->NH, m->Bt, 0, m->Bt * m->NH};
+  MA_M_CUDA(cudaMemsetAsync(m->wgrads, 0, m->wgrads_count * sizeof(float), st), "zero weight gradients");
   MA_M_CUDA(launch_loss_backward(m->logits, m->targets, m->lse_rows, m->dlogits, R, V, st), "lossBackward");
   // linearBackward: dStream = dLogits . W^T ; dW = lnf.out^T . dLogits
   MA_M_CUDA(launch_gemm_bf16(m->dlogits, false, m->linw, false, m->dstream, R, E, V, m->status, st),
@@ -377,8 +389,8 @@ int ma_model_backward(ma_model* m, ma_stream_t stream) {
     // dX straight to bf16 (the fp32 dX rounded by castFloatToBfloat gives the same values)
     MA_M_CUDA(launch_grad_dx_bf16(m->dstream, false, y.qw, y.kw, y.vw, m->dq16, m->dk, m->dv, R, E, m->status, st),
               "computeGradDx + castFloatToBfloat");
-    MA_M_CUDA(launch_grad_dw_splitk_bf16(y.ln1.out, m->dq16, m->dk, m->dv, y.dqw, y.dkw, y.dvw, m->ws, R, E,
-                                         m->status, st), "computeGradDw");
+    MA_M_CUDA(launch_grad_dw_splitk_f32(y.ln1.out, m->dq16, m->dk, m->dv, y.dqw, y.dkw, y.dvw, R, E, m->status,
+                                        st), "computeGradDw");
     MA_M_CUDA(launch_layernorm_backward(m->dstream, y.ln1.xn, y.ln1.gamma, y.ln1.stdev, y.ln1.dgamma,
                                         y.ln1.dbeta, R, E, st, m->dbranch), "layernormBackward + residualAdd");
   }
