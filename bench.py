@@ -37,6 +37,9 @@ METRIC = "causal bf16 FlashAttn fwd+bwd TFLOP/s per GPU, % tensor peak, at 1/2/4
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
+DATASHEET_BF16_TFLOPS = 2250.0  # B200 dense bf16 (NVIDIA's 4.5 PFLOP/s figure is with 2:4 sparsity)
+
+
 def load_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -367,6 +370,9 @@ def run_gpu(args):
         },
         "per_gpu_tflops": round(value / world, 3),
         "frac_of_peak": round(value / world / peak, 4),
+        # the datasheet's dense bf16 figure (2.25 PFLOP/s per B200), for comparison
+        # with the north_star target, next to the measured-peak fraction above
+        "frac_of_datasheet_peak": round(value / world / DATASHEET_BF16_TFLOPS, 4),
         "clocks": clocks,
         "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
