@@ -570,6 +570,11 @@ cudaError_t launch_gemm_splitk_f32(const __nv_bfloat16* A, const __nv_bfloat16* 
   const Operand a{A, false}, b{B, false};
   void* c[1] = {C};
   const bool cf[1] = {true};
+  if (N % 128 == 0) {  // 128-wide tiles: fewer operand re-reads, N = 128 UMMAs
+    const int tiles = ((M + 127) / 128) * (N / 128);
+    return run_gemm<128, true, true, false>(&a, 1, &b, 1, c, cf, 1, 1, M, N, K, status, st,
+                                            pick_ksplit(tiles, K));
+  }
   const int tiles = ((M + 127) / 128) * ((N + 63) / 64);
   return run_gemm<64, true, true, false>(&a, 1, &b, 1, c, cf, 1, 1, M, N, K, status, st,
                                          pick_ksplit(tiles, K));
@@ -644,6 +649,11 @@ cudaError_t launch_grad_dw_splitk_f32(const __nv_bfloat16* x, const __nv_bfloat1
   const Operand b[3] = {{dq16, false}, {dk, false}, {dv, false}};
   void* c[3] = {dqw, dkw, dvw};
   const bool cf[3] = {true, true, true};
+  if (n % 128 == 0) {
+    const int tiles = 3 * ((n + 127) / 128) * (n / 128);
+    return run_gemm<128, true, true, false>(&a, 1, b, 3, c, cf, 3, 1, n, n, rows, status, st,
+                                            pick_ksplit(tiles, rows));
+  }
   const int tiles = 3 * ((n + 127) / 128) * ((n + 63) / 64);
   return run_gemm<64, true, true, false>(&a, 1, b, 3, c, cf, 3, 1, n, n, rows, status, st, pick_ksplit(tiles, rows));
 }
