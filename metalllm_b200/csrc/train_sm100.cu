@@ -225,8 +225,7 @@ __global__ void __launch_bounds__(LN_WARPS * 32, 2) layernorm_backward_vec_kerne
                                               const uint4* __restrict__ gamma, const float* __restrict__ stdev,
                                               float* __restrict__ dgamma, float* __restrict__ dbeta, int rows,
                                               int cols, const uint4* __restrict__ res) {
-  extern __shared__ float red[];  // [2][cols]
-  for (int c = threadIdx.x; c < 2 * cols; c += blockDim.x) red[c] = 0.0f;
+  extern __shared__ float red[];  // [warps][2][cols]: each warp's column partial sums
   const int lane = threadIdx.x % 32, w = threadIdx.x / 32, nw = blockDim.x / 32;
   const int c8 = cols / 8;
   float gm[NCH][8], pg[NCH][8], pb[NCH][8];
@@ -307,21 +306,27 @@ __global__ void __launch_bounds__(LN_WARPS * 32, 2) layernorm_backward_vec_kerne
       }
     }
   }
-  __syncthreads();
+  // this warp's partials to its own rows of the block buffer (16-byte
+  // stores, no atomics), then one thread per column sums the warps and adds
+  // the block's total into the output
+  float* wr = red + (size_t)w * 2 * cols;
 #pragma unroll
   for (int k = 0; k < NCH; ++k) {
     const int c = lane + 32 * k;
-    if (c < c8)
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        atomicAdd(&red[c * 8 + i], pg[k][i]);
-        atomicAdd(&red[cols + c * 8 + i], pb[k][i]);
-      }
+    if (c < c8) {
+      float4* g4 = reinterpret_cast<float4*>(wr + c * 8);
+      float4* b4 = reinterpret_cast<float4*>(wr + cols + c * 8);
+      g4[0] = make_float4(pg[k][0], pg[k][1], pg[k][2], pg[k][3]);
+      g4[1] = make_float4(pg[k][4], pg[k][5], pg[k][6], pg[k][7]);
+      b4[0] = make_float4(pb[k][0], pb[k][1], pb[k][2], pb[k][3]);
+      b4[1] = make_float4(pb[k][4], pb[k][5], pb[k][6], pb[k][7]);
+    }
   }
   __syncthreads();
-  for (int c = threadIdx.x; c < cols; c += blockDim.x) {
-    atomicAdd(dgamma + c, red[c]);
-    atomicAdd(dbeta + c, red[cols + c]);
+  for (int c = threadIdx.x; c < 2 * cols; c += blockDim.x) {
+    float t = 0.0f;
+    for (int q = 0; q < nw; ++q) t += red[(size_t)q * 2 * cols + c];
+    atomicAdd(c < cols ? dgamma + c : dbeta + (c - cols), t);
   }
 }
 
@@ -473,16 +478,20 @@ cudaError_t launch_layernorm_backward(__nv_bfloat16* dz, const __nv_bfloat16* xn
     // flight, few column atomics at the end
     int blocks = (rows + LN_WARPS - 1) / LN_WARPS;
     if (blocks > 2 * 148) blocks = 2 * 148;
-    const size_t sm = 2 * cols * sizeof(float);
+    const size_t sm = (size_t)LN_WARPS * 2 * cols * sizeof(float);
     uint4* d = reinterpret_cast<uint4*>(dz);
     const uint4* n = reinterpret_cast<const uint4*>(xn);
     const uint4* g = reinterpret_cast<const uint4*>(gamma);
     const uint4* rv = reinterpret_cast<const uint4*>(res);
+    auto run = [&](auto kern) {
+      if (sm > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+      kern<<<blocks, LN_WARPS * 32, sm, st>>>(d, n, g, stdev, dgamma, dbeta, rows, cols, rv);
+    };
     switch (nch) {
-      case 1: layernorm_backward_vec_kernel<1><<<blocks, LN_WARPS * 32, sm, st>>>(d, n, g, stdev, dgamma, dbeta, rows, cols, rv); break;
-      case 2: layernorm_backward_vec_kernel<2><<<blocks, LN_WARPS * 32, sm, st>>>(d, n, g, stdev, dgamma, dbeta, rows, cols, rv); break;
-      case 3: layernorm_backward_vec_kernel<3><<<blocks, LN_WARPS * 32, sm, st>>>(d, n, g, stdev, dgamma, dbeta, rows, cols, rv); break;
-      default: layernorm_backward_vec_kernel<4><<<blocks, LN_WARPS * 32, sm, st>>>(d, n, g, stdev, dgamma, dbeta, rows, cols, rv); break;
+      case 1: run(layernorm_backward_vec_kernel<1>); break;
+      case 2: run(layernorm_backward_vec_kernel<2>); break;
+      case 3: run(layernorm_backward_vec_kernel<3>); break;
+      default: run(layernorm_backward_vec_kernel<4>); break;
     }
   } else {
     int blocks = (rows + LN_WARPS - 1) / LN_WARPS;
