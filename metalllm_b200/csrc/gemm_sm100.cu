@@ -305,6 +305,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int grow = row0 + row;
     float dsum = 0.0f;  // FUSE_D: this row's partial dot for the current head
     if (ok) {
+      // the row's residual / mask / O slice, loaded in one burst before the
+      // accumulator is read (one memory round trip instead of one per chunk)
+      constexpr int NPF = (ACT == 3 || FUSE_D) ? BN / 8 : (ACT == 2 ? BN / 16 : 1);
+      uint4 pf[NPF];
+      if constexpr (ACT == 3 || ACT == 2 || FUSE_D) {
+        if (grow < args.M) {
+          const uint4* src = ACT == 3   ? reinterpret_cast<const uint4*>(args.res + (size_t)grow * args.N + col0)
+                             : FUSE_D ? reinterpret_cast<const uint4*>(args.o_in + (size_t)grow * args.N + col0)
+                                      : reinterpret_cast<const uint4*>(args.mask + (size_t)grow * args.N + col0);
+#pragma unroll
+          for (int i = 0; i < NPF; ++i) pf[i] = __ldg(src + i);
+        }
+      }
       tc_fence_after();
       uint8_t* stage = gbase;  // the ring is idle now
 #pragma unroll
@@ -333,16 +346,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           v1.w = pack_bf16(__uint_as_float(r[14]), __uint_as_float(r[15]));
           if constexpr (ACT == 3) {  // residual add on the rounded values
             if (grow < args.M) {
-              const uint4* rp = reinterpret_cast<const uint4*>(args.res + (size_t)grow * args.N + col0 + cc);
-              const uint4 ra = __ldg(rp), rb = __ldg(rp + 1);
-              v0 = add_bf16x8(v0, ra);
-              v1 = add_bf16x8(v1, rb);
+              v0 = add_bf16x8(v0, pf[cc / 8]);
+              v1 = add_bf16x8(v1, pf[cc / 8 + 1]);
             }
           }
           if constexpr (ACT == 1 || ACT == 2) {  // on the rounded values, as the separate kernels do
             if (grow < args.M) {
               uint8_t* mp = args.mask + (size_t)grow * args.N + col0 + cc;
-              uint4 mk = ACT == 2 ? *reinterpret_cast<const uint4*>(mp) : make_uint4(0, 0, 0, 0);
+              uint4 mk = ACT == 2 ? pf[ACT == 2 ? cc / 16 : 0] : make_uint4(0, 0, 0, 0);
               uint32_t* w = reinterpret_cast<uint32_t*>(&v0);  // v0, v1: 8 words, 16 values
               uint32_t* wb = reinterpret_cast<uint32_t*>(&v1);
               uint8_t* mb = reinterpret_cast<uint8_t*>(&mk);
@@ -365,8 +376,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           *reinterpret_cast<uint4*>(rowp + (((ch + 1) ^ (row & 7)) * 16)) = v1;
           if constexpr (FUSE_D) {  // D from the rounded bf16 values, as computeD reads them
             if (grow < args.M) {
-              const uint4* op = reinterpret_cast<const uint4*>(args.o_in + (size_t)grow * args.N + col0 + cc);
-              dsum += dot_bf16x8(v0, __ldg(op)) + dot_bf16x8(v1, __ldg(op + 1));
+              dsum += dot_bf16x8(v0, pf[cc / 8]) + dot_bf16x8(v1, pf[cc / 8 + 1]);
               if ((col0 + cc + 16) % args.head_dim == 0) {
                 const int nh = args.N / args.head_dim;
                 args.d_out[(size_t)grow * nh + (col0 + cc) / args.head_dim] = __float2bfloat16_rn(dsum);
