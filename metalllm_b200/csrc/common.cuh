@@ -5,9 +5,41 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/metalattn.h"
 
 namespace ma {
+
+// Programmatic dependent launch: wait until the previous kernel in the stream
+// has completed and its writes are visible (a no-op when the kernel was not
+// launched as a dependent), then let the next kernel be scheduled.
+__device__ __forceinline__ void pdl_wait_and_release() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Kernel launch with programmatic dependent launch allowed: the kernel may be
+// scheduled while the previous kernel in the stream is still draining; every
+// kernel of this library starts with pdl_wait_and_release(), which waits for
+// that kernel's completion before any memory is touched, so stream order is
+// kept.  Errors are reported through cudaGetLastError as for <<<>>>.
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 
 // Per-kernel bits of the device status word (ma_device_status).
 enum : uint32_t {

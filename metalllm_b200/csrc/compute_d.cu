@@ -37,6 +37,7 @@ __global__ void __launch_bounds__(256) compute_d_kernel(const uint4* __restrict_
                                                         long long item_begin,
                                                         long long item_end, int T, int NH,
                                                         int bh_begin, int bh_end) {
+  pdl_wait_and_release();
   const int lane_in_item = threadIdx.x % G;
   const long long items_per_block = blockDim.x / G;
   const bool full_range = (bh_begin == 0 && bh_end < 0);
@@ -87,7 +88,7 @@ cudaError_t launch_compute_d(const __nv_bfloat16* dO, const __nv_bfloat16* O,
     const long long per_block = threads / 8;
     long long blocks = (items + per_block - 1) / per_block;
     blocks = blocks < (long long)sms * 16 ? blocks : (long long)sms * 16;
-    compute_d_kernel<8><<<(unsigned)blocks, threads, 0, st>>>(
+    launch_pdl(compute_d_kernel<8>, (unsigned)blocks, threads, 0, st, 
         reinterpret_cast<const uint4*>(dO), reinterpret_cast<const uint4*>(O), Dv, item_begin,
         item_end, s.T, s.NH, bh_begin_arg, bh_end_arg);
     count_launches(1);
@@ -95,7 +96,7 @@ cudaError_t launch_compute_d(const __nv_bfloat16* dO, const __nv_bfloat16* O,
     const long long per_block = threads / 16;
     long long blocks = (items + per_block - 1) / per_block;
     blocks = blocks < (long long)sms * 16 ? blocks : (long long)sms * 16;
-    compute_d_kernel<16><<<(unsigned)blocks, threads, 0, st>>>(
+    launch_pdl(compute_d_kernel<16>, (unsigned)blocks, threads, 0, st, 
         reinterpret_cast<const uint4*>(dO), reinterpret_cast<const uint4*>(O), Dv, item_begin,
         item_end, s.T, s.NH, bh_begin_arg, bh_end_arg);
     count_launches(1);

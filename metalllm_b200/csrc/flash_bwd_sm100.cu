@@ -263,6 +263,7 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
                      const __grid_constant__ CUtensorMap tmdQ, __nv_bfloat16* __restrict__ dK,
                      __nv_bfloat16* __restrict__ dV, const BwdParams prm) {
+  pdl_wait_and_release();
   using C = BwdCfg<HD, PERSIST>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ int abort_flag;
@@ -737,6 +738,7 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
 // Zeroes the dQ columns of the (batch, head) shard range.
 __global__ void zero_dq_shard_kernel(float4* __restrict__ dQ, int T, int N, int D, int NH,
                                      int bh_begin, int bh_end) {
+  pdl_wait_and_release();
   const long long per_bh = (long long)T * (D / 4);
   const long long total = (long long)(bh_end - bh_begin) * per_bh;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
@@ -776,7 +778,7 @@ cudaError_t launch_bwd_kernel(const __nv_bfloat16* dO, const __nv_bfloat16* q,
   cudaError_t e = cudaFuncSetAttribute(flash_bwd_kernel<HD, PERSIST>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
   if (e != cudaSuccess) return e;
-  flash_bwd_kernel<HD, PERSIST><<<grid, C::NUM_THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, tdo, tdq, dK,
+  launch_pdl(flash_bwd_kernel<HD, PERSIST>, grid, C::NUM_THREADS, C::SMEM_BYTES, st, tq, tk, tv, tdo, tdq, dK,
                                                                         dV, prm);
   count_launches(1);
   return cudaGetLastError();
@@ -793,7 +795,7 @@ cudaError_t launch_bwd(const __nv_bfloat16* dO, const __nv_bfloat16* Dv, const f
   if (s.bh_begin == 0 && s.bh_end == s.B * s.NH) {
     e = cudaMemsetAsync(dQ, 0, (size_t)s.B * s.T * s.N * sizeof(float), st);
   } else {
-    zero_dq_shard_kernel<<<1184, 256, 0, st>>>(reinterpret_cast<float4*>(dQ), s.T, s.N, s.D, s.NH,
+    launch_pdl(zero_dq_shard_kernel, 1184, 256, 0, st, reinterpret_cast<float4*>(dQ), s.T, s.N, s.D, s.NH,
                                               s.bh_begin, s.bh_end);
     count_launches(1);
     e = cudaGetLastError();

@@ -129,6 +129,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
                      const FwdParams prm) {
+  pdl_wait_and_release();
   using C = FwdCfg<HD>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ int abort_flag;
@@ -560,7 +561,7 @@ cudaError_t launch_fwd(const __nv_bfloat16* q, const __nv_bfloat16* k, const __n
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int grid = prm.nunits < sms ? prm.nunits : sms;
-  flash_fwd_kernel<HD><<<grid, NUM_THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, to, prm);
+  launch_pdl(flash_fwd_kernel<HD>, grid, NUM_THREADS, C::SMEM_BYTES, st, tq, tk, tv, to, prm);
   count_launches(1);
   return cudaGetLastError();
 }

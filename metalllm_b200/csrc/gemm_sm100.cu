@@ -123,6 +123,7 @@ __device__ __forceinline__ float dot_bf16x8(uint4 a, uint4 b) {
 template <int BN, bool A_MN, bool B_MN, bool HAS_F32, bool FUSE_D = false, int ACT = 0>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_kernel(const __grid_constant__ GemmMaps maps, const GemmArgs args) {
+  pdl_wait_and_release();
   using C = GemmCfg<BN, HAS_F32>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ int abort_flag;
@@ -497,7 +498,7 @@ cudaError_t run_gemm(const Operand* A, int na, const Operand* Bop, int nb, void*
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
   if (e != cudaSuccess) return e;
   const dim3 grid((M + BM - 1) / BM, (N + BN - 1) / BN, nz * args.ksplit);
-  kern<<<grid, NUM_THREADS, Cfg::SMEM_BYTES, st>>>(maps, args);
+  launch_pdl(kern, grid, NUM_THREADS, Cfg::SMEM_BYTES, st, maps, args);
   count_launches(1);
   return cudaGetLastError();
 }

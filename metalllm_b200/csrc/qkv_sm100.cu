@@ -48,6 +48,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                const __grid_constant__ CUtensorMap tmWk, const __grid_constant__ CUtensorMap tmWv,
                const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                const __grid_constant__ CUtensorMap tmV, int N, uint32_t* status) {
+  pdl_wait_and_release();
   using C = QkvCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ int abort_flag;
@@ -194,7 +195,7 @@ cudaError_t launch(const __nv_bfloat16* X, __nv_bfloat16* q, __nv_bfloat16* k, _
                                        C::SMEM_BYTES);
   if (e != cudaSuccess) return e;
   const dim3 grid((rows + BM - 1) / BM, N / BN);
-  qkv_kernel<BN><<<grid, NUM_THREADS, C::SMEM_BYTES, st>>>(tx, twq, twk, twv, tq, tk, tv, N, status);
+  launch_pdl(qkv_kernel<BN>, grid, NUM_THREADS, C::SMEM_BYTES, st, tx, twq, twk, twv, tq, tk, tv, N, status);
   count_launches(1);
   return cudaGetLastError();
 }

@@ -34,6 +34,7 @@ __device__ __forceinline__ __nv_bfloat16 tobf(float x) { return __float2bfloat16
 __global__ void embed_forward_kernel(const int* __restrict__ tok, const __nv_bfloat16* __restrict__ emb,
                                      const __nv_bfloat16* __restrict__ pos, __nv_bfloat16* __restrict__ out,
                                      int rows, int T, int E) {
+  pdl_wait_and_release();
   const int r = blockIdx.x;
   if (r >= rows) return;
   const __nv_bfloat16* e = emb + (long long)tok[r] * E;
@@ -45,6 +46,7 @@ __global__ void embed_forward_kernel(const int* __restrict__ tok, const __nv_bfl
 // dEmb[tok[r]] += dZ[r] (fp32 atomics; dEmb zeroed first)
 __global__ void embed_backward_kernel(const int* __restrict__ tok, const __nv_bfloat16* __restrict__ dz,
                                       float* __restrict__ demb, int rows, int E) {
+  pdl_wait_and_release();
   const int r = blockIdx.x;
   if (r >= rows) return;
   float* d = demb + (long long)tok[r] * E;
@@ -55,6 +57,7 @@ __global__ void embed_backward_kernel(const int* __restrict__ tok, const __nv_bf
 // dPos[t][c] = bf16(sum_b dZ[b*T + t][c])
 __global__ void pos_grad_kernel(const __nv_bfloat16* __restrict__ dz, __nv_bfloat16* __restrict__ dpos,
                                 int B, int T, int E) {
+  pdl_wait_and_release();
   const long long n = (long long)T * E;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
        i += (long long)gridDim.x * blockDim.x) {
@@ -72,6 +75,7 @@ __global__ void layernorm_forward_kernel(const __nv_bfloat16* __restrict__ x, __
                                          __nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ gamma,
                                          const __nv_bfloat16* __restrict__ beta, float* __restrict__ stdev,
                                          int rows, int cols, float eps) {
+  pdl_wait_and_release();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
   if (warp >= rows) return;
   const __nv_bfloat16* xr = x + (long long)warp * cols;
@@ -106,6 +110,7 @@ __global__ void layernorm_backward_kernel(__nv_bfloat16* __restrict__ dz, const 
                                           const __nv_bfloat16* __restrict__ gamma, const float* __restrict__ stdev,
                                           float* __restrict__ dgamma, float* __restrict__ dbeta, int rows,
                                           int cols, const __nv_bfloat16* __restrict__ res) {
+  pdl_wait_and_release();
   extern __shared__ float red[];  // [2][cols]
   for (int c = threadIdx.x; c < 2 * cols; c += blockDim.x) red[c] = 0.0f;
   __syncthreads();
@@ -166,6 +171,7 @@ __global__ void layernorm_forward_vec_kernel(const uint4* __restrict__ x, uint4*
                                              uint4* __restrict__ out, const uint4* __restrict__ gamma,
                                              const uint4* __restrict__ beta, float* __restrict__ stdev, int rows,
                                              int cols, float eps) {
+  pdl_wait_and_release();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
   if (warp >= rows) return;
   const int c8 = cols / 8;
@@ -225,6 +231,7 @@ __global__ void __launch_bounds__(LN_WARPS * 32, 2) layernorm_backward_vec_kerne
                                               const uint4* __restrict__ gamma, const float* __restrict__ stdev,
                                               float* __restrict__ dgamma, float* __restrict__ dbeta, int rows,
                                               int cols, const uint4* __restrict__ res) {
+  pdl_wait_and_release();
   extern __shared__ float red[];  // [warps][2][cols]: each warp's column partial sums
   const int lane = threadIdx.x % 32, w = threadIdx.x / 32, nw = blockDim.x / 32;
   const int c8 = cols / 8;
@@ -333,6 +340,7 @@ __global__ void __launch_bounds__(LN_WARPS * 32, 2) layernorm_backward_vec_kerne
 // ---------------------------------------------------------------- glue
 
 __global__ void cast_kernel(const float4* __restrict__ in, uint2* __restrict__ out, long long n4) {
+  pdl_wait_and_release();
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4;
        i += (long long)gridDim.x * blockDim.x) {
     const float4 v = in[i];
@@ -346,6 +354,7 @@ __global__ void cast_kernel(const float4* __restrict__ in, uint2* __restrict__ o
 // (loss.metal:9-59).
 __global__ void loss_forward_kernel(const __nv_bfloat16* __restrict__ x, const int* __restrict__ y,
                                     float* __restrict__ out, float* __restrict__ lse, int rows, int cols) {
+  pdl_wait_and_release();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
   if (warp >= rows) return;
   const __nv_bfloat16* xr = x + (long long)warp * cols;
@@ -366,6 +375,7 @@ __global__ void loss_forward_kernel(const __nv_bfloat16* __restrict__ x, const i
 
 // mean of the per-row losses into *mean (one block, fixed order)
 __global__ void mean_kernel(const float* __restrict__ v, int n, float* __restrict__ mean) {
+  pdl_wait_and_release();
   __shared__ float part[32];
   float s = 0.0f;
   for (int i = threadIdx.x; i < n; i += blockDim.x) s += v[i];
@@ -385,6 +395,7 @@ __global__ void mean_kernel(const float* __restrict__ v, int n, float* __restric
 __global__ void loss_backward_kernel(const __nv_bfloat16* __restrict__ x, const int* __restrict__ y,
                                      const float* __restrict__ lse, __nv_bfloat16* __restrict__ dz, int rows,
                                      int cols) {
+  pdl_wait_and_release();
   const long long n = (long long)rows * cols;
   const float inv = 1.0f / rows;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
@@ -408,6 +419,7 @@ __global__ void loss_backward_kernel(const __nv_bfloat16* __restrict__ x, const 
 __global__ void adam_fused_kernel(const AdamSegment* __restrict__ segs, float* __restrict__ p,
                                   __nv_bfloat16* __restrict__ m, __nv_bfloat16* __restrict__ v, float b1,
                                   float b2, float lr_t, float ob1, float ob2, float eps) {
+  pdl_wait_and_release();
   const AdamSegment sg = segs[blockIdx.y];
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < sg.count;
        i += (long long)gridDim.x * blockDim.x) {
@@ -429,7 +441,7 @@ __global__ void adam_fused_kernel(const AdamSegment* __restrict__ segs, float* _
 // ---------------------------------------------------------------- launchers
 cudaError_t launch_embed_forward(const int* tok, const __nv_bfloat16* emb, const __nv_bfloat16* pos,
                                  __nv_bfloat16* out, int rows, int T, int E, cudaStream_t st) {
-  embed_forward_kernel<<<rows, 128, 0, st>>>(tok, emb, pos, out, rows, T, E);
+  launch_pdl(embed_forward_kernel, rows, 128, 0, st, tok, emb, pos, out, rows, T, E);
   count_launches(1);
   return cudaGetLastError();
 }
@@ -438,8 +450,8 @@ cudaError_t launch_embed_backward(const int* tok, const __nv_bfloat16* dz, float
                                   int B, int T, int V, int E, cudaStream_t st) {
   cudaError_t e = cudaMemsetAsync(demb, 0, (size_t)V * E * sizeof(float), st);
   if (e != cudaSuccess) return e;
-  embed_backward_kernel<<<B * T, 128, 0, st>>>(tok, dz, demb, B * T, E);
-  pos_grad_kernel<<<ew_blocks((long long)T * E), EW_THREADS, 0, st>>>(dz, dpos, B, T, E);
+  launch_pdl(embed_backward_kernel, B * T, 128, 0, st, tok, dz, demb, B * T, E);
+  launch_pdl(pos_grad_kernel, ew_blocks((long long)T * E), EW_THREADS, 0, st, dz, dpos, B, T, E);
   count_launches(2);
   return cudaGetLastError();
 }
@@ -454,13 +466,13 @@ cudaError_t launch_layernorm_forward(const __nv_bfloat16* x, __nv_bfloat16* xn, 
   auto um = [](void* p) { return reinterpret_cast<uint4*>(p); };
   if (cols % 8 == 0 && nch <= 4) {
     switch (nch) {
-      case 1: layernorm_forward_vec_kernel<1><<<grid, block, 0, st>>>(u(x), um(xn), um(out), u(gamma), u(beta), stdev, rows, cols, eps); break;
-      case 2: layernorm_forward_vec_kernel<2><<<grid, block, 0, st>>>(u(x), um(xn), um(out), u(gamma), u(beta), stdev, rows, cols, eps); break;
-      case 3: layernorm_forward_vec_kernel<3><<<grid, block, 0, st>>>(u(x), um(xn), um(out), u(gamma), u(beta), stdev, rows, cols, eps); break;
-      default: layernorm_forward_vec_kernel<4><<<grid, block, 0, st>>>(u(x), um(xn), um(out), u(gamma), u(beta), stdev, rows, cols, eps); break;
+      case 1: launch_pdl(layernorm_forward_vec_kernel<1>, grid, block, 0, st, u(x), um(xn), um(out), u(gamma), u(beta), stdev, rows, cols, eps); break;
+      case 2: launch_pdl(layernorm_forward_vec_kernel<2>, grid, block, 0, st, u(x), um(xn), um(out), u(gamma), u(beta), stdev, rows, cols, eps); break;
+      case 3: launch_pdl(layernorm_forward_vec_kernel<3>, grid, block, 0, st, u(x), um(xn), um(out), u(gamma), u(beta), stdev, rows, cols, eps); break;
+      default: launch_pdl(layernorm_forward_vec_kernel<4>, grid, block, 0, st, u(x), um(xn), um(out), u(gamma), u(beta), stdev, rows, cols, eps); break;
     }
   } else {
-    layernorm_forward_kernel<<<grid, block, 0, st>>>(x, xn, out, gamma, beta, stdev, rows, cols, eps);
+    launch_pdl(layernorm_forward_kernel, grid, block, 0, st, x, xn, out, gamma, beta, stdev, rows, cols, eps);
   }
   count_launches(1);
   return cudaGetLastError();
@@ -485,7 +497,7 @@ cudaError_t launch_layernorm_backward(__nv_bfloat16* dz, const __nv_bfloat16* xn
     const uint4* rv = reinterpret_cast<const uint4*>(res);
     auto run = [&](auto kern) {
       if (sm > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-      kern<<<blocks, LN_WARPS * 32, sm, st>>>(d, n, g, stdev, dgamma, dbeta, rows, cols, rv);
+      launch_pdl(kern, blocks, LN_WARPS * 32, sm, st, d, n, g, stdev, dgamma, dbeta, rows, cols, rv);
     };
     switch (nch) {
       case 1: run(layernorm_backward_vec_kernel<1>); break;
@@ -496,7 +508,7 @@ cudaError_t launch_layernorm_backward(__nv_bfloat16* dz, const __nv_bfloat16* xn
   } else {
     int blocks = (rows + LN_WARPS - 1) / LN_WARPS;
     if (blocks > 148 * 4) blocks = 148 * 4;
-    layernorm_backward_kernel<<<blocks, LN_WARPS * 32, 2 * cols * sizeof(float), st>>>(dz, xn, gamma, stdev,
+    launch_pdl(layernorm_backward_kernel, blocks, LN_WARPS * 32, 2 * cols * sizeof(float), st, dz, xn, gamma, stdev,
                                                                                          dgamma, dbeta, rows, cols,
                                                                                          res);
   }
@@ -506,7 +518,7 @@ cudaError_t launch_layernorm_backward(__nv_bfloat16* dz, const __nv_bfloat16* xn
 
 cudaError_t launch_cast_f32_bf16(const float* in, __nv_bfloat16* out, long long n, cudaStream_t st) {
   const long long n4 = n / 4;
-  cast_kernel<<<ew_blocks(n4), EW_THREADS, 0, st>>>(reinterpret_cast<const float4*>(in),
+  launch_pdl(cast_kernel, ew_blocks(n4), EW_THREADS, 0, st, reinterpret_cast<const float4*>(in),
                                                     reinterpret_cast<uint2*>(out), n4);
   count_launches(1);
   return cudaGetLastError();
@@ -515,15 +527,15 @@ cudaError_t launch_cast_f32_bf16(const float* in, __nv_bfloat16* out, long long 
 cudaError_t launch_loss_forward(const __nv_bfloat16* x, const int* y, float* out, float* lse, float* mean,
                                 int rows, int cols, cudaStream_t st) {
   const int wpb = 8;
-  loss_forward_kernel<<<(rows + wpb - 1) / wpb, wpb * 32, 0, st>>>(x, y, out, lse, rows, cols);
-  mean_kernel<<<1, 1024, 0, st>>>(out, rows, mean);
+  launch_pdl(loss_forward_kernel, (rows + wpb - 1) / wpb, wpb * 32, 0, st, x, y, out, lse, rows, cols);
+  launch_pdl(mean_kernel, 1, 1024, 0, st, out, rows, mean);
   count_launches(2);
   return cudaGetLastError();
 }
 
 cudaError_t launch_loss_backward(const __nv_bfloat16* x, const int* y, const float* lse, __nv_bfloat16* dz,
                                  int rows, int cols, cudaStream_t st) {
-  loss_backward_kernel<<<ew_blocks((long long)rows * cols), EW_THREADS, 0, st>>>(x, y, lse, dz, rows, cols);
+  launch_pdl(loss_backward_kernel, ew_blocks((long long)rows * cols), EW_THREADS, 0, st, x, y, lse, dz, rows, cols);
   count_launches(1);
   return cudaGetLastError();
 }
@@ -533,7 +545,7 @@ cudaError_t launch_adam_fused(const AdamSegment* segs, int nsegs, long long max_
   if (nsegs <= 0) return cudaSuccess;
   long long bx = (max_count + 4 * EW_THREADS - 1) / (4 * EW_THREADS);
   if (bx < 1) bx = 1;
-  adam_fused_kernel<<<dim3((unsigned)bx, (unsigned)nsegs), EW_THREADS, 0, st>>>(segs, p, m, v, 0.9f, 0.999f, lr_t,
+  launch_pdl(adam_fused_kernel, dim3((unsigned)bx, (unsigned)nsegs), EW_THREADS, 0, st, segs, p, m, v, 0.9f, 0.999f, lr_t,
                                                                              0.1f, 0.001f, 1e-8f);
   count_launches(1);
   return cudaGetLastError();
