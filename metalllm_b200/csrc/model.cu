@@ -287,6 +287,7 @@ int ma_model_create(const MaModelConfig* c, ma_model** out) {
   // the optimizer's segment table (one fused launch per step)
   std::vector<ma::AdamSegment> segs;
   for (const auto& p : m->params) {
+    if (p.count % 4 != 0) return fail(cudaErrorInvalidValue, "parameter size not a multiple of 4");
     segs.push_back({p.grad, p.weight, (long long)p.count, (long long)p.offset, p.grad_f32 ? 1 : 0});
     m->max_count = std::max(m->max_count, (long long)p.count);
   }

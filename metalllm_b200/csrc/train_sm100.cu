@@ -421,18 +421,47 @@ __global__ void adam_fused_kernel(const AdamSegment* __restrict__ segs, float* _
                                   float b2, float lr_t, float ob1, float ob2, float eps) {
   pdl_wait_and_release();
   const AdamSegment sg = segs[blockIdx.y];
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < sg.count;
+  // four elements per step (counts are multiples of 4, offsets of 8): 16-byte
+  // fp32 and 8-byte bf16 accesses
+  const long long n4 = sg.count / 4;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4;
        i += (long long)gridDim.x * blockDim.x) {
-    const float gi = sg.grad_f32 ? bf(tobf(static_cast<const float*>(sg.grad)[i]))
-                                 : bf(static_cast<const __nv_bfloat16*>(sg.grad)[i]);
-    const long long j = sg.offset + i;
-    const float vi = fmaf(b2, bf(v[j]), ob2 * (gi * gi));
-    const float mi = fmaf(b1, bf(m[j]), ob1 * gi);
-    v[j] = tobf(vi);
-    m[j] = tobf(mi);
-    const float pj = p[j] - lr_t * mi * rsqrtf(vi + eps);
-    p[j] = pj;
-    sg.weight[i] = tobf(pj);
+    float g[4];
+    if (sg.grad_f32) {
+      const float4 gf = static_cast<const float4*>(sg.grad)[i];
+      g[0] = bf(tobf(gf.x));
+      g[1] = bf(tobf(gf.y));
+      g[2] = bf(tobf(gf.z));
+      g[3] = bf(tobf(gf.w));
+    } else {
+      const uint2 gb = static_cast<const uint2*>(sg.grad)[i];
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&gb);
+      const float2 lo = __bfloat1622float2(h[0]), hi = __bfloat1622float2(h[1]);
+      g[0] = lo.x;
+      g[1] = lo.y;
+      g[2] = hi.x;
+      g[3] = hi.y;
+    }
+    const long long j = sg.offset / 4 + i;
+    float4 pv = reinterpret_cast<float4*>(p)[j];
+    const uint2 mv = reinterpret_cast<const uint2*>(m)[j], vv = reinterpret_cast<const uint2*>(v)[j];
+    const __nv_bfloat16* mh = reinterpret_cast<const __nv_bfloat16*>(&mv);
+    const __nv_bfloat16* vh = reinterpret_cast<const __nv_bfloat16*>(&vv);
+    float* pp = reinterpret_cast<float*>(&pv);
+    __nv_bfloat16 mo[4], vo[4], wo[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float vi = fmaf(b2, bf(vh[e]), ob2 * (g[e] * g[e]));
+      const float mi = fmaf(b1, bf(mh[e]), ob1 * g[e]);
+      vo[e] = tobf(vi);
+      mo[e] = tobf(mi);
+      pp[e] = pp[e] - lr_t * mi * rsqrtf(vi + eps);
+      wo[e] = tobf(pp[e]);
+    }
+    reinterpret_cast<float4*>(p)[j] = pv;
+    reinterpret_cast<uint2*>(m)[j] = *reinterpret_cast<const uint2*>(mo);
+    reinterpret_cast<uint2*>(v)[j] = *reinterpret_cast<const uint2*>(vo);
+    reinterpret_cast<uint2*>(sg.weight)[i] = *reinterpret_cast<const uint2*>(wo);
   }
 }
 
@@ -543,7 +572,7 @@ cudaError_t launch_loss_backward(const __nv_bfloat16* x, const int* y, const flo
 cudaError_t launch_adam_fused(const AdamSegment* segs, int nsegs, long long max_count, float* p,
                               __nv_bfloat16* m, __nv_bfloat16* v, float lr_t, cudaStream_t st) {
   if (nsegs <= 0) return cudaSuccess;
-  long long bx = (max_count + 4 * EW_THREADS - 1) / (4 * EW_THREADS);
+  long long bx = (max_count / 4 + 2 * EW_THREADS - 1) / (2 * EW_THREADS);
   if (bx < 1) bx = 1;
   launch_pdl(adam_fused_kernel, dim3((unsigned)bx, (unsigned)nsegs), EW_THREADS, 0, st, segs, p, m, v, 0.9f, 0.999f, lr_t,
                                                                              0.1f, 0.001f, 1e-8f);
