@@ -100,8 +100,11 @@ struct FwdParams {
 };
 
 // Work units, heaviest first (causal work grows with the pair index):
-// k -> (pair = npairs-1 - k / nbh, bh = bh_begin + k % nbh), dealt round-robin:
-// CTA c takes k = c, c + G, c + 2G, ... (G = gridDim.x).
+// k -> (pair = npairs-1 - k / nbh, bh = bh_begin + k % nbh), dealt in rounds
+// of G = gridDim.x in alternating direction: in round g CTA c takes
+// k = g*G + c for even g and g*G + G-1-c for odd g, which balances the
+// decreasing unit sizes across CTAs (a CTA with a large unit in one round
+// gets a small one in the next).
 struct Unit {
   int pair, b, h, nA, nB, nkv;
 };
@@ -120,7 +123,9 @@ __device__ __forceinline__ Unit decode_unit(const FwdParams& prm, int k) {
 
 // The g-th unit of this CTA, or -1 when it has none left.
 __device__ __forceinline__ int unit_of_round(const FwdParams& prm, int g) {
-  const long long k = (long long)g * gridDim.x + blockIdx.x;
+  const int G = gridDim.x;
+  const long long k = (long long)g * G + ((g & 1) ? G - 1 - (int)blockIdx.x : (int)blockIdx.x);
+  // past the end only in the last (partial) round: nothing follows it
   return k < prm.nunits ? (int)k : -1;
 }
 
