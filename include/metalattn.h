@@ -88,6 +88,22 @@ MA_API int ma_flashAttentionForward(const ma_bf16* q, const ma_bf16* k, const ma
                              ma_bf16* out, float* l, const AttentionParams* p,
                              uint32_t B, ma_stream_t stream);
 
+/* flashAttentionForward followed by computeD when dO is already known (an
+ * attention-only step, or a recomputing backward): writes out, l as
+ * ma_flashAttentionForward and D as ma_computeD(dO, out) would.  At D = 64 the
+ * dot products are formed in the forward's epilogue from the bf16-rounded O
+ * (one launch, O is not read back; D may differ from ma_computeD's by one
+ * bf16 rounding step, the fp32 sum running in another order); at D = 128 the
+ * two kernels run back to back.  No counterpart in the reference (its host
+ * calls computeD in the backward, model.h:639-647). */
+MA_API int ma_flashAttentionForwardComputeD(const ma_bf16* q, const ma_bf16* k, const ma_bf16* v,
+                                            const ma_bf16* dO, ma_bf16* out, float* l, ma_bf16* D,
+                                            const AttentionParams* p, uint32_t B, ma_stream_t stream);
+MA_API int ma_flashAttentionForwardComputeD_shard(const ma_bf16* q, const ma_bf16* k, const ma_bf16* v,
+                                                  const ma_bf16* dO, ma_bf16* out, float* l, ma_bf16* D,
+                                                  const AttentionParams* p, uint32_t B, uint32_t bh_begin,
+                                                  uint32_t bh_end, ma_stream_t stream);
+
 /* computeD: D[row, h] = bf16(sum_c dO[row, h*D+c] * O[row, h*D+c]), fp32 sum.
  * Replaces attention.metal:166-171 (buffers 0..3) dispatched at model.h:639-647. */
 MA_API int ma_computeD(const ma_bf16* dO, const ma_bf16* O, ma_bf16* D,

@@ -45,6 +45,8 @@ SIGNATURES = {
     "ma_computeQKV": [_P, _P, _P, _P, _P, _P, _P, _PP, _U32, _P],
     "ma_flashAttentionForward": [_P, _P, _P, _P, _P, _PP, _U32, _P],
     "ma_computeD": [_P, _P, _P, _PP, _U32, _P],
+    "ma_flashAttentionForwardComputeD": [_P, _P, _P, _P, _P, _P, _P, _PP, _U32, _P],
+    "ma_flashAttentionForwardComputeD_shard": [_P, _P, _P, _P, _P, _P, _P, _PP, _U32, _U32, _U32, _P],
     "ma_flashAttentionBackward": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _PP, _U32, _P],
     "ma_flashAttentionForward_shard": [_P, _P, _P, _P, _P, _PP, _U32, _U32, _U32, _P],
     "ma_computeD_shard": [_P, _P, _P, _PP, _U32, _U32, _U32, _P],

@@ -196,6 +196,28 @@ def flashAttentionForward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, p: 
     return out, l
 
 
+def flashAttentionForwardComputeD(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, dO: torch.Tensor,
+                                  p: AttentionParams, B: int, out: Optional[torch.Tensor] = None,
+                                  l: Optional[torch.Tensor] = None, D: Optional[torch.Tensor] = None,
+                                  shard: Optional[tuple] = None, stream: Optional[torch.cuda.Stream] = None):
+    """out, l, D = flashAttentionForward then computeD(dO, out), for callers
+    that know dO before the forward (ma_flashAttentionForwardComputeD; at
+    head size 64 D is formed in the forward's epilogue)."""
+    act = (B, p.M, p.N)
+    for t, n in ((q, "q"), (k, "k"), (v, "v"), (dO, "dO")):
+        _check(t, n, torch.bfloat16, act)
+    out = _out(out, q, act, torch.bfloat16, "out")
+    l = _out(l, q, (B, p.M, p.NH), torch.float32, "l")
+    D = _out(D, q, (B, p.M, p.NH), torch.bfloat16, "D")
+    if shard is None:
+        _lib.call("ma_flashAttentionForwardComputeD", _ptr(q), _ptr(k), _ptr(v), _ptr(dO), _ptr(out), _ptr(l),
+                  _ptr(D), ctypes.byref(p), B, _stream(stream))
+    else:
+        _lib.call("ma_flashAttentionForwardComputeD_shard", _ptr(q), _ptr(k), _ptr(v), _ptr(dO), _ptr(out),
+                  _ptr(l), _ptr(D), ctypes.byref(p), B, shard[0], shard[1], _stream(stream))
+    return out, l, D
+
+
 def computeD(dO: torch.Tensor, O: torch.Tensor, p: AttentionParams, B: int,
              D: Optional[torch.Tensor] = None, shard: Optional[tuple] = None,
              stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:

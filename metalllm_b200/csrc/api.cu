@@ -114,7 +114,7 @@ using bf16m = __nv_bfloat16*;
 
 int forward_impl(const ma_bf16* q, const ma_bf16* k, const ma_bf16* v, ma_bf16* out, float* l,
                  const AttentionParams* p, uint32_t B, uint32_t b0, uint32_t b1, bool range,
-                 ma_stream_t stream) {
+                 ma_stream_t stream, const ma_bf16* dO = nullptr, ma_bf16* D = nullptr) {
   ma::AttnShape s;
   int rc = check_shape(p, B, b0, b1, range, &s);
   if (rc) return rc;
@@ -123,14 +123,29 @@ int forward_impl(const ma_bf16* q, const ma_bf16* k, const ma_bf16* v, ma_bf16* 
   MA_REQUIRE_PTR(v);
   MA_REQUIRE_PTR(out);
   MA_REQUIRE_PTR(l);
+  const bool with_d = dO != nullptr || D != nullptr;
+  if (with_d) {
+    MA_REQUIRE_PTR(dO);
+    if (!D) return fail(MA_ERR_NULL, "pointer 'D' is NULL");
+    if (reinterpret_cast<uintptr_t>(D) & 1u) return fail(MA_ERR_ALIGN, "pointer 'D' is not 2-byte aligned");
+  }
   uint32_t* status = nullptr;
   rc = device_status_word(&status);
   if (rc) return rc;
   if (s.bh_end == s.bh_begin) return ok();
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // D = 64: computeD in the forward's epilogue; D = 128: the separate kernel after it
+  const bool fused = with_d && s.D == 64;
   cudaError_t e = ma::launch_flash_fwd(reinterpret_cast<bf16p>(q), reinterpret_cast<bf16p>(k),
                                        reinterpret_cast<bf16p>(v), reinterpret_cast<bf16m>(out), l, s,
-                                       status, reinterpret_cast<cudaStream_t>(stream));
+                                       status, st, fused ? reinterpret_cast<bf16p>(dO) : nullptr,
+                                       fused ? reinterpret_cast<bf16m>(D) : nullptr);
   if (e != cudaSuccess) return cuda_fail(e, "flashAttentionForward launch");
+  if (with_d && !fused) {
+    e = ma::launch_compute_d(reinterpret_cast<bf16p>(dO), reinterpret_cast<bf16p>(out), reinterpret_cast<bf16m>(D),
+                             s, st);
+    if (e != cudaSuccess) return cuda_fail(e, "computeD launch");
+  }
   return ok();
 }
 
@@ -223,6 +238,19 @@ int ma_flashAttentionForward_shard(const ma_bf16* q, const ma_bf16* k, const ma_
                                    ma_bf16* out, float* l, const AttentionParams* p, uint32_t B,
                                    uint32_t bh_begin, uint32_t bh_end, ma_stream_t stream) {
   return forward_impl(q, k, v, out, l, p, B, bh_begin, bh_end, true, stream);
+}
+
+int ma_flashAttentionForwardComputeD(const ma_bf16* q, const ma_bf16* k, const ma_bf16* v,
+                                     const ma_bf16* dO, ma_bf16* out, float* l, ma_bf16* D,
+                                     const AttentionParams* p, uint32_t B, ma_stream_t stream) {
+  return forward_impl(q, k, v, out, l, p, B, 0, 0, false, stream, dO, D);
+}
+
+int ma_flashAttentionForwardComputeD_shard(const ma_bf16* q, const ma_bf16* k, const ma_bf16* v,
+                                           const ma_bf16* dO, ma_bf16* out, float* l, ma_bf16* D,
+                                           const AttentionParams* p, uint32_t B, uint32_t bh_begin,
+                                           uint32_t bh_end, ma_stream_t stream) {
+  return forward_impl(q, k, v, out, l, p, B, bh_begin, bh_end, true, stream, dO, D);
 }
 
 int ma_computeD(const ma_bf16* dO, const ma_bf16* O, ma_bf16* D, const AttentionParams* p,
@@ -584,10 +612,14 @@ int pipeline_chunk(ma_host_pipeline* pl, int c, uint32_t b0, uint32_t bc, bool b
   uint32_t* status = nullptr;
   rc = device_status_word(&status);
   if (rc) return rc;
-  e = ma::launch_flash_fwd(s.q, s.k, s.v, s.out, s.l, sh, status, pl->comp);
+  // with the backward, dO is already here: computeD rides in the forward's
+  // epilogue at D = 64
+  const bool fuse_d = backward && sh.D == 64;
+  e = ma::launch_flash_fwd(s.q, s.k, s.v, s.out, s.l, sh, status, pl->comp, fuse_d ? s.dO : nullptr,
+                           fuse_d ? s.D : nullptr);
   if (e != cudaSuccess) return cuda_fail(e, "host pipeline: flashAttentionForward launch");
   if (backward) {
-    e = ma::launch_compute_d(s.dO, s.out, s.D, sh, pl->comp);
+    if (!fuse_d) e = ma::launch_compute_d(s.dO, s.out, s.D, sh, pl->comp);
     if (e != cudaSuccess) return cuda_fail(e, "host pipeline: computeD launch");
     e = ma::launch_flash_bwd(s.dO, s.D, s.l, s.q, s.k, s.v, s.dQ, s.dK, s.dV, sh, status, pl->comp);
     if (e != cudaSuccess) return cuda_fail(e, "host pipeline: flashAttentionBackward launch");

@@ -68,9 +68,11 @@ void count_launches(unsigned n);
 // Launchers (each returns the cudaError_t of its launch).
 cudaError_t launch_compute_d(const __nv_bfloat16* dO, const __nv_bfloat16* O,
                              __nv_bfloat16* Dv, const AttnShape& s, cudaStream_t st);
+// dO, Dv (D = 64 only, both or neither): computeD fused into the epilogue.
 cudaError_t launch_flash_fwd(const __nv_bfloat16* q, const __nv_bfloat16* k,
                              const __nv_bfloat16* v, __nv_bfloat16* out, float* lse,
-                             const AttnShape& s, uint32_t* status, cudaStream_t st);
+                             const AttnShape& s, uint32_t* status, cudaStream_t st,
+                             const __nv_bfloat16* dO = nullptr, __nv_bfloat16* Dv = nullptr);
 cudaError_t launch_flash_bwd(const __nv_bfloat16* dO, const __nv_bfloat16* Dv,
                              const float* lse, const __nv_bfloat16* q,
                              const __nv_bfloat16* k, const __nv_bfloat16* v, float* dQ,

@@ -97,7 +97,26 @@ struct FwdParams {
   float scale_log2;
   float* lse;
   uint32_t* status;
+  // fused computeD (D = 64 only, both or neither set): D[row][h] =
+  // bf16(sum_c O[row][h*64+c] * dO[row][h*64+c]) from the bf16-rounded O
+  const __nv_bfloat16* dO;
+  __nv_bfloat16* D;
 };
+
+// sum over 8 bf16 pairs of a[i] * b[i], fp32 (products of bf16 values are
+// exact in fp32)
+__device__ __forceinline__ float dot_bf16x8(uint4 a, uint4 b) {
+  const __nv_bfloat162* x = reinterpret_cast<const __nv_bfloat162*>(&a);
+  const __nv_bfloat162* y = reinterpret_cast<const __nv_bfloat162*>(&b);
+  float s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 fx = __bfloat1622float2(x[i]), fy = __bfloat1622float2(y[i]);
+    s = fmaf(fx.x, fy.x, s);
+    s = fmaf(fx.y, fy.y, s);
+  }
+  return s;
+}
 
 // Work units, heaviest first (causal work grows with the pair index):
 // k -> (pair = npairs-1 - k / nbh, bh = bh_begin + k % nbh), dealt in rounds
@@ -363,6 +382,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       // Instantiated twice so that the other tiles carry no masking code.
       auto tile = [&](auto diag_tag, int j) -> bool {
         constexpr bool DIAG = decltype(diag_tag)::value;
+        if constexpr (DIAG && C::P_TMEM) {
+          // the unit's last key tile: this thread's dO row goes into its row
+          // of the (still unused) O staging, in the staging's swizzle, while
+          // the tile is processed; the epilogue reads it back before
+          // writing O over it (each thread touches only its own row).  Issued
+          // only now: a copy in flight during the whole unit slows its UMMAs
+          const int grow = qtile * BM + row;
+          if (prm.dO && grow < prm.T) {
+            const __nv_bfloat16* src = prm.dO + ((long long)un.b * prm.T + grow) * (prm.NH * HD) + un.h * HD;
+#pragma unroll
+            for (int i = 0; i < HD / 8; ++i) {
+              const uint32_t dst =
+                  smem_u32(pbuf + (i / 8) * (BM * 128) + row * 128 + (((i % 8) ^ (row & 7)) * 16));
+              asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src + i * 8) : "memory");
+            }
+            asm volatile("cp.async.commit_group;" ::: "memory");
+          }
+        }
         if (!mbar_wait_warp(BAR_SF(x), sc & 1, abort_p)) return false;
         tc_fence_after();
         float s[BN];
@@ -477,6 +514,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (epi) {
         tc_fence_after();
         const float inv = 1.0f / l_sum;
+        const int grow = qtile * BM + row;
+        const bool fuse_d = C::P_TMEM && prm.dO && grow < prm.T;
+        if (fuse_d) asm volatile("cp.async.wait_group 0;" ::: "memory");
+        float dsum = 0.0f;
         // stage O (bf16) in this tile's P buffer (free: its last PV is done)
 #pragma unroll
         for (int cc = 0; cc < HD; cc += 16) {
@@ -494,15 +535,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           v1.w = pack_bf16(__uint_as_float(r[14]) * inv, __uint_as_float(r[15]) * inv);
           const int kb = cc / 64, ch = (cc % 64) / 8;
           uint8_t* blk = pbuf + kb * (BM * 128) + row * 128;
-          *reinterpret_cast<uint4*>(blk + ((ch ^ (row & 7)) * 16)) = v0;
-          *reinterpret_cast<uint4*>(blk + (((ch + 1) ^ (row & 7)) * 16)) = v1;
+          uint4* p0 = reinterpret_cast<uint4*>(blk + ((ch ^ (row & 7)) * 16));
+          uint4* p1 = reinterpret_cast<uint4*>(blk + (((ch + 1) ^ (row & 7)) * 16));
+          if (fuse_d) dsum += dot_bf16x8(v0, *p0) + dot_bf16x8(v1, *p1);  // dO, then O over it
+          *p0 = v0;
+          *p1 = v1;
         }
         tc_fence_before();
         mbar_arrive(BAR_OE(x));  // O_X may be overwritten by the next unit
         fence_proxy_async_smem();
-        const int grow = qtile * BM + row;
-        if (grow < prm.T)
-          prm.lse[((long long)un.b * prm.T + grow) * prm.NH + un.h] = (m_used + log2f(l_sum)) * LN2;
+        if (grow < prm.T) {
+          const long long ri = ((long long)un.b * prm.T + grow) * prm.NH + un.h;
+          prm.lse[ri] = (m_used + log2f(l_sum)) * LN2;
+          if (fuse_d) prm.D[ri] = __float2bfloat16_rn(dsum);
+        }
       }
       // every thread of the warpgroup takes this barrier and leaves it with the
       // same verdict, so the warpgroup stays in step after a failed wait
@@ -529,7 +575,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 template <int HD>
 cudaError_t launch_fwd(const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* v,
                        __nv_bfloat16* out, float* lse, const AttnShape& s, uint32_t* status,
-                       cudaStream_t st) {
+                       cudaStream_t st, const __nv_bfloat16* dO, __nv_bfloat16* Dv) {
   using C = FwdCfg<HD>;
   // The setmaxnreg split assumes the kernel was compiled to exactly
   // LAUNCH_REGS registers per thread; refuse to launch otherwise.
@@ -559,6 +605,8 @@ cudaError_t launch_fwd(const __nv_bfloat16* q, const __nv_bfloat16* k, const __n
   prm.scale_log2 = LOG2E / sqrtf((float)HD);
   prm.lse = lse;
   prm.status = status;
+  prm.dO = dO;
+  prm.D = Dv;
   cudaError_t e = cudaFuncSetAttribute(flash_fwd_kernel<HD>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
   if (e != cudaSuccess) return e;
@@ -575,10 +623,12 @@ cudaError_t launch_fwd(const __nv_bfloat16* q, const __nv_bfloat16* k, const __n
 
 cudaError_t launch_flash_fwd(const __nv_bfloat16* q, const __nv_bfloat16* k,
                              const __nv_bfloat16* v, __nv_bfloat16* out, float* lse,
-                             const AttnShape& s, uint32_t* status, cudaStream_t st) {
+                             const AttnShape& s, uint32_t* status, cudaStream_t st,
+                             const __nv_bfloat16* dO, __nv_bfloat16* Dv) {
   if (s.bh_end <= s.bh_begin) return cudaSuccess;
-  return s.D == 64 ? launch_fwd<64>(q, k, v, out, lse, s, status, st)
-                   : launch_fwd<128>(q, k, v, out, lse, s, status, st);
+  if ((dO == nullptr) != (Dv == nullptr) || (dO && s.D != 64)) return cudaErrorInvalidValue;
+  return s.D == 64 ? launch_fwd<64>(q, k, v, out, lse, s, status, st, dO, Dv)
+                   : launch_fwd<128>(q, k, v, out, lse, s, status, st, nullptr, nullptr);
 }
 
 }  // namespace ma

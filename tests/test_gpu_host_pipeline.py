@@ -1,5 +1,6 @@
 """Host-resident batches through ma_host_pipeline_*: the chunked copy /
 compute / copy-back pipeline gives the same bits as the device entry points
+(forward with computeD, then backward)
 (every (batch, head) is independent, so chunking the batch changes nothing),
 for a ragged last chunk, both head sizes, pinned and pageable host memory,
 and repeated calls on one pipeline."""
@@ -33,8 +34,7 @@ def _host(B, T, H, D, seed, pin):
 def _device_reference(A, q, k, v, dO, B, T, H, D):
     p = A.make_params(T, H, D)
     dq, dk, dv, ddo = (t.cuda() for t in (q, k, v, dO))
-    out, l = A.flashAttentionForward(dq, dk, dv, p, B)
-    Dv = A.computeD(ddo, out, p, B)
+    out, l, Dv = A.flashAttentionForwardComputeD(dq, dk, dv, ddo, p, B)
     dQ, dK, dV = A.flashAttentionBackward(ddo, Dv, l, dq, dk, dv, p, B)
     torch.cuda.synchronize()
     return [t.cpu() for t in (out, l, dQ, dK, dV)]

@@ -179,6 +179,36 @@ def test_shard_entry_points(A, T):
             assert np.isnan(g).all()
 
 
+@pytest.mark.parametrize("B,T,H,D,shard", [(2, 100, 3, 64, None), (4, 256, 6, 64, None),
+                                         (2, 1024, 2, 64, None), (3, 200, 2, 64, (1, 5)),
+                                         (2, 130, 3, 128, None)])
+def test_forward_with_fused_compute_d(A, B, T, H, D, shard):
+    """ma_flashAttentionForwardComputeD: out and l bit-identical to the plain
+    forward, D within one bf16 step of computeD on the same O (the fused fp32
+    sum runs in another order); a shard touches only its (batch, head) slabs."""
+    q, k, v, do = inputs(B, T, H, D, seed=27)
+    p = A.make_params(T, H, D)
+    tq, tk, tv, tdo = up(q), up(k), up(v), up(do)
+    sentinel = lambda shp, dt: torch.full(shp, 7.0, dtype=dt, device="cuda")
+    ref_out, ref_l = sentinel((B, T, H * D), torch.bfloat16), sentinel((B, T, H), torch.float32)
+    A.flashAttentionForward(tq, tk, tv, p, B, out=ref_out, l=ref_l, shard=shard)
+    ref_D = sentinel((B, T, H), torch.bfloat16)
+    A.computeD(tdo, ref_out, p, B, D=ref_D, shard=shard)
+    out, l, Dv = (sentinel((B, T, H * D), torch.bfloat16), sentinel((B, T, H), torch.float32),
+                  sentinel((B, T, H), torch.bfloat16))
+    A.flashAttentionForwardComputeD(tq, tk, tv, tdo, p, B, out=out, l=l, D=Dv, shard=shard)
+    torch.cuda.synchronize()
+    assert A.device_status() == 0
+    assert torch.equal(out, ref_out) and torch.equal(l, ref_l)
+    got, want = Dv.float().cpu().numpy(), ref_D.float().cpu().numpy()
+    assert np.abs(got - want).max() <= 2 ** -7 * max(1.0, np.abs(want).max())
+    if shard is not None:  # untouched slabs keep the sentinel
+        flat = Dv.float().cpu().numpy()
+        for bh in list(range(0, shard[0])) + list(range(shard[1], B * H)):
+            b, h = divmod(bh, H)
+            assert np.all(flat[b, :, h] == 7.0)
+
+
 def test_determinism(A):
     B, T, H, D = 2, 512, 2, 64
     q, k, v, do = inputs(B, T, H, D, seed=21)
