@@ -81,7 +81,7 @@ struct FwdCfg {
   static constexpr uint32_t OFF_BAR = OFF_P + 2 * STG_BYTES;
   // q_full/empty[QST], k_full/empty[KST], v_full/empty[VST], per tile X:
   // s_full, s_free, p_full, pv_done, o_free
-  static constexpr int NBAR = 2 * QST + 2 * KST + 2 * VST + 2 * 5;
+  static constexpr int NBAR = 2 * QST + 2 * KST + 2 * VST + 2 * 6;
   static constexpr uint32_t OFF_TSLOT = OFF_BAR + NBAR * 8;
   static constexpr uint32_t SMEM_BYTES = OFF_TSLOT + 16 + 1024;  // + alignment slack
   static constexpr uint32_t TCOL_S = 0;     // S_A, S_B at columns 0, 128
@@ -152,6 +152,7 @@ template <int HD>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                     const __grid_constant__ CUtensorMap tmdO,
                      const FwdParams prm) {
   pdl_wait_and_release();
   using C = FwdCfg<HD>;
@@ -176,6 +177,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   auto BAR_PF = [&](int x) { return barX + 8u * (2 * 2 + x); };
   auto BAR_PV = [&](int x) { return barX + 8u * (3 * 2 + x); };
   auto BAR_OE = [&](int x) { return barX + 8u * (4 * 2 + x); };
+  auto BAR_DO = [&](int x) { return barX + 8u * (5 * 2 + x); };  // dO tile of X landed (fused computeD)
   const uint32_t tslot = sbase + C::OFF_TSLOT;
 
   if (threadIdx.x == 0) {
@@ -198,6 +200,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(BAR_PF(x), 128);
       mbar_init(BAR_PV(x), 1);
       mbar_init(BAR_OE(x), 128);
+      mbar_init(BAR_DO(x), 1);
     }
     fence_mbar_init();
   }
@@ -366,6 +369,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const bool wg_leader = (warp == 4 + 4 * x) && lane == 0;
     uint8_t* pbuf = gbase + C::OFF_P + x * C::STG_BYTES;
     uint32_t sc = 0;  // S_X consumed so far (== P_X produced)
+    uint32_t nd = 0;  // dO tiles of X loaded so far (fused computeD)
     bool ok = true;
     for (int g = 0; ok; ++g) {
       const int k = unit_of_round(prm, g);
@@ -383,21 +387,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       auto tile = [&](auto diag_tag, int j) -> bool {
         constexpr bool DIAG = decltype(diag_tag)::value;
         if constexpr (DIAG && C::P_TMEM) {
-          // the unit's last key tile: this thread's dO row goes into its row
-          // of the (still unused) O staging, in the staging's swizzle, while
-          // the tile is processed; the epilogue reads it back before
-          // writing O over it (each thread touches only its own row).  Issued
-          // only now: a copy in flight during the whole unit slows its UMMAs
-          const int grow = qtile * BM + row;
-          if (prm.dO && grow < prm.T) {
-            const __nv_bfloat16* src = prm.dO + ((long long)un.b * prm.T + grow) * (prm.NH * HD) + un.h * HD;
-#pragma unroll
-            for (int i = 0; i < HD / 8; ++i) {
-              const uint32_t dst =
-                  smem_u32(pbuf + (i / 8) * (BM * 128) + row * 128 + (((i % 8) ^ (row & 7)) * 16));
-              asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src + i * 8) : "memory");
-            }
-            asm volatile("cp.async.commit_group;" ::: "memory");
+          // the unit's last key tile: the dO tile of X goes by TMA into the O
+          // staging (idle until the epilogue; rows past T read as zero); the
+          // epilogue reads each chunk back before writing O over it
+          if (prm.dO && wg_leader) {
+            mbar_arrive_expect_tx(BAR_DO(x), BM * HD * 2);
+            for (int kb = 0; kb < C::KB; ++kb)
+              tma_load_3d(smem_u32(pbuf) + kb * BM * 128, &tmdO, BAR_DO(x), un.h * HD + kb * 64, qtile * BM,
+                          un.b);
           }
         }
         if (!mbar_wait_warp(BAR_SF(x), sc & 1, abort_p)) return false;
@@ -515,8 +512,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tc_fence_after();
         const float inv = 1.0f / l_sum;
         const int grow = qtile * BM + row;
-        const bool fuse_d = C::P_TMEM && prm.dO && grow < prm.T;
-        if (fuse_d) asm volatile("cp.async.wait_group 0;" ::: "memory");
+        const bool fuse_d = C::P_TMEM && prm.dO;
+        bool dok = true;
+        if (fuse_d) dok = mbar_wait_warp(BAR_DO(x), nd & 1, abort_p);
         float dsum = 0.0f;
         // stage O (bf16) in this tile's P buffer (free: its last PV is done)
 #pragma unroll
@@ -547,8 +545,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (grow < prm.T) {
           const long long ri = ((long long)un.b * prm.T + grow) * prm.NH + un.h;
           prm.lse[ri] = (m_used + log2f(l_sum)) * LN2;
-          if (fuse_d) prm.D[ri] = __float2bfloat16_rn(dsum);
+          if (fuse_d && dok) prm.D[ri] = __float2bfloat16_rn(dsum);
         }
+        if (fuse_d) ++nd;
       }
       // every thread of the warpgroup takes this barrier and leaves it with the
       // same verdict, so the warpgroup stays in step after a failed wait
@@ -586,7 +585,7 @@ cudaError_t launch_fwd(const __nv_bfloat16* q, const __nv_bfloat16* k, const __n
     return a.numRegs == LAUNCH_REGS ? cudaSuccess : cudaErrorInvalidKernelImage;
   }();
   if (reg_check != cudaSuccess) return reg_check;
-  CUtensorMap tq, tk, tv, to;
+  CUtensorMap tq, tk, tv, to, tdo;
   const CUtensorMapDataType bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B;
   if (!make_tmap_3d(&tq, q, bf, 2, s.N, s.T, s.B, 64, BM, sw) ||
@@ -594,6 +593,11 @@ cudaError_t launch_fwd(const __nv_bfloat16* q, const __nv_bfloat16* k, const __n
       !make_tmap_3d(&tv, v, bf, 2, s.N, s.T, s.B, 64, BN, sw) ||
       !make_tmap_3d(&to, out, bf, 2, s.N, s.T, s.B, 64, BM, sw))
     return cudaErrorInvalidValue;
+  if (dO) {
+    if (!make_tmap_3d(&tdo, dO, bf, 2, s.N, s.T, s.B, 64, BM, sw)) return cudaErrorInvalidValue;
+  } else {
+    tdo = tq;  // not read without dO
+  }
   FwdParams prm;
   prm.T = s.T;
   prm.NH = s.NH;
@@ -614,7 +618,7 @@ cudaError_t launch_fwd(const __nv_bfloat16* q, const __nv_bfloat16* k, const __n
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int grid = prm.nunits < sms ? prm.nunits : sms;
-  launch_pdl(flash_fwd_kernel<HD>, grid, NUM_THREADS, C::SMEM_BYTES, st, tq, tk, tv, to, prm);
+  launch_pdl(flash_fwd_kernel<HD>, grid, NUM_THREADS, C::SMEM_BYTES, st, tq, tk, tv, to, tdo, prm);
   count_launches(1);
   return cudaGetLastError();
 }
