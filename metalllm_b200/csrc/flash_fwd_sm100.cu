@@ -22,7 +22,10 @@
 //                query row = TMEM lane; row max/sum in registers, lazy O
 //                rescaling (only when the running max grows by more than 2^8),
 //                epilogue O/rowsum -> bf16 -> smem -> TMA store, and
-//                l = m + ln(rowsum) in fp32.
+//                l = m + ln(rowsum) in fp32.  Given dO (D=64), the leader
+//                also TMA-loads the dO tile into the O staging during the
+//                last key tile and the epilogue forms computeD's
+//                D = sum(bf16(O) * dO) per row before writing O over it.
 // Conventions match the reference: scale 1/sqrt(D) applied to Q K^T, key >
 // query masked, l stored fp32 at [row*NH + head], O = (sum P V) / rowsum.  S
 // stays fp32 (the reference rounds it to bf16); P is bf16 as in the reference
