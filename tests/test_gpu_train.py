@@ -17,6 +17,9 @@ from metalllm_b200.inputs import bf16_bits_to_f32  # noqa: E402
 pytestmark = pytest.mark.gpu
 
 SMALL = dict(B=2, T=64, E=128, NH=2, layers=2, mlp_scale=2, vocab=128)
+# head size 128, a sequence length that is not a multiple of the 128-row
+# tile, a wider MLP and another vocabulary size
+SMALL_D128 = dict(B=3, T=200, E=256, NH=2, layers=1, mlp_scale=4, vocab=192)
 
 
 @pytest.fixture(scope="module")
@@ -51,9 +54,9 @@ def _grad(model, name):
     return g if g.dtype == np.float32 else bf16_bits_to_f32(g)
 
 
-def test_small_model_step_matches_oracle(T):
+@pytest.mark.parametrize("c", [SMALL, SMALL_D128], ids=["d64", "d128_ragged"])
+def test_small_model_step_matches_oracle(T, c):
     from oracle import train_oracle as O
-    c = SMALL
     model = T.TrainingModel(**c, seed=3)
     shapes = _shapes(c)
     assert set(model.param_names()) == set(shapes)
