@@ -563,11 +563,15 @@ cudaError_t launch_gemm_bf16_act(const __nv_bfloat16* A, const __nv_bfloat16* B,
 
 // Split-K GEMM into an fp32 output (zeroed here): C[M][N] = A . B with both
 // operands MN-major ([K][M], [K][N]); used for weight gradients, whose K (the
-// B*T activation rows) is long and whose M x N is small.  Enough K chunks to
-// give about two CTAs per SM.
-int pick_ksplit(int tiles, int K) {
+// B*T activation rows) is long and whose M x N is small.  As many K chunks
+// as fill the co-resident CTA slots (ctas_per_sm per SM) in one wave, never
+// more: a grid just past the slots would run a nearly empty second wave.
+int pick_ksplit(int tiles, int K, int ctas_per_sm) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int nk = (K + BK - 1) / BK;
-  int s = (296 + tiles - 1) / tiles;
+  int s = (sms * ctas_per_sm) / tiles;
   if (s > nk / 4) s = nk / 4;  // at least 4 K steps per chunk
   return s < 1 ? 1 : s;
 }
@@ -584,11 +588,11 @@ cudaError_t launch_gemm_splitk_f32(const __nv_bfloat16* A, const __nv_bfloat16* 
   if (N % 128 == 0) {  // 128-wide tiles: fewer operand re-reads, N = 128 UMMAs
     const int tiles = ((M + 127) / 128) * (N / 128);
     return run_gemm<128, true, true, false>(&a, 1, &b, 1, c, cf, 1, 1, M, N, K, status, st,
-                                            pick_ksplit(tiles, K));
+                                            pick_ksplit(tiles, K, 2));
   }
   const int tiles = ((M + 127) / 128) * ((N + 63) / 64);
   return run_gemm<64, true, true, false>(&a, 1, &b, 1, c, cf, 1, 1, M, N, K, status, st,
-                                         pick_ksplit(tiles, K));
+                                         pick_ksplit(tiles, K, 3));
 }
 
 // rows = B*M activations rows, n = N (= NH*D)
@@ -663,10 +667,11 @@ cudaError_t launch_grad_dw_splitk_f32(const __nv_bfloat16* x, const __nv_bfloat1
   if (n % 128 == 0) {
     const int tiles = 3 * ((n + 127) / 128) * (n / 128);
     return run_gemm<128, true, true, false>(&a, 1, b, 3, c, cf, 3, 1, n, n, rows, status, st,
-                                            pick_ksplit(tiles, rows));
+                                            pick_ksplit(tiles, rows, 2));
   }
   const int tiles = 3 * ((n + 127) / 128) * ((n + 63) / 64);
-  return run_gemm<64, true, true, false>(&a, 1, b, 3, c, cf, 3, 1, n, n, rows, status, st, pick_ksplit(tiles, rows));
+  return run_gemm<64, true, true, false>(&a, 1, b, 3, c, cf, 3, 1, n, n, rows, status, st,
+                                         pick_ksplit(tiles, rows, 3));
 }
 
 cudaError_t launch_grad_dx_bf16(void* dx, bool dx_f32, const __nv_bfloat16* qw, const __nv_bfloat16* kw,
