@@ -15,6 +15,8 @@
  * Device buffers are allocated once by the constructor.  Errors throw
  * std::runtime_error with the library's message (the reference exits).
  *
+ * metalattn::Model mirrors the reference's Model (model.h) over ma_model_*.
+ *
  * Header-only; needs cuda_runtime.h and linking with -lmetalattn -lcudart.
  */
 #ifndef METALATTN_HPP_
@@ -154,6 +156,92 @@ class CudaAttention {
   void *qw_ = nullptr, *kw_ = nullptr, *vw_ = nullptr, *projw_ = nullptr, *dProjw_ = nullptr, *dKw_ = nullptr,
        *dVw_ = nullptr;
   void *dQ_ = nullptr, *dX_ = nullptr, *dQw_ = nullptr, *l_ = nullptr, *D_ = nullptr;
+};
+
+// The reference's Model (model.h:17-860): the whole training step (embedding,
+// layers of LayerNorm + attention + MLP, final LayerNorm, vocabulary
+// projection, loss, Adam) with the constructor's shape arguments (m = block
+// size, v = vocabulary, e = embedding width, s = MLP scale, d = head size)
+// plus the layer count, a batch of B sequences, the learning rate and the
+// initialisation seed.  forward() takes host token ids and targets
+// ([B][m] uint32, as model.h:414 reads them) and returns the mean loss.
+class Model {
+ public:
+  Model(int m, int v, int e, int s, int d, int layers, int batch = 1, float lr = 0.003f, uint64_t seed = 0)
+      : B_(batch), m_(m) {
+    if (m <= 0 || v <= 0 || e <= 0 || s <= 0 || d <= 0 || layers <= 0 || batch <= 0 || e % d != 0)
+      throw std::runtime_error("Model: invalid shape");
+    MaModelConfig cfg{static_cast<uint32_t>(batch), static_cast<uint32_t>(m), static_cast<uint32_t>(e),
+                      static_cast<uint32_t>(e / d), static_cast<uint32_t>(layers), static_cast<uint32_t>(s),
+                      static_cast<uint32_t>(v), lr, seed};
+    if (ma_model_create(&cfg, &model_) != MA_OK)
+      throw std::runtime_error(std::string("ma_model_create: ") + ma_model_last_error());
+    check_cuda(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
+    const size_t n = static_cast<size_t>(batch) * m;
+    check_cuda(cudaMalloc(&tokens_, n * 4), "cudaMalloc");
+    check_cuda(cudaMalloc(&targets_, n * 4), "cudaMalloc");
+  }
+
+  Model(const Model&) = delete;
+  Model& operator=(const Model&) = delete;
+
+  ~Model() {
+    if (stream_) cudaStreamSynchronize(stream_);
+    if (tokens_) cudaFree(tokens_);
+    if (targets_) cudaFree(targets_);
+    if (model_) ma_model_destroy(model_);
+    if (stream_) cudaStreamDestroy(stream_);
+  }
+
+  // model.h:414-536
+  float forward(const uint32_t* tokens, const uint32_t* targets) {
+    const size_t n = static_cast<size_t>(B_) * m_;
+    check_cuda(cudaMemcpyAsync(tokens_, tokens, n * 4, cudaMemcpyHostToDevice, stream_), "cudaMemcpyAsync");
+    check_cuda(cudaMemcpyAsync(targets_, targets, n * 4, cudaMemcpyHostToDevice, stream_), "cudaMemcpyAsync");
+    run(ma_model_forward(model_, static_cast<const int32_t*>(tokens_), static_cast<const int32_t*>(targets_),
+                         reinterpret_cast<ma_stream_t>(stream_)),
+        "ma_model_forward");
+    check_cuda(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");
+    float loss = 0.0f;
+    run(ma_model_read(model_, "loss", &loss, sizeof(loss)), "ma_model_read");
+    return loss;
+  }
+
+  // model.h:538-712
+  void backward() { run(ma_model_backward(model_, reinterpret_cast<ma_stream_t>(stream_)), "ma_model_backward"); }
+
+  // model.h:726-757 (Adam)
+  void step() {
+    run(ma_model_step(model_, reinterpret_cast<ma_stream_t>(stream_)), "ma_model_step");
+    check_cuda(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");
+    uint32_t status = 0;
+    run(ma_model_status(model_, &status), "ma_model_status");
+    if (status) throw std::runtime_error("a kernel gave up on a bounded wait (model status word set)");
+  }
+
+  // synchronous copies of a named tensor (a parameter, "grad.<name>", "logits", ...)
+  void read(const char* name, void* host, uint64_t bytes) {
+    check_cuda(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");
+    run(ma_model_read(model_, name, host, bytes), "ma_model_read");
+  }
+  void write(const char* name, const void* host, uint64_t bytes) {
+    check_cuda(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");
+    run(ma_model_write(model_, name, host, bytes), "ma_model_write");
+  }
+
+  ma_model* handle() const { return model_; }
+  cudaStream_t stream() const { return stream_; }
+
+ private:
+  static void run(int rc, const char* what) {
+    if (rc != MA_OK) throw std::runtime_error(std::string(what) + ": " + ma_model_last_error());
+  }
+
+  int B_, m_;
+  ma_model* model_ = nullptr;
+  cudaStream_t stream_ = nullptr;
+  void* tokens_ = nullptr;
+  void* targets_ = nullptr;
 };
 
 }  // namespace metalattn

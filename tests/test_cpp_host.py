@@ -1,8 +1,9 @@
-"""The C++ host mirror of the reference's MetalAttention harness
-(include/metalattn.hpp, main.cpp:955-1284): it compiles and links as a
-reference-side C++ host would (CPU test), and on a GPU its forward/backward
+"""The C++ host mirrors in include/metalattn.hpp: CudaAttention (the
+reference's MetalAttention harness, main.cpp:955-1284) compiles and links as
+a reference-side C++ host would (CPU test), and on a GPU its forward/backward
 give the same bits as the same entry points called from Python, with dX and
-dQw rounded to bf16 on the host as the reference does."""
+dQw rounded to bf16 on the host as the reference does; Model (model.h's
+Model) gives the same loss sequence as the Python TrainingModel."""
 import subprocess
 from pathlib import Path
 
@@ -110,3 +111,69 @@ def test_cpp_mirror_matches_python_path(tmp_path, cuda_lib, m, n, d, B):
             bits(dVw)]
     for name, g_, w_ in zip(("out", "dprojw", "dX", "dqw", "dkw", "dvw"), parts, want):
         assert np.array_equal(g_, w_), name
+
+
+MODEL_SRC = r'''
+#include "metalattn.hpp"
+#include <cstdio>
+#include <cstdlib>
+#include <vector>
+// usage: model in.bin  (tokens[B*m], targets[B*m] uint32); prints one loss per step
+int main(int argc, char** argv) {
+  const int m = 64, v = 128, e = 128, s = 2, d = 64, layers = 2, B = 2;
+  std::vector<uint32_t> tok(B * m), tgt(B * m);
+  FILE* f = std::fopen(argv[1], "rb");
+  if (!f || std::fread(tok.data(), 4, tok.size(), f) != tok.size() ||
+      std::fread(tgt.data(), 4, tgt.size(), f) != tgt.size())
+    return 3;
+  std::fclose(f);
+  try {
+    metalattn::Model model(m, v, e, s, d, layers, B, 0.003f, 3);
+    for (int i = 0; i < 4; ++i) {  // Model::forward returns the loss (model.h:414), then backward, step
+      const float loss = model.forward(tok.data(), tgt.data());
+      model.backward();
+      model.step();
+      std::printf("%.9g\n", loss);
+    }
+  } catch (const std::exception& ex) {
+    std::fprintf(stderr, "%s\n", ex.what());
+    return 5;
+  }
+  return 0;
+}
+'''
+
+
+@pytest.mark.gpu
+def test_cpp_model_mirror_matches_python_training_model(tmp_path, cuda_lib):
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    from metalllm_b200 import train as T
+    src, exe, inp = tmp_path / "model.cpp", tmp_path / "model", tmp_path / "tok.bin"
+    src.write_text(MODEL_SRC)
+    libdir = ROOT / "metalllm_b200"
+    subprocess.run(["g++", "-std=c++17", "-O2", "-I", str(ROOT / "include"), "-I", str(CUDA / "include"), str(src),
+                    "-L", str(libdir), "-lmetalattn", "-L", str(CUDA / "lib64"), "-lcudart",
+                    f"-Wl,-rpath,{libdir}", f"-Wl,-rpath,{CUDA / 'lib64'}", "-o", str(exe)], check=True)
+    rng = np.random.default_rng(9)
+    tok = rng.integers(0, 128, (2, 64)).astype(np.uint32)
+    tgt = rng.integers(0, 128, (2, 64)).astype(np.uint32)
+    with open(inp, "wb") as f:
+        f.write(tok.tobytes())
+        f.write(tgt.tobytes())
+    r = subprocess.run([str(exe), str(inp)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    cpp_losses = [float(x) for x in r.stdout.split()]
+    model = T.TrainingModel(B=2, T=64, E=128, NH=2, layers=2, mlp_scale=2, vocab=128, lr=0.003, seed=3)
+    ttok = torch.from_numpy(tok.astype(np.int32)).cuda()
+    ttgt = torch.from_numpy(tgt.astype(np.int32)).cuda()
+    py_losses = []
+    for _ in range(4):
+        model.forward(ttok, ttgt)
+        py_losses.append(model.loss())
+        model.backward()
+        model.step()
+    model.close()
+    assert np.array_equal(np.float32(cpp_losses), np.float32(py_losses)), (cpp_losses, py_losses)
+    assert cpp_losses[-1] < cpp_losses[0]
