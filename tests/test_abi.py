@@ -140,3 +140,52 @@ def test_python_api_refuses_cpu_tensors():
     x = torch.zeros(1, 64, 64, dtype=torch.bfloat16)
     with pytest.raises(ValueError, match="CUDA"):
         A.flashAttentionForward(x, x, x, p, 1)
+
+
+def test_forward_compute_d_validates_its_extra_buffers(cuda_lib):
+    """ma_flashAttentionForwardComputeD checks dO and D like every other
+    buffer, before any device work."""
+    p = _params()
+    rc = cuda_lib.ma_flashAttentionForwardComputeD(ALIGNED, ALIGNED, ALIGNED, None, ALIGNED, ALIGNED, ALIGNED,
+                                                   ctypes.byref(p), 1, None)
+    assert rc == 2 and "'dO'" in _err(cuda_lib)
+    rc = cuda_lib.ma_flashAttentionForwardComputeD(ALIGNED, ALIGNED, ALIGNED, ALIGNED, ALIGNED, ALIGNED, None,
+                                                   ctypes.byref(p), 1, None)
+    assert rc == 2 and "'D'" in _err(cuda_lib)
+    rc = cuda_lib.ma_flashAttentionForwardComputeD(ALIGNED, ALIGNED, ALIGNED, ALIGNED, ALIGNED, ALIGNED,
+                                                   ALIGNED + 1, ctypes.byref(p), 1, None)
+    assert rc == 3 and "'D'" in _err(cuda_lib)
+    bad = _params(N=383)
+    rc = cuda_lib.ma_flashAttentionForwardComputeD(ALIGNED, ALIGNED, ALIGNED, ALIGNED, ALIGNED, ALIGNED, ALIGNED,
+                                                   ctypes.byref(bad), 1, None)
+    assert rc == 1
+
+
+def test_host_pipeline_validates_before_allocating(cuda_lib):
+    """The host-buffer pipeline rejects bad shapes, a zero chunk and NULL
+    outputs without touching a device; its run entry points reject a NULL
+    pipeline, and destroying NULL is a no-op."""
+    out = ctypes.c_void_p(ALIGNED)
+    bad = _params(D=96, N=384)
+    assert cuda_lib.ma_host_pipeline_create(ctypes.byref(bad), 8, ctypes.byref(out)) == 1
+    assert out.value is None  # cleared on failure
+    p = _params()
+    assert cuda_lib.ma_host_pipeline_create(ctypes.byref(p), 0, ctypes.byref(out)) == 1
+    assert cuda_lib.ma_host_pipeline_create(ctypes.byref(p), 8, None) == 2
+    rc = cuda_lib.ma_flashAttentionForward_host(None, ALIGNED, ALIGNED, ALIGNED, ALIGNED, ALIGNED, 8, None)
+    assert rc == 2, _err(cuda_lib)
+    rc = cuda_lib.ma_attentionForwardBackward_host(None, ALIGNED, ALIGNED, ALIGNED, ALIGNED, ALIGNED, ALIGNED,
+                                                   ALIGNED, ALIGNED, ALIGNED, 8, None)
+    assert rc == 2
+    assert cuda_lib.ma_host_pipeline_destroy(None) == 0
+
+
+def test_host_pipeline_without_gpu_fails_cleanly(cuda_lib):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    out = ctypes.c_void_p()
+    p = _params()
+    rc = cuda_lib.ma_host_pipeline_create(ctypes.byref(p), 8, ctypes.byref(out))
+    assert rc in (4, 7), _err(cuda_lib)
+    assert out.value is None
