@@ -141,9 +141,11 @@ int ma_model_create(const MaModelConfig* c, ma_model** out) {
     return merr(MA_ERR_SHAPE, "empty model configuration");
   if (c->E % c->NH != 0 || (c->E / c->NH != 64 && c->E / c->NH != 128))
     return merr(MA_ERR_SHAPE, "head size E/NH must be 64 or 128");
-  if (c->E % 64 != 0 || c->vocab % 64 != 0 || (c->E * c->mlp_scale) % 64 != 0)
+  if (c->E % 64 != 0 || c->vocab % 64 != 0 || ((uint64_t)c->E * c->mlp_scale) % 64 != 0)
     return merr(MA_ERR_SHAPE, "E, vocab and the MLP width must be multiples of 64");
   if ((uint64_t)c->B * c->T >= (1u << 30)) return merr(MA_ERR_LIMIT, "B*T too large");
+  if (c->E > 16384 || (uint64_t)c->E * c->mlp_scale > 65536 || c->vocab > (1u << 20) || c->layers > 4096)
+    return merr(MA_ERR_LIMIT, "E <= 16384, E*mlp_scale <= 65536, vocab <= 2^20 and layers <= 4096");
   int dev = 0, major = 0;
   MA_M_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
   MA_M_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev), "device attribute");

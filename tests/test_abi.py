@@ -189,3 +189,31 @@ def test_host_pipeline_without_gpu_fails_cleanly(cuda_lib):
     rc = cuda_lib.ma_host_pipeline_create(ctypes.byref(p), 8, ctypes.byref(out))
     assert rc in (4, 7), _err(cuda_lib)
     assert out.value is None
+
+
+def test_model_create_validates_its_configuration():
+    """ma_model_create rejects empty, inconsistent and oversized
+    configurations before it touches a device, and leaves *model NULL."""
+    import torch
+    from metalllm_b200 import train as T
+    lib = T._bind()
+    h = ctypes.c_void_p(ALIGNED)
+
+    def create(**kw):
+        c = dict(B=2, T=64, E=128, NH=2, layers=1, mlp_scale=2, vocab=128, lr=0.003, seed=0)
+        c.update(kw)
+        cfg = T.MaModelConfig(c["B"], c["T"], c["E"], c["NH"], c["layers"], c["mlp_scale"], c["vocab"], c["lr"],
+                              c["seed"])
+        return lib.ma_model_create(ctypes.byref(cfg), ctypes.byref(h))
+
+    assert lib.ma_model_create(None, ctypes.byref(h)) == 2
+    assert create(B=0) == 1 and h.value is None
+    assert create(NH=3) == 1                # head size 128/3
+    assert create(E=96, NH=1) == 1          # head size 96
+    assert create(vocab=100) == 1           # vocabulary not a multiple of 64
+    assert create(E=32768, NH=256) == 8     # E above 16384
+    assert create(mlp_scale=1024) == 8      # MLP width above 65536
+    assert create(vocab=1 << 21) == 8       # vocabulary above 2^20
+    if not torch.cuda.is_available():
+        assert create() in (4, 7), lib.ma_model_last_error()
+        assert h.value is None
