@@ -193,7 +193,8 @@ MA_API int ma_computeGradDw(const ma_bf16* x, const float* dQ, const ma_bf16* dK
  * the weights from `seed` with the reference's distributions
  * (main.cpp:1594-1620).  forward/backward/step only enqueue work on `stream`.
  * No counterpart in the attention-only reference ABI: it replaces model.h's
- * orchestration. */
+ * orchestration.  Limits (else MA_ERR_LIMIT): B*T < 2^30, E <= 16384,
+ * E*mlp_scale <= 65536, vocab <= 2^20, layers <= 4096. */
 typedef struct MaModelConfig {
   uint32_t B;          /* sequences per step */
   uint32_t T;          /* sequence length (BLOCK_SIZE) */
