@@ -68,7 +68,10 @@ int device_status_word(uint32_t** out) {
     e = cudaMalloc(&p, sizeof(uint32_t));
     if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(status word)");
     e = cudaMemset(p, 0, sizeof(uint32_t));
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(status word)");
+    if (e != cudaSuccess) {
+      cudaFree(p);
+      return cuda_fail(e, "cudaMemset(status word)");
+    }
     g_status[dev] = static_cast<uint32_t*>(p);
   }
   *out = g_status[dev];
