@@ -277,10 +277,12 @@ MA_API uint64_t ma_kernel_launch_count(void);
  * PCIe, so a pipeline splits the batch into chunks of `chunk_B` sequences
  * and overlaps, on three internal streams, the host->device copy of chunk
  * c+1, the kernels of chunk c and the device->host copy of chunk c-1 (the
- * copy engines of the two directions run concurrently).  Results equal, bit
- * for bit, ma_flashAttentionForward (forward only) or
- * ma_flashAttentionForwardComputeD then ma_flashAttentionBackward (forward
- * and backward) on device buffers: every (batch, head) is independent.
+ * copy engines of the two directions run concurrently).  Results equal
+ * ma_flashAttentionForward (forward only) or ma_flashAttentionForwardComputeD
+ * then ma_flashAttentionBackward (forward and backward) on device buffers,
+ * since every (batch, head) is independent: bit for bit, except dQ, whose
+ * fp32 partial sums from different key tiles are added in no fixed order
+ * (as by the reference's atomics, attention.metal:292-296).
  *   - Host pointers should be page-locked (cudaHostAlloc / cudaHostRegister);
  *     pageable memory gives the same results without the overlap.
  *   - A pipeline belongs to the device current at create and owns three

@@ -315,7 +315,8 @@ class HostPipeline:
     split into chunks of `chunk_B` sequences whose host->device copies,
     kernels and device->host copies overlap on three internal streams.  The
     reference needs no such step (its Metal buffers are shared CPU/GPU memory,
-    model.h:236-253); the results equal the device entry points bit for bit.
+    model.h:236-253); O, l, dK and dV equal the device entry points bit for
+    bit, and dQ to fp32 rounding (its reduce-adds arrive in no fixed order).
     Host tensors should be pinned (`tensor.pin_memory()`) for the overlap."""
 
     def __init__(self, T: int, NH: int, D: int, chunk_B: int, device=None):

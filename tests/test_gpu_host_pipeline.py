@@ -1,9 +1,10 @@
 """Host-resident batches through ma_host_pipeline_*: the chunked copy /
 compute / copy-back pipeline gives the same bits as the device entry points
-(forward with computeD, then backward)
-(every (batch, head) is independent, so chunking the batch changes nothing),
-for a ragged last chunk, both head sizes, pinned and pageable host memory,
-and repeated calls on one pipeline."""
+(forward with computeD, then backward) for O, l, dK and dV, and dQ to fp32
+rounding (its bulk reduce-adds from different key tiles arrive in no fixed
+order), since every (batch, head) is independent and chunking the batch
+changes nothing; for a ragged last chunk, both head sizes, pinned and
+pageable host memory, and repeated calls on one pipeline."""
 import numpy as np
 import pytest
 
@@ -31,6 +32,14 @@ def _host(B, T, H, D, seed, pin):
     return [t.pin_memory() if pin else t for t in ts]
 
 
+def _same(name, g, r):
+    if name == "dQ":
+        ref = r.double()
+        assert (g.double() - ref).abs().max().item() <= 1e-5 * max(1.0, ref.abs().max().item()), name
+    else:
+        assert torch.equal(g, r), name
+
+
 def _device_reference(A, q, k, v, dO, B, T, H, D):
     p = A.make_params(T, H, D)
     dq, dk, dv, ddo = (t.cuda() for t in (q, k, v, dO))
@@ -52,7 +61,7 @@ def test_host_pipeline_matches_device_entry_points(A, B, T, H, D, chunk, pin):
         stream.synchronize()
         assert A.device_status() == 0
         for name, g, r in zip(("out", "l", "dQ", "dK", "dV"), got, ref):
-            assert torch.equal(g, r), name
+            _same(name, g, r)
     out, l = pl.forward(q, k, v, B, stream=stream)
     stream.synchronize()
     assert torch.equal(out, ref[0]) and torch.equal(l, ref[1])
@@ -66,8 +75,8 @@ def test_host_pipeline_smaller_batch_than_chunk_and_errors(A):
     pl = A.HostPipeline(T, H, D, 8)
     got = pl.forward_backward(q, k, v, dO, B)
     torch.cuda.synchronize()
-    for g, r in zip(got, ref):
-        assert torch.equal(g, r)
+    for name, g, r in zip(("out", "l", "dQ", "dK", "dV"), got, ref):
+        _same(name, g, r)
     with pytest.raises(ValueError):
         pl.forward(q.cuda(), k, v, B)
     with pytest.raises(A.MetalAttnError, match="MA_ERR_SHAPE"):
