@@ -43,6 +43,11 @@ def _check(t: torch.Tensor, name: str, dtype: torch.dtype, shape: tuple) -> None
         raise TypeError(f"{name} must be a torch.Tensor")
     if not t.is_cuda:
         raise ValueError(f"{name} must be a CUDA tensor (no CPU path exists)")
+    cur = torch.cuda.current_device()
+    if t.device.index != cur:
+        # the entry points launch on the current device; another device's
+        # pointer would be dereferenced from there
+        raise ValueError(f"{name} is on {t.device} but the current CUDA device is cuda:{cur}")
     if t.dtype != dtype:
         raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
     if tuple(t.shape) != tuple(shape) and t.numel() != _numel(shape):

@@ -51,6 +51,7 @@ struct Layer {
 
 struct ma_model {
   MaModelConfig cfg{};
+  int device = -1;  // the device current at create; every buffer lives there
   int R = 0, T = 0, E = 0, H = 0, V = 0, NH = 0, D = 0, L = 0, Bt = 0;
   std::vector<void*> allocs;
   std::vector<ma::Param> params;
@@ -126,6 +127,17 @@ int merr(int code, const std::string& msg) {
                                    cudaGetErrorString(e_) + ")");                              \
   } while (0)
 
+// Work for a model must be enqueued with its own device current: from another
+// device the kernels would run there on this device's pointers.
+int check_device(const ma_model* m) {
+  int dev = -1;
+  MA_M_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev != m->device)
+    return merr(MA_ERR_NO_DEVICE, "the model lives on device " + std::to_string(m->device) +
+                                      ", the current device is " + std::to_string(dev));
+  return MA_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -153,6 +165,7 @@ int ma_model_create(const MaModelConfig* c, ma_model** out) {
 
   ma_model* m = new ma_model();
   m->cfg = *c;
+  m->device = dev;
   m->Bt = (int)c->B;
   m->T = (int)c->T;
   m->E = (int)c->E;
@@ -311,6 +324,7 @@ int ma_model_destroy(ma_model* m) {
 int ma_model_forward(ma_model* m, const int32_t* tokens, const int32_t* targets, ma_stream_t stream) {
   using namespace ma;
   if (!m || !tokens || !targets) return merr(MA_ERR_NULL, "NULL argument");
+  if (int rc = check_device(m)) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   m->tokens = tokens;
   m->targets = targets;
@@ -355,6 +369,7 @@ static cudaError_t wgrad(ma_model* m, const __nv_bfloat16* X, const __nv_bfloat1
 int ma_model_backward(ma_model* m, ma_stream_t stream) {
   using namespace ma;
   if (!m || !m->tokens) return merr(MA_ERR_NULL, "backward before forward");
+  if (int rc = check_device(m)) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int R = m->R, E = m->E, H = m->H, V = m->V;
   AttnShape s{m->T, E, m->D, m->NH, m->Bt, 0, m->Bt * m->NH};
@@ -405,6 +420,7 @@ int ma_model_backward(ma_model* m, ma_stream_t stream) {
 int ma_model_step(ma_model* m, ma_stream_t stream) {
   using namespace ma;
   if (!m) return merr(MA_ERR_NULL, "NULL model");
+  if (int rc = check_device(m)) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   m->step_count += 1.0f;
   const float t = m->step_count;
@@ -490,6 +506,7 @@ int ma_model_read(ma_model* m, const char* name, void* host, uint64_t bytes) {
   int rc = ma_model_tensor(m, name, &p, &n);
   if (rc) return rc;
   if (!host || bytes != n) return merr(MA_ERR_RANGE, std::string("size mismatch for ") + name);
+  if ((rc = check_device(m))) return rc;
   MA_M_CUDA(cudaMemcpy(host, p, n, cudaMemcpyDeviceToHost), "cudaMemcpy");
   return MA_OK;
 }
@@ -500,6 +517,7 @@ int ma_model_write(ma_model* m, const char* name, const void* host, uint64_t byt
   int rc = ma_model_tensor(m, name, &p, &n);
   if (rc) return rc;
   if (!host || bytes != n) return merr(MA_ERR_RANGE, std::string("size mismatch for ") + name);
+  if ((rc = check_device(m))) return rc;
   MA_M_CUDA(cudaMemcpy(p, host, n, cudaMemcpyHostToDevice), "cudaMemcpy");
   for (const auto& q : m->params) {
     if (q.name == name) {
@@ -523,6 +541,7 @@ const char* ma_model_param_name(ma_model* m, uint32_t i) {
 
 int ma_model_status(ma_model* m, uint32_t* status) {
   if (!m || !status) return merr(MA_ERR_NULL, "NULL argument");
+  if (int rc = check_device(m)) return rc;
   MA_M_CUDA(cudaMemcpy(status, m->status, 4, cudaMemcpyDeviceToHost), "cudaMemcpy");
   return MA_OK;
 }

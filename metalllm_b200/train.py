@@ -98,6 +98,8 @@ class TrainingModel:
             if t.dtype != torch.int32 or not t.is_cuda or not t.is_contiguous() or \
                     t.numel() != self.cfg.B * self.cfg.T:
                 raise ValueError(f"{n} must be a contiguous int32 CUDA tensor of B*T elements")
+            if t.device.index != torch.cuda.current_device():
+                raise ValueError(f"{n} is on {t.device}, not on the current CUDA device")
         self._tokens, self._targets = tokens, targets  # kept alive until backward
         _check(_bind().ma_model_forward(self._h, _P(tokens.data_ptr()), _P(targets.data_ptr()),
                                         self._stream(stream)), "ma_model_forward")
