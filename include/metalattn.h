@@ -192,6 +192,8 @@ MA_API int ma_computeGradDw(const ma_bf16* x, const float* dQ, const ma_bf16* dK
  * allocates and owns all its buffers at creation (cudaMalloc) and initialises
  * the weights from `seed` with the reference's distributions
  * (main.cpp:1594-1620).  forward/backward/step only enqueue work on `stream`.
+ * The model belongs to the device current at create; its other calls return
+ * MA_ERR_NO_DEVICE while another device is current.
  * No counterpart in the attention-only reference ABI: it replaces model.h's
  * orchestration.  Limits (else MA_ERR_LIMIT): B*T < 2^30, E <= 16384,
  * E*mlp_scale <= 65536, vocab <= 2^20, layers <= 4096. */
