@@ -34,6 +34,9 @@ from metalllm_b200.inputs import CONFIGS, attention_inputs, causal_flops  # noqa
 from metalllm_b200.shards import plan as plan_shards  # noqa: E402
 
 METRIC = "causal bf16 FlashAttn fwd+bwd TFLOP/s per GPU, % tensor peak, at 1/2/4/8 GPUs"
+# `value` is the whole job's rate (the sum over the N GPUs); per_gpu_tflops
+# holds the per-GPU figure the metric names
+UNIT = "TFLOP/s (sum over all GPUs)"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -113,6 +116,179 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(rows)}
 
 
+# ----------------------------------------------------------- shared helpers
+def arm_config(cfg, world, mode, batch=0):
+    """The `config` object of the bench line, identical for the GPU arm and
+    the reference arm (same workload, same split)."""
+    c = CONFIGS[cfg]
+    B, T, H, D = c["B"], c["T"], c["H"], c["D"]
+    if batch:
+        B = batch
+    if mode == "weak":
+        Bl, nshards, global_shards, global_batch = B, B * H, B * H * world, B * world
+    else:
+        sp = plan_shards(B, H, world, 0)
+        Bl, nshards, global_shards, global_batch = sp.local_batch, sp.shards, B * H, B
+    in_bytes = 4 * Bl * T * H * D * 2
+    return {
+        "workload": workload_desc(cfg),
+        "B_per_gpu": Bl, "T": T, "H": H, "d": D, "causal": True,
+        "global_batch": global_batch,
+        "parallelism": f"(batch x head) shards, {nshards} on rank 0 of {global_shards}, no collective",
+        "l2": ("inputs larger than L2 (Q,K,V,dO = %.1f MB per step per GPU > 126 MB)" % (in_bytes / 1e6))
+              if in_bytes > 126e6 else "L2 flushed (256 MB write) before every step, outside the timed steps",
+        "flops_convention": "fwd 2*B*H*T^2*d + bwd 5*B*H*T^2*d (causal T^2/2 pairs)",
+    }
+
+
+def host_inputs(cfg, seed, b_begin, nb):
+    """Q, K, V, dO bits of batch rows [b_begin, b_begin + nb) of a config,
+    shape [nb, T, H*D] (any row range regenerates independently)."""
+    from metalllm_b200.inputs import STREAM_DO, STREAM_K, STREAM_Q, STREAM_V, normal_bf16
+    c = CONFIGS[cfg]
+    T, H, D = c["T"], c["H"], c["D"]
+    n = nb * T * H * D
+    return {name: normal_bf16(n, seed, st, sc, offset=b_begin * T * H * D).reshape(nb, T, H * D)
+            for name, st, sc in (("q", STREAM_Q, c["qkv_scale"]), ("k", STREAM_K, c["qkv_scale"]),
+                                 ("v", STREAM_V, c["qkv_scale"]), ("do", STREAM_DO, c["do_scale"]))}
+
+
+class Ctx:
+    """The rank's device, stream and the collective helpers of the run."""
+
+    def __init__(self, torch, dist, world, rank, local):
+        self.torch, self.dist = torch, dist
+        self.world, self.rank, self.local = world, rank, local
+        self.dev = torch.device("cuda", local)
+        self.stream = torch.cuda.Stream(device=self.dev)
+
+    def barrier(self):
+        self.torch.cuda.synchronize(self.dev)
+        if self.world > 1:
+            self.dist.barrier(device_ids=[self.local])
+        self.torch.cuda.synchronize(self.dev)
+
+    def max_over_ranks(self, x: float) -> float:
+        if self.world == 1:
+            return x
+        t = self.torch.tensor([x], dtype=self.torch.float64, device=self.dev)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+
+def time_split(ctx, A, cfg, steps, warmup, seed, peak):
+    """A config's B*H (batch, head) shards split evenly over the ranks
+    (shards.plan): every rank runs forward (computeD fused) + backward over
+    its shards; time = max over ranks of the device time of `steps` steps.
+    Returns the aggregate (whole-config) and per-GPU TFLOP/s."""
+    torch = ctx.torch
+    c = CONFIGS[cfg]
+    B, T, H, D = c["B"], c["T"], c["H"], c["D"]
+    sp = plan_shards(B, H, ctx.world, ctx.rank)
+    Bl = sp.local_batch
+    shard = (sp.local_bh_begin, sp.local_bh_end)
+    x = host_inputs(cfg, seed, sp.b_begin, Bl)
+    up = lambda a: torch.from_numpy(a.view(np.int16)).view(torch.bfloat16).to(ctx.dev)
+    q, k, v, do = up(x["q"]), up(x["k"]), up(x["v"]), up(x["do"])
+    del x
+    act = (Bl, T, H * D)
+    out = torch.empty(act, dtype=torch.bfloat16, device=ctx.dev)
+    l = torch.empty((Bl, T, H), dtype=torch.float32, device=ctx.dev)
+    Dv = torch.empty((Bl, T, H), dtype=torch.bfloat16, device=ctx.dev)
+    dQ = torch.empty(act, dtype=torch.float32, device=ctx.dev)
+    dK = torch.empty(act, dtype=torch.bfloat16, device=ctx.dev)
+    dV = torch.empty(act, dtype=torch.bfloat16, device=ctx.dev)
+    p = A.make_params(T, H, D)
+    st = ctx.stream
+    flush = None
+    if 4 * q.numel() * 2 <= 126e6:  # inputs fit in L2: flush before every step
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=ctx.dev)
+
+    def step(ev=None):
+        if ev is not None:
+            ev[0].record(st)
+        A.flashAttentionForwardComputeD(q, k, v, do, p, Bl, out=out, l=l, D=Dv, shard=shard, stream=st)
+        if ev is not None:
+            ev[1].record(st)
+        A.flashAttentionBackward(do, Dv, l, q, k, v, p, Bl, dQ=dQ, dK=dK, dV=dV, shard=shard, stream=st)
+        if ev is not None:
+            ev[2].record(st)
+
+    for _ in range(warmup):
+        step()
+    ctx.barrier()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ctx.barrier()
+    start.record(st)
+    for i in range(steps):
+        if flush is not None:
+            with torch.cuda.stream(st):
+                flush.fill_(i & 0xFF)
+        step(evs[i])
+    stop.record(st)
+    ctx.barrier()
+    if flush is None:
+        elapsed = start.elapsed_time(stop)
+    else:
+        elapsed = sum(e[0].elapsed_time(e[2]) for e in evs)
+    fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    bwd_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+    if A.device_status(st) != 0:
+        raise RuntimeError(f"a kernel reported a timeout while timing {cfg}")
+    elapsed = ctx.max_over_ranks(elapsed)
+    fwd_ms = ctx.max_over_ranks(fwd_ms)
+    bwd_ms = ctx.max_over_ranks(bwd_ms)
+    fwd1, bwd1 = causal_flops(1, T, 1, D)
+    total = (fwd1 + bwd1) * B * H
+    agg = total * steps / (elapsed * 1e-3) / 1e12
+    per_gpu = agg / ctx.world
+    return {
+        "workload": workload_desc(cfg), "n_gpus": ctx.world, "shards_per_gpu": sp.shards,
+        "steps": steps, "ms_per_step": round(elapsed / steps, 4),
+        "aggregate_tflops": round(agg, 2), "per_gpu_tflops": round(per_gpu, 2),
+        "frac": round(per_gpu / peak, 4),
+        "fwd_ms": round(fwd_ms, 4), "bwd_ms": round(bwd_ms, 4),
+        "fwd_tflops": round(fwd1 * sp.shards / (fwd_ms * 1e-3) / 1e12, 2),
+        "bwd_tflops": round(bwd1 * sp.shards / (bwd_ms * 1e-3) / 1e12, 2),
+        "l2": "flushed before every step" if flush is not None else "inputs larger than L2",
+    }
+
+
+def copy_bandwidth(ctx, nbytes=256 << 20, reps=3):
+    """Pinned host<->device copy rates (GB/s) on this box: each direction
+    alone, and both at once on two streams (as the host pipeline runs them)."""
+    torch = ctx.torch
+    h_src = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    h_dst = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    d_dst = torch.empty(nbytes, dtype=torch.uint8, device=ctx.dev)
+    d_src = torch.empty(nbytes, dtype=torch.uint8, device=ctx.dev)
+    s1, s2 = torch.cuda.Stream(device=ctx.dev), torch.cuda.Stream(device=ctx.dev)
+
+    def timed(pairs):
+        best = [float("inf")] * len(pairs)
+        for _ in range(reps):
+            torch.cuda.synchronize(ctx.dev)
+            evs = []
+            for (dst, src), s in zip(pairs, (s1, s2)):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(s)
+                with torch.cuda.stream(s):
+                    dst.copy_(src, non_blocking=True)
+                e1.record(s)
+                evs.append((e0, e1))
+            torch.cuda.synchronize(ctx.dev)
+            for i, (e0, e1) in enumerate(evs):
+                best[i] = min(best[i], e0.elapsed_time(e1))
+        return [nbytes / (ms * 1e-3) / 1e9 for ms in best]
+
+    h2d = timed([(d_dst, h_src)])[0]
+    d2h = timed([(h_dst, d_src)])[0]
+    both = timed([(d_dst, h_src), (h_dst, d_src)])
+    return {"h2d_gbs": round(h2d, 2), "d2h_gbs": round(d2h, 2), "concurrent_h2d_gbs": round(both[0], 2),
+            "concurrent_d2h_gbs": round(both[1], 2), "bytes_per_copy": nbytes}
+
+
 # ------------------------------------------------------------ GPU arm
 def run_gpu(args):
     import torch
@@ -133,6 +309,7 @@ def run_gpu(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
     lib = _lib.load()
+    ctx = Ctx(torch, dist, world, rank, local)
 
     c = CONFIGS[args.config]
     B, T, H, D = c["B"], c["T"], c["H"], c["D"]
@@ -173,11 +350,10 @@ def run_gpu(args):
     dQ = torch.empty(act, dtype=torch.float32, device=dev)
     dK = torch.empty(act, dtype=torch.bfloat16, device=dev)
     dV = torch.empty(act, dtype=torch.bfloat16, device=dev)
-    stream = torch.cuda.Stream(device=dev)
+    stream = ctx.stream
 
     fwd1, bwd1 = causal_flops(1, T, 1, D)           # per (batch, head) shard
     fwd_flops, bwd_flops = fwd1 * nshards, bwd1 * nshards
-    step_flops = fwd_flops + bwd_flops
 
     # dO is an input of this attention-only step, so computeD rides in the
     # forward's epilogue (ma_flashAttentionForwardComputeD; at d=128 it is
@@ -194,18 +370,7 @@ def run_gpu(args):
         if ev is not None:
             ev[3].record(stream)
 
-    def barrier():
-        torch.cuda.synchronize(dev)
-        if world > 1:
-            dist.barrier(device_ids=[local])
-        torch.cuda.synchronize(dev)
-
-    def max_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+    barrier, max_over_ranks = ctx.barrier, ctx.max_over_ranks
 
     # ---- warm-up
     for _ in range(args.warmup):
@@ -287,6 +452,7 @@ def run_gpu(args):
 
     e2e_steps = max(3, min(args.steps, 10))
     e2e_value = None
+    e2e_roof = None
     if not args.no_e2e:
         for _ in range(2):
             e2e_step()
@@ -300,6 +466,19 @@ def run_gpu(args):
         barrier()
         e2e_ms = max_over_ranks(e0.elapsed_time(e1))
         e2e_value = round((fwd1 + bwd1) * global_shards * e2e_steps / (e2e_ms * 1e-3) / 1e12, 3)
+        # the copy-bound ceiling of the same step: its bytes at the box's
+        # measured pinned copy rates (both directions at once, as the
+        # pipeline runs them), or the device step if that is longer
+        bw = copy_bandwidth(ctx)
+        h2d_ms = h2d / (bw["concurrent_h2d_gbs"] * 1e9) * 1e3
+        d2h_ms = d2h / (bw["concurrent_d2h_gbs"] * 1e9) * 1e3
+        bound_ms = max(h2d_ms, d2h_ms, ms_per_step)
+        e2e_step_ms = e2e_ms / e2e_steps
+        e2e_roof = dict(bw, h2d_ms=round(h2d_ms, 3), d2h_ms=round(d2h_ms, 3),
+                        device_step_ms=round(ms_per_step, 4), bound_ms=round(bound_ms, 3),
+                        e2e_ms_per_step=round(e2e_step_ms, 3), frac=round(bound_ms / e2e_step_ms, 4),
+                        note="bound = max(H2D bytes / concurrent H2D rate, D2H bytes / concurrent D2H rate, "
+                             "device step); frac = bound / measured e2e step")
 
     # ---- roofline of the dominant kernel (backward: 5/7 of the FLOPs)
     peaks, peak_src = load_peaks()
@@ -359,6 +538,36 @@ def run_gpu(args):
         "flashAttentionBackward": {"ms": round(bwd_avg, 4), "tflops": round(bwd_tflops, 2),
                                    "frac": round(bwd_tflops / peak, 4)},
     }
+    # free the headline's buffers before the other configs
+    del q, k, v, do, out, l, Dv, dQ, dK, dV, flush
+    if pipeline is not None:
+        pipeline.close()
+    torch.cuda.empty_cache()
+
+    # ---- the north_star split: configs 3 and 4's 128 (batch, head) shards
+    # over the N GPUs of this run, and, on one GPU, the other BASELINE configs
+    extra_steps = max(3, min(args.steps, 10))
+    extras_sampler = ClockSampler(bus)
+    extras = {}
+    configs = None
+    if not args.no_extras:
+        extras_sampler.start()
+        for cfg in ("c3", "c4"):
+            extras[f"strong_{cfg}"] = time_split(ctx, A, cfg, extra_steps, 3, args.seed, peak)
+            torch.cuda.empty_cache()
+        if world == 1:
+            configs = {"c1": time_split(ctx, A, "c1", extra_steps, 3, args.seed, peak),
+                       "c2": {"workload": workload_desc("c2"), "per_gpu_tflops": round(value, 2),
+                              "frac": round(value / peak, 4), "ms_per_step": round(ms_per_step, 4),
+                              "note": "the headline of this line"},
+                       "c3": extras["strong_c3"], "c4": extras["strong_c4"]}
+            torch.cuda.empty_cache()
+            configs["c5"] = measure_train(extra_steps, 3, args.seed)
+        ex_clocks = extras_sampler.stop()
+        for v_ in extras.values():
+            v_["clocks"] = ex_clocks
+        if configs is not None:
+            configs["clocks"] = ex_clocks
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -372,7 +581,7 @@ def run_gpu(args):
     line = {
         "metric": METRIC,
         "value": round(value, 3),
-        "unit": "TFLOP/s",
+        "unit": UNIT,
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
@@ -382,32 +591,28 @@ def run_gpu(args):
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic: Q,K,V,dO i.i.d. normal (splitmix64 + Box-Muller, seed %d), bf16" % args.seed,
-        "config": {
-            "workload": workload_desc(args.config),
-            "B_per_gpu": Bl, "T": T, "H": H, "d": D, "causal": True,
-            "global_batch": B * world if args.mode == "weak" else B,
-            "parallelism": f"(batch x head) shards, {nshards} on rank 0 of {global_shards}, no collective",
-            "l2": ("inputs larger than L2 (Q,K,V,dO = %.1f MB per step per GPU > 126 MB)" % (4 * n_local * 2 / 1e6))
-                  if flush is None else "L2 flushed (256 MB write) before every step, outside the timed steps",
-            "flops_convention": "fwd 2*B*H*T^2*d + bwd 5*B*H*T^2*d (causal T^2/2 pairs)",
-        },
+        "config": arm_config(args.config, world, args.mode, args.batch),
         "per_gpu_tflops": round(value / world, 3),
         "frac_of_peak": round(value / world / peak, 4),
         # the datasheet's dense bf16 figure (2.25 PFLOP/s per B200), for comparison
         # with the north_star target, next to the measured-peak fraction above
         "frac_of_datasheet_peak": round(value / world / DATASHEET_BF16_TFLOPS, 4),
         "clocks": clocks,
-        "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
                 "note": ("pinned host Q,K,V,dO -> device, fwd+computeD+bwd, O,l,dQ,dK,dV -> host; "
                          + (f"ma_attentionForwardBackward_host, chunks of {pipeline.chunk_B} sequences, "
                             "copies in / kernels / copies out overlapped" if pipeline is not None
-                            else "whole-tensor copies around the shard kernels on one stream"))},
+                            else "whole-tensor copies around the shard kernels on one stream")),
+                "copy_roofline": e2e_roof},
         "gpu_launches": int(launches),
         "roofline": roofline,
         "kernels": extra_kernels,
         "cpu_baseline": cpu,
     }
+    line.update(extras)
+    if configs is not None:
+        line["configs"] = configs
     print(json.dumps(line), flush=True)
 
 
@@ -455,7 +660,7 @@ def cpu_baseline(cfg, seed, budget_s=15.0, nthreads=0):
     cpu_step(o, x, nthreads)
     t2 = time.perf_counter() - t0
     val = per_shard * n2 / t2 / 1e12
-    return {"value": round(val, 6), "unit": "TFLOP/s", "cores": nthreads, "kind": "port",
+    return {"value": round(val, 6), "unit": UNIT, "cores": nthreads, "kind": "port",
             "sample": f"{n2} of {c['B'] * c['H']} (batch, head) shards of {cfg} "
                       f"(T={T}, d={D}), fwd+computeD+bwd, {t2:.2f} s"}
 
@@ -492,16 +697,15 @@ def run_reference(args):
               f"(T={T}, d={D}), fwd+computeD+bwd")
     line = {
         "impl": "reference",
-        "metric": METRIC, "value": round(val, 6), "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "metric": METRIC, "value": round(val, 6), "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(total / args.steps * 1e3, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16 in/out, fp32 math",
+        "scaling": args.mode, "vs_baseline": None, "dtype": "bf16 in/out, fp32 math",
         "data": "synthetic (same generator and seed as the GPU arm)",
-        "config": {"workload": workload_desc(args.config), "B_per_gpu": c["B"], "T": T, "H": c["H"],
-                   "d": D, "causal": True},
-        "cpu_baseline": {"value": round(val, 6), "unit": "TFLOP/s", "cores": nthreads,
+        "config": arm_config(args.config, args.gpus, args.mode, args.batch),
+        "cpu_baseline": {"value": round(val, 6), "unit": UNIT, "cores": nthreads,
                          "kind": "port", "sample": sample},
-        "e2e": {"value": round(val, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+        "e2e": {"value": round(val, 6), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
         "note": ("The reference runs only on Apple Metal (unavailable on this box); this arm "
                  "times its scalar multithreaded C++ restatement (oracle/attn_oracle.cpp)."),
@@ -510,28 +714,24 @@ def run_reference(args):
 
 
 # ------------------------------------------------------- config-5 training step
-def run_train(args):
+def measure_train(steps, warmup, seed):
     """Config 5 (BASELINE): one metalLLM training iteration -- forward,
     backward and Adam over B=64 sequences of T=256, E=384, 6 heads of 64,
     6 layers, MLP x2, vocabulary 128 -- in ms/iter, eager (one launch per
     kernel) and replayed from a CUDA graph, plus the share of the attention
-    kernels measured standalone on the same shapes."""
-    import numpy as np
+    kernels measured standalone on the same shapes.  Runs on the current
+    device; returns a dict."""
     import torch
-    rank = env_int("RANK", 0)
-    if rank != 0:  # a single-GPU workload: replicas only, rank 0 reports
-        return
-    torch.cuda.set_device(env_int("LOCAL_RANK", 0))
     from metalllm_b200 import attention as A
     from metalllm_b200 import train as T
     from metalllm_b200._lib import load
     B, Tn, E, NH, L, S, V = 64, 256, 384, 6, 6, 2, 128
-    model = T.TrainingModel(B, Tn, E, NH, L, S, V, lr=0.003, seed=args.seed)
-    rng = np.random.default_rng(args.seed)
+    model = T.TrainingModel(B, Tn, E, NH, L, S, V, lr=0.003, seed=seed)
+    rng = np.random.default_rng(seed)
     tok = torch.from_numpy(rng.integers(0, V, (B, Tn)).astype(np.int32)).cuda()
     tgt = torch.from_numpy(rng.integers(0, V, (B, Tn)).astype(np.int32)).cuda()
     lib = load()
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         model.train_step(tok, tgt)
     torch.cuda.synchronize()
     loss0 = model.loss()
@@ -546,15 +746,11 @@ def run_train(args):
         torch.cuda.synchronize()
         return e0.elapsed_time(e1) / k
 
-    props = torch.cuda.get_device_properties(torch.cuda.current_device())
-    sampler = ClockSampler(f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0")
     n0 = lib.ma_kernel_launch_count()
-    sampler.start()
     torch.cuda.nvtx.range_push("eager")  # lets a profiler select the timed eager steps
-    eager_ms = timed(lambda: model.train_step(tok, tgt), args.steps)
+    eager_ms = timed(lambda: model.train_step(tok, tgt), steps)
     torch.cuda.nvtx.range_pop()
-    clocks = sampler.stop()
-    launches = (lib.ma_kernel_launch_count() - n0) // args.steps
+    launches = (lib.ma_kernel_launch_count() - n0) // steps
     loss1 = model.loss()
     graph = {}
     try:
@@ -566,13 +762,18 @@ def run_train(args):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
             model.train_step(tok, tgt)
-        for _ in range(args.warmup):
+        for _ in range(warmup):
             g.replay()
-        graph = {"ms_per_iter": round(timed(g.replay, args.steps), 4),
+        graph = {"ms_per_iter": round(timed(g.replay, steps), 4),
                  "note": "whole step captured once and replayed (the Adam bias correction of the "
                          "captured step is reused)"}
+        del g
     except Exception as e:  # capture unsupported by something in the step
         graph = {"error": str(e)[:200]}
+    status = model.status()
+    model.close()
+    if status != 0:
+        raise RuntimeError("a kernel of the training step reported a timeout")
     # attention share: the attention kernels of one layer, standalone, x layers
     p = A.make_params(Tn, NH, E // NH)
     mk = lambda: torch.randn(B, Tn, E, device="cuda").to(torch.bfloat16)
@@ -592,33 +793,51 @@ def run_train(args):
         core(); rest()
     core_ms = timed(core, 20) * L
     block_ms = core_ms + timed(rest, 20) * L
-    step_ms = eager_ms
     flops = L * 7.0 * B * NH * Tn * Tn * (E // NH)   # causal attention core, fwd + bwd
-    line = {
-        "metric": "config-5 training step ms/iter (forward + backward + Adam), attention share",
-        "value": round(eager_ms, 4), "unit": "ms/iter", "n_gpus": 1, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(eager_ms, 4), "higher_is_better": False,
-        "scaling": "replicas only", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic: tokens and targets uniform in [0, 128), weights initialised as main.cpp",
-        "config": {"workload": "c5: 6-layer metalLLM training step", "B": B, "T": Tn, "E": E,
-                   "heads": NH, "d": E // NH, "layers": L, "mlp_scale": S, "vocab": V},
-        "graph": graph, "gpu_launches": int(launches),
+    return {
+        "workload": "c5: 6-layer metalLLM training step (forward + backward + Adam)",
+        "ms_per_iter": round(eager_ms, 4), "graph": graph, "gpu_launches_per_iter": int(launches),
+        "config": {"B": B, "T": Tn, "E": E, "heads": NH, "d": E // NH, "layers": L, "mlp_scale": S,
+                   "vocab": V},
         "attention_share": {
-            "core_ms": round(core_ms, 4), "core_share": round(core_ms / step_ms, 4),
+            "core_ms": round(core_ms, 4), "core_share": round(core_ms / eager_ms, 4),
             "core_tflops": round(flops / (core_ms * 1e-3) / 1e12, 2),
-            "block_ms": round(block_ms, 4), "block_share": round(block_ms / step_ms, 4),
+            "block_ms": round(block_ms, 4), "block_share": round(block_ms / eager_ms, 4),
             "note": "flashAttentionForward + computeD + flashAttentionBackward (core) and with "
                     "computeQKV, projForward/BackwarddW/dX, computeGradDx/Dw (block), timed "
                     "standalone on the step's shapes, times the 6 layers, over the eager step; "
                     "the block figure uses the public single-pass weight-gradient entry points, "
                     "slower than the model's split-K path, so it is an upper bound"},
         "loss": {"after_warmup": round(loss0, 4), "after_timed": round(loss1, 4)},
-        "clocks": clocks,
         "reference": "published: ~13 ms/iter for this model at B=1 on an M4 MacBook Air "
                      "(README.md:5,121); not comparable hardware",
     }
+
+
+def run_train(args):
+    """`--train`: config 5 alone, as its own JSON line (ms/iter, lower is better)."""
+    import torch
+    rank = env_int("RANK", 0)
+    if rank != 0:  # a single-GPU workload: replicas only, rank 0 reports
+        return
+    torch.cuda.set_device(env_int("LOCAL_RANK", 0))
+    props = torch.cuda.get_device_properties(torch.cuda.current_device())
+    sampler = ClockSampler(f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0")
+    sampler.start()
+    r = measure_train(args.steps, args.warmup, args.seed)
+    clocks = sampler.stop()
+    line = {
+        "metric": "config-5 training step ms/iter (forward + backward + Adam), attention share",
+        "value": r["ms_per_iter"], "unit": "ms/iter", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": r["ms_per_iter"], "higher_is_better": False,
+        "scaling": "replicas only", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: tokens and targets uniform in [0, 128), weights initialised as main.cpp",
+        "config": dict(workload="c5: 6-layer metalLLM training step", **r["config"]),
+        "graph": r["graph"], "gpu_launches": r["gpu_launches_per_iter"],
+        "attention_share": r["attention_share"], "loss": r["loss"], "clocks": clocks,
+        "reference": r["reference"],
+    }
     print(json.dumps(line), flush=True)
-    model.close()
 
 
 def main():
@@ -632,6 +851,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) leg")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the configs 1, 3, 4, 5 and the split of configs 3 and 4 over the GPUs")
     ap.add_argument("--e2e-chunks", type=int, default=8,
                     help="chunks the host-buffer pipeline splits the local batch into")
     ap.add_argument("--mode", default="weak", choices=["weak", "strong"],

@@ -249,8 +249,10 @@ MA_API const char* ma_model_last_error(void);
  *     stream capture.
  *   - All calls on a device share the scratch: calls that overlap on the GPU
  *     (other streams, other host threads) race and give wrong results.
- *   - A bounded wait that runs out in its kernels is recorded only in the
- *     scratch (cleared by the next call), not in ma_device_status.
+ *   - A bounded wait that runs out in its kernels sets a bit in a status
+ *     word inside the scratch; ma_device_status (which allocates nothing)
+ *     reads and clears it together with the other entry points' word, and
+ *     the bit stays set until that read.
  * No counterpart in the reference. */
 #define MA_NOALLOC_MAX_D_ENTRIES (1u << 21)
 MA_API int ma_flashAttentionBackward_noalloc(const ma_bf16* dZ, const ma_bf16* O, const float* l,
@@ -263,10 +265,33 @@ MA_API int ma_flashAttentionBackward_noalloc(const ma_bf16* dZ, const ma_bf16* O
  * Replaces the reference's printed command-buffer error (model.h:361-365). */
 MA_API const char* ma_last_error_string(void);
 
-/* Reads and clears the current device's kernel status word: 0 = no kernel
- * gave up; otherwise a bit mask of the kernels whose bounded waits ran out.
- * Synchronises `stream` first.  Returns MA_OK or an MA_ERR_* code. */
+/* Bits of the status word read by ma_device_status: the kernels whose bounded
+ * waits ran out. */
+#define MA_STATUS_FWD_TIMEOUT (1u << 0)  /* flashAttentionForward */
+#define MA_STATUS_BWD_TIMEOUT (1u << 1)  /* flashAttentionBackward */
+#define MA_STATUS_QKV_TIMEOUT (1u << 2)  /* computeQKV */
+#define MA_STATUS_GEMM_TIMEOUT (1u << 3) /* the GEMMs around attention */
+
+/* Reads and clears the current device's kernel status: 0 = no kernel gave
+ * up; otherwise a bit mask (MA_STATUS_*) of the kernels whose bounded waits
+ * ran out since the last read, by any entry point on this device, including
+ * ma_flashAttentionBackward_noalloc.  Synchronises `stream` first.  Allocates
+ * nothing.  Returns MA_OK or an MA_ERR_* code. */
 MA_API int ma_device_status(uint32_t* status, ma_stream_t stream);
+
+/* Test hook of the kernels' time-out path.  The next launch of each kernel
+ * named in `kernels` (MA_STATUS_FWD_TIMEOUT and/or MA_STATUS_BWD_TIMEOUT) lets
+ * one wait run out on purpose: once its first tensor-core products are in
+ * flight, its UMMA-issuing thread waits on an mbarrier that nothing arrives
+ * at, for `wait_ns` nanoseconds (1 .. 10^9).  The kernel then winds down as
+ * after a real time-out: every role stops at its next wait, the copies and
+ * products already in flight are waited for, TMEM is freed and the kernel's
+ * bit is set in the status word ma_device_status reads.  That launch's
+ * outputs are undefined; nothing faults or traps, and later launches are not
+ * affected.  A request not yet taken is replaced by the next call; kernels = 0
+ * cancels it.  Diagnostic; no counterpart in the reference, which only prints
+ * a failed command buffer's error (model.h:358-366). */
+MA_API int ma_debug_expire_next_wait(uint32_t kernels, uint32_t wait_ns);
 
 /* Number of kernels this library has launched in this process (all devices,
  * all threads), for accounting of launches in timed regions.  Diagnostic;

@@ -10,6 +10,11 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().parent / "libmetalattn.so"
 
 MA_OK = 0
+# bits of the status word read by ma_device_status (MA_STATUS_* in metalattn.h)
+STATUS_FWD_TIMEOUT = 1 << 0
+STATUS_BWD_TIMEOUT = 1 << 1
+STATUS_QKV_TIMEOUT = 1 << 2
+STATUS_GEMM_TIMEOUT = 1 << 3
 ERROR_NAMES = {
     1: "MA_ERR_SHAPE",
     2: "MA_ERR_NULL",
@@ -63,6 +68,7 @@ SIGNATURES = {
     "ma_flashAttentionForward_host": [_P, _P, _P, _P, _P, _P, _U32, _P],
     "ma_attentionForwardBackward_host": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _U32, _P],
     "ma_device_status": [ctypes.POINTER(ctypes.c_uint32), _P],
+    "ma_debug_expire_next_wait": [_U32, _U32],
     "ma_version": [],
 }
 

@@ -263,10 +263,20 @@ def flashAttentionBackward(dZ: torch.Tensor, d: torch.Tensor, l: torch.Tensor, q
 
 
 def device_status(stream: Optional[torch.cuda.Stream] = None) -> int:
-    """Reads and clears the device's kernel status word (0 = no bounded wait ran out)."""
+    """Reads and clears the device's kernel status (0 = no bounded wait ran
+    out; else a mask of the _lib.STATUS_* bits), for every entry point
+    including flashAttentionBackward_noalloc."""
     st = ctypes.c_uint32(0)
     _lib.call("ma_device_status", ctypes.byref(st), _stream(stream))
     return st.value
+
+
+def debug_expire_next_wait(kernels: int, wait_ns: int = 1_000_000) -> None:
+    """Test hook of the time-out path: the next launch of each kernel in
+    `kernels` (_lib.STATUS_FWD_TIMEOUT / _lib.STATUS_BWD_TIMEOUT) lets a wait
+    run out after `wait_ns` and winds down as after a real time-out (its bit
+    then shows in device_status).  kernels=0 cancels a pending request."""
+    _lib.call("ma_debug_expire_next_wait", int(kernels), int(wait_ns))
 
 
 class CudaAttention:

@@ -22,6 +22,19 @@ std::atomic<unsigned long long> g_launches{0};
 void ma::count_launches(unsigned n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
 namespace {
+// Pending ma_debug_expire_next_wait request: kernel bits and the wait in ns.
+std::mutex g_expire_mu;
+uint32_t g_expire_mask = 0, g_expire_ns = 0;
+}  // namespace
+
+uint32_t ma::take_expire_request(uint32_t kernel_bit) {
+  std::lock_guard<std::mutex> lock(g_expire_mu);
+  if (!(g_expire_mask & kernel_bit)) return 0;
+  g_expire_mask &= ~kernel_bit;
+  return g_expire_ns;
+}
+
+namespace {
 
 thread_local std::string g_last_error;
 
@@ -77,6 +90,11 @@ int device_status_word(uint32_t** out) {
   *out = g_status[dev];
   return MA_OK;
 }
+
+// Device address of the allocation-free entry point's status word on `dev`,
+// or nullptr while that entry point has not run there (defined with its
+// scratch array below).
+uint32_t* noalloc_status_word_if_set_up(int dev);
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
@@ -427,22 +445,49 @@ const char* ma_last_error_string(void) { return g_last_error.c_str(); }
 
 int ma_device_status(uint32_t* status, ma_stream_t stream) {
   if (!status) return fail(MA_ERR_NULL, "status pointer is NULL");
-  uint32_t* word = nullptr;
-  int rc = device_status_word(&word);
-  if (rc) return rc;
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(MA_ERR_NO_DEVICE, "device ordinal %d out of range", dev);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  cudaError_t e = cudaStreamSynchronize(st);
+  e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
-  uint32_t host = 0;
-  e = cudaMemcpy(&host, word, sizeof(uint32_t), cudaMemcpyDeviceToHost);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy(status word)");
-  e = cudaMemset(word, 0, sizeof(uint32_t));
-  if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(status word)");
-  *status = host;
+  // Two words may exist on this device: the one the allocating entry points
+  // use and the one in the allocation-free entry point's scratch.  Only words
+  // already set up are read, so this call allocates nothing.
+  uint32_t* words[2] = {nullptr, noalloc_status_word_if_set_up(dev)};
+  {
+    std::lock_guard<std::mutex> lock(g_status_mu);
+    words[0] = g_status[dev];
+  }
+  uint32_t all = 0;
+  for (uint32_t* word : words) {
+    if (!word) continue;
+    uint32_t host = 0;
+    e = cudaMemcpy(&host, word, sizeof(uint32_t), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy(status word)");
+    e = cudaMemset(word, 0, sizeof(uint32_t));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(status word)");
+    all |= host;
+  }
+  *status = all;
   return ok();
 }
 
 uint64_t ma_kernel_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int ma_debug_expire_next_wait(uint32_t kernels, uint32_t wait_ns) {
+  const uint32_t supported = MA_STATUS_FWD_TIMEOUT | MA_STATUS_BWD_TIMEOUT;
+  if (kernels & ~supported)
+    return fail(MA_ERR_RANGE, "ma_debug_expire_next_wait: kernel mask 0x%x names kernels without the hook "
+                "(supported: MA_STATUS_FWD_TIMEOUT | MA_STATUS_BWD_TIMEOUT)", kernels);
+  if (kernels && (wait_ns == 0 || wait_ns > 1000000000u))
+    return fail(MA_ERR_RANGE, "ma_debug_expire_next_wait: wait_ns=%u outside 1 .. 10^9", wait_ns);
+  std::lock_guard<std::mutex> lock(g_expire_mu);
+  g_expire_mask = kernels;
+  g_expire_ns = kernels ? wait_ns : 0;
+  return ok();
+}
 
 int ma_version(void) { return 100; }
 
@@ -496,6 +541,15 @@ int noalloc_scratch(void** out) {
   return MA_OK;
 }
 
+// The status word is the first word of the scratch.  It starts at zero (the
+// array is zero-initialised when the module loads), the kernels only set bits
+// in it, and ma_device_status reads and clears it, so a time-out stays
+// visible until it has been read, whatever calls come in between.
+uint32_t* noalloc_status_word_if_set_up(int dev) {
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  return static_cast<uint32_t*>(g_noalloc_base[dev]);
+}
+
 }  // namespace
 
 extern "C" int ma_flashAttentionBackward_noalloc(const ma_bf16* dZ, const ma_bf16* O,
@@ -528,11 +582,10 @@ extern "C" int ma_flashAttentionBackward_noalloc(const ma_bf16* dZ, const ma_bf1
   uint32_t* status = static_cast<uint32_t*>(base);
   __nv_bfloat16* Dv = reinterpret_cast<__nv_bfloat16*>(static_cast<unsigned char*>(base) + kNoallocHeaderBytes);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  // The scratch keeps the previous call's contents: the status word must
-  // start at zero; D is overwritten in full by computeD below.
-  cudaError_t e = cudaMemsetAsync(status, 0, sizeof(uint32_t), st);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(no-alloc status word)");
-  e = ma::launch_compute_d(reinterpret_cast<bf16p>(dZ), reinterpret_cast<bf16p>(O), Dv, s, st);
+  // The scratch keeps the previous call's contents.  D is overwritten in full
+  // by computeD below; the status word is cleared only by ma_device_status,
+  // which reads it (a time-out is not lost to a later call).
+  cudaError_t e = ma::launch_compute_d(reinterpret_cast<bf16p>(dZ), reinterpret_cast<bf16p>(O), Dv, s, st);
   if (e != cudaSuccess) return cuda_fail(e, "computeD launch (no-alloc)");
   e = ma::launch_flash_bwd(reinterpret_cast<bf16p>(dZ), Dv, l, reinterpret_cast<bf16p>(q),
                            reinterpret_cast<bf16p>(k), reinterpret_cast<bf16p>(v), dQ,
@@ -544,10 +597,12 @@ extern "C" int ma_flashAttentionBackward_noalloc(const ma_bf16* dZ, const ma_bf1
 // ---------------------------------------------------------------------------
 // Host-resident batches: chunked copy / compute / copy-back pipeline.
 // Chunk c uses buffer slot c % kSlots.  Stream order per chunk:
-//   h2d : [wait compute(c - kSlots) done: its inputs are consumed] copy in -> in_ready
-//   comp: wait in_ready, [wait d2h(c - kSlots) done: outputs read] kernels -> comp_done
+//   h2d : [wait the slot's previous compute done: its inputs are consumed] copy in -> in_ready
+//   comp: wait in_ready, [wait the slot's previous copy out done: outputs read] kernels -> comp_done
 //   d2h : wait comp_done, copy out -> out_done
-// so copies in, kernels and copies out of neighbouring chunks overlap.
+// so copies in, kernels and copies out of neighbouring chunks overlap.  The
+// slot's previous use may belong to an earlier run of the pipeline, on any
+// stream: the waits are on the slot's events, not on stream order.
 struct ma_host_pipeline {
   static constexpr int kSlots = 3;
   int device = -1;
@@ -559,6 +614,7 @@ struct ma_host_pipeline {
                   *dV = nullptr, *D = nullptr;
     float *l = nullptr, *dQ = nullptr;
     cudaEvent_t in_ready = nullptr, comp_done = nullptr, out_done = nullptr;
+    bool used = false;  // a chunk (of this or an earlier run) has recorded its events
   } slot[kSlots];
   cudaStream_t h2d = nullptr, comp = nullptr, d2h = nullptr;
   cudaEvent_t start = nullptr;
@@ -588,7 +644,7 @@ int pipeline_chunk(ma_host_pipeline* pl, int c, uint32_t b0, uint32_t bc, bool b
                    const ma_bf16* k, const ma_bf16* v, const ma_bf16* dO, ma_bf16* out, float* l, float* dQ,
                    ma_bf16* dK, ma_bf16* dV) {
   auto& s = pl->slot[c % ma_host_pipeline::kSlots];
-  const bool reuse = c >= ma_host_pipeline::kSlots;
+  const bool reuse = s.used;
   const size_t per_seq = (size_t)pl->p.M * pl->p.N, per_seq_rows = (size_t)pl->p.M * pl->p.NH;
   const size_t off = (size_t)b0 * per_seq, off_rows = (size_t)b0 * per_seq_rows;
   const size_t n = (size_t)bc * per_seq, n_rows = (size_t)bc * per_seq_rows;
@@ -638,7 +694,17 @@ int pipeline_chunk(ma_host_pipeline* pl, int c, uint32_t b0, uint32_t bc, bool b
   }
   if (e == cudaSuccess) e = cudaEventRecord(s.out_done, pl->d2h);
   if (e != cudaSuccess) return cuda_fail(e, "host pipeline: copy out");
+  s.used = true;
   return MA_OK;
+}
+
+// After a failed run: copies of the chunks already enqueued may still read or
+// write the caller's host buffers; wait for them before returning the error,
+// so the caller may free or reuse those buffers at once.
+void pipeline_drain(ma_host_pipeline* pl) {
+  cudaStreamSynchronize(pl->h2d);
+  cudaStreamSynchronize(pl->comp);
+  cudaStreamSynchronize(pl->d2h);
 }
 
 int pipeline_run(ma_host_pipeline* pl, bool backward, const ma_bf16* q, const ma_bf16* k, const ma_bf16* v,
@@ -660,18 +726,27 @@ int pipeline_run(ma_host_pipeline* pl, bool backward, const ma_bf16* q, const ma
   if (e == cudaSuccess) e = cudaStreamWaitEvent(pl->h2d, pl->start, 0);
   if (e == cudaSuccess) e = cudaStreamWaitEvent(pl->comp, pl->start, 0);
   if (e == cudaSuccess) e = cudaStreamWaitEvent(pl->d2h, pl->start, 0);
-  if (e != cudaSuccess) return cuda_fail(e, "host pipeline: start");
+  if (e != cudaSuccess) {
+    pipeline_drain(pl);
+    return cuda_fail(e, "host pipeline: start");
+  }
   const uint32_t nchunks = (B + pl->chunk_B - 1) / pl->chunk_B;
   for (uint32_t c = 0; c < nchunks; ++c) {
     const uint32_t b0 = c * pl->chunk_B;
     const uint32_t bc = B - b0 < pl->chunk_B ? B - b0 : pl->chunk_B;
     rc = pipeline_chunk(pl, (int)c, b0, bc, backward, q, k, v, dO, out, l, dQ, dK, dV);
-    if (rc) return rc;
+    if (rc) {
+      pipeline_drain(pl);
+      return rc;
+    }
   }
   // the d2h stream is in order, so its last record covers every chunk (and,
   // through the waits, every kernel and copy in)
   e = cudaStreamWaitEvent(st, pl->slot[(nchunks - 1) % ma_host_pipeline::kSlots].out_done, 0);
-  if (e != cudaSuccess) return cuda_fail(e, "host pipeline: finish");
+  if (e != cudaSuccess) {
+    pipeline_drain(pl);
+    return cuda_fail(e, "host pipeline: finish");
+  }
   return ok();
 }
 

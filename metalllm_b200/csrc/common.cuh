@@ -43,11 +43,17 @@ inline void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
 
 // Per-kernel bits of the device status word (ma_device_status).
 enum : uint32_t {
-  STATUS_FWD_TIMEOUT = 1u << 0,
-  STATUS_BWD_TIMEOUT = 1u << 1,
-  STATUS_QKV_TIMEOUT = 1u << 2,
-  STATUS_GEMM_TIMEOUT = 1u << 3,
+  STATUS_FWD_TIMEOUT = MA_STATUS_FWD_TIMEOUT,
+  STATUS_BWD_TIMEOUT = MA_STATUS_BWD_TIMEOUT,
+  STATUS_QKV_TIMEOUT = MA_STATUS_QKV_TIMEOUT,
+  STATUS_GEMM_TIMEOUT = MA_STATUS_GEMM_TIMEOUT,
 };
+
+// Test hook of the bounded waits' time-out path (ma_debug_expire_next_wait):
+// returns the wait, in ns, that this launch of the kernel with status bit
+// `kernel_bit` must let run out on a barrier nothing arrives at, or 0; a
+// request is consumed by the launch that takes it.
+uint32_t take_expire_request(uint32_t kernel_bit);
 
 // Problem description shared by the attention kernels.  Row strides are in
 // elements: a (batch, position) row of Q/K/V/O/dO/dK/dV/dQ holds N = NH*D

@@ -117,8 +117,9 @@ struct BwdCfg {
   static constexpr uint32_t OFF_BAR = OFF_STAT + SSTAGES * STAT_BYTES;
   // kv_full/empty[KVB], qd_full/empty[S], st_full/empty[8], then s_full,
   // s_free, p_ready, p_free, dq_full, dq_free, dqs_full, dqs_free, done,
-  // acc_free
-  static constexpr int NBAR = 2 * KVB + 2 * STAGES + 2 * SSTAGES + 10;
+  // acc_free, never (nothing arrives: the time-out test hook), fin (the
+  // UMMA issuer's wind-down)
+  static constexpr int NBAR = 2 * KVB + 2 * STAGES + 2 * SSTAGES + 12;
   static constexpr uint32_t OFF_TSLOT = OFF_BAR + NBAR * 8;
   static constexpr uint32_t SMEM_BYTES = OFF_TSLOT + 16 + 1024;
   static constexpr uint32_t TCOL_S = 0;
@@ -135,6 +136,7 @@ struct BwdParams {
   const float* lse;
   const __nv_bfloat16* Dv;
   uint32_t* status;
+  uint32_t expire_ns;  // time-out test hook (ma_debug_expire_next_wait), 0 = off
 };
 
 // Unit k -> (batch, head, key tile); its query tiles are kt .. nkt-1.
@@ -289,6 +291,8 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
   const uint32_t BAR_DSE = BAR_SF + 56;   // dQ staging read by the reduction
   const uint32_t BAR_DONE = BAR_SF + 64;  // a unit's last UMMA completed
   const uint32_t BAR_ACC = BAR_SF + 72;   // dK/dV TMEM read by the epilogue
+  const uint32_t BAR_NEVER = BAR_SF + 80; // nothing arrives (time-out test hook)
+  const uint32_t BAR_FIN = BAR_SF + 88;   // the UMMA issuer's last commit (wind-down)
   const uint32_t tslot = sbase + C::OFF_TSLOT;
   float* stat_base = reinterpret_cast<float*>(gbase + C::OFF_STAT);
 
@@ -316,6 +320,8 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
     mbar_init(BAR_DSE, 1);
     mbar_init(BAR_DONE, 1);
     mbar_init(BAR_ACC, C::NDRAIN);
+    mbar_init(BAR_NEVER, 1);
+    mbar_init(BAR_FIN, 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -335,12 +341,14 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
       if (lane == 0) {
         tma_prefetch_desc(&tmQ);
         tma_prefetch_desc(&tmdO);
+        uint32_t kv_armed = 0, q_armed = 0;  // loads issued into each ring
         for (StepIter s = first_step(prm); s.valid; advance(prm, s)) {
           const int col0 = s.u.h * HD;
           if (s.i == 0) {  // K/V of a new unit
             const int kvs = s.uc % C::KVB;
             if (s.uc >= C::KVB && !mbar_wait(BAR_KE(kvs), ((s.uc / C::KVB) - 1) & 1, abort_p)) break;
             mbar_arrive_expect_tx(BAR_KF(kvs), 2 * C::KV_BYTES);
+            ++kv_armed;
             for (int kb = 0; kb < C::KB; ++kb) {
               tma_load_3d(sbase + C::OFF_K + kvs * C::KV_BYTES + kb * BK * 128, &tmK, BAR_KF(kvs),
                           col0 + kb * 64, s.u.kt * BK, s.u.b);
@@ -352,12 +360,17 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
           if (s.t >= C::STAGES && !mbar_wait(BAR_QE(st), ((s.t / C::STAGES) - 1) & 1, abort_p)) break;
           const int qt = s.u.kt + s.i;
           mbar_arrive_expect_tx(BAR_QF(st), 2 * C::QD_BYTES);
+          ++q_armed;
           for (int kb = 0; kb < C::KB; ++kb) {
             tma_load_3d(sbase + C::OFF_Q + st * C::QD_BYTES + kb * BQ * 128, &tmQ, BAR_QF(st),
                         col0 + kb * 64, qt * BQ, s.u.b);
             tma_load_3d(sbase + C::OFF_DO + st * C::QD_BYTES + kb * BQ * 128, &tmdO, BAR_QF(st),
                         col0 + kb * 64, qt * BQ, s.u.b);
           }
+        }
+        if (*abort_p) {  // wind-down: let the loads still in flight land
+          drain_ring(BAR_KF, C::KVB, kv_armed);
+          drain_ring(BAR_QF, C::STAGES, q_armed);
         }
       }
     } else if (warp == 1) {
@@ -402,6 +415,9 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
           ok = issue_s(la);
           advance(prm, la);
         }
+        // time-out test hook: with the first products in flight, wait on a
+        // barrier nothing arrives at until the hook's limit runs out
+        if (ok && prm.expire_ns) ok = mbar_wait(BAR_NEVER, 0, abort_p, prm.expire_ns);
         for (; ok && cur.valid; advance(prm, cur)) {
           if (C::EARLY_S && la.valid) {
             if (!issue_s(la)) break;
@@ -453,6 +469,10 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
             if (!issue_s(la)) break;
             advance(prm, la);
           }
+        }
+        if (*abort_p) {  // wind-down: every UMMA issued must complete before TMEM is freed
+          umma_commit(BAR_FIN);
+          mbar_wait_for(BAR_FIN, 0, kDrainLimitNs);
         }
       }
     } else if (warp == 2) {
@@ -814,6 +834,7 @@ cudaError_t launch_bwd(const __nv_bfloat16* dO, const __nv_bfloat16* Dv, const f
   prm.lse = lse;
   prm.Dv = Dv;
   prm.status = status;
+  prm.expire_ns = take_expire_request(STATUS_BWD_TIMEOUT);
   // persistent (one CTA per SM) for short sequences at D=64, else one unit per CTA
   if (HD == 64 && prm.nkt <= PERSIST_MAX_NKT) {
     int dev = 0, sms = 148;

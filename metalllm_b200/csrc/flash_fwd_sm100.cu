@@ -83,8 +83,9 @@ struct FwdCfg {
   static constexpr uint32_t OFF_P = OFF_V + VST * KV_BYTES;      // [2 tiles] P / O staging
   static constexpr uint32_t OFF_BAR = OFF_P + 2 * STG_BYTES;
   // q_full/empty[QST], k_full/empty[KST], v_full/empty[VST], per tile X:
-  // s_full, s_free, p_full, pv_done, o_free
-  static constexpr int NBAR = 2 * QST + 2 * KST + 2 * VST + 2 * 6;
+  // s_full, s_free, p_full, pv_done, o_free, do_full; then never (nothing
+  // arrives: the time-out test hook) and fin (the UMMA issuer's wind-down)
+  static constexpr int NBAR = 2 * QST + 2 * KST + 2 * VST + 2 * 6 + 2;
   static constexpr uint32_t OFF_TSLOT = OFF_BAR + NBAR * 8;
   static constexpr uint32_t SMEM_BYTES = OFF_TSLOT + 16 + 1024;  // + alignment slack
   static constexpr uint32_t TCOL_S = 0;     // S_A, S_B at columns 0, 128
@@ -104,6 +105,7 @@ struct FwdParams {
   // bf16(sum_c O[row][h*64+c] * dO[row][h*64+c]) from the bf16-rounded O
   const __nv_bfloat16* dO;
   __nv_bfloat16* D;
+  uint32_t expire_ns;  // time-out test hook (ma_debug_expire_next_wait), 0 = off
 };
 
 // sum over 8 bf16 pairs of a[i] * b[i], fp32 (products of bf16 values are
@@ -181,6 +183,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   auto BAR_PV = [&](int x) { return barX + 8u * (3 * 2 + x); };
   auto BAR_OE = [&](int x) { return barX + 8u * (4 * 2 + x); };
   auto BAR_DO = [&](int x) { return barX + 8u * (5 * 2 + x); };  // dO tile of X landed (fused computeD)
+  const uint32_t BAR_NEVER = barX + 8u * 12;  // nothing arrives (time-out test hook)
+  const uint32_t BAR_FIN = barX + 8u * 13;    // the UMMA issuer's last commit (wind-down)
   const uint32_t tslot = sbase + C::OFF_TSLOT;
 
   if (threadIdx.x == 0) {
@@ -205,6 +209,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(BAR_OE(x), 128);
       mbar_init(BAR_DO(x), 1);
     }
+    mbar_init(BAR_NEVER, 1);
+    mbar_init(BAR_FIN, 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -256,6 +262,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         col0 + kb * 64, j * BN, un.b);
           ++vc;
         }
+      }
+      if (*abort_p) {  // wind-down: let the loads still in flight land
+        drain_ring(BAR_QF, C::QST, qc);
+        drain_ring(BAR_KF, C::KST, kc);
+        drain_ring(BAR_VF, C::VST, vc);
       }
     } else if (warp == 1 && lane == 0) {
       // ----------------------------------------------------------- MMA
@@ -322,6 +333,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // prologue: S_A(0), S_B(0); K_0 is consumed once both are done
         ok = wait_k(0) && issue_s(0, 0) && (n[1] == 0 || issue_s(1, 0));
         if (ok) umma_commit(BAR_KE(kc % C::KST));
+        // time-out test hook: with the first products in flight, wait on a
+        // barrier nothing arrives at until the hook's limit runs out
+        if (ok && g == 0 && prm.expire_ns) ok = mbar_wait(BAR_NEVER, 0, abort_p, prm.expire_ns);
         for (int j = 0; ok && j < un.nkv; ++j) {
           if (C::EARLY_S) {
             // S_X(j+1) as soon as softmax X has read S_X(j) (issue_s waits for
@@ -358,6 +372,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int x = 0; x < 2; ++x)
           if (n[x] > 0) ++uc[x];
       }
+      if (*abort_p) {  // wind-down: every UMMA issued must complete before TMEM is freed
+        umma_commit(BAR_FIN);
+        mbar_wait_for(BAR_FIN, 0, kDrainLimitNs);
+      }
     }
   } else {
     reg_alloc<REGS_SOFTMAX>();
@@ -372,7 +390,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const bool wg_leader = (warp == 4 + 4 * x) && lane == 0;
     uint8_t* pbuf = gbase + C::OFF_P + x * C::STG_BYTES;
     uint32_t sc = 0;  // S_X consumed so far (== P_X produced)
-    uint32_t nd = 0;  // dO tiles of X loaded so far (fused computeD)
+    uint32_t nd = 0;  // dO tiles of X consumed so far (fused computeD)
+    uint32_t nd_armed = 0;  // dO tile loads issued (leader)
     bool ok = true;
     for (int g = 0; ok; ++g) {
       const int k = unit_of_round(prm, g);
@@ -395,6 +414,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           // epilogue reads each chunk back before writing O over it
           if (prm.dO && wg_leader) {
             mbar_arrive_expect_tx(BAR_DO(x), BM * HD * 2);
+            ++nd_armed;
             for (int kb = 0; kb < C::KB; ++kb)
               tma_load_3d(smem_u32(pbuf) + kb * BM * 128, &tmdO, BAR_DO(x), un.h * HD + kb * 64, qtile * BM,
                           un.b);
@@ -562,7 +582,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         bulk_commit();
       }
     }
-    if (wg_leader) bulk_wait<0>();
+    if (wg_leader) {
+      bulk_wait<0>();
+      // wind-down: a dO tile load whose epilogue never ran must land first
+      if (*abort_p && nd_armed > 0) mbar_wait_for(BAR_DO(x), (nd_armed - 1) & 1, kDrainLimitNs);
+    }
   }
 
   tc_fence_before();
@@ -614,6 +638,7 @@ cudaError_t launch_fwd(const __nv_bfloat16* q, const __nv_bfloat16* k, const __n
   prm.status = status;
   prm.dO = dO;
   prm.D = Dv;
+  prm.expire_ns = take_expire_request(STATUS_FWD_TIMEOUT);
   cudaError_t e = cudaFuncSetAttribute(flash_fwd_kernel<HD>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
   if (e != cudaSuccess) return e;

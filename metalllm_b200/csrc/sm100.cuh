@@ -95,6 +95,35 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   }
 }
 
+// Waits for phase `parity` for at most `limit_ns`, without looking at the
+// abort flag: the wind-down after a time-out uses it to let the copies and
+// tensor-core work it issued itself complete before the CTA frees its TMEM
+// and exits.  Returns whether the phase completed.
+__device__ __forceinline__ bool mbar_wait_for(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 0 && globaltimer_ns() - t0 > limit_ns) return false;
+  }
+}
+
+// Limit of the wind-down waits above (in-flight copies and UMMAs finish in
+// microseconds).
+constexpr uint64_t kDrainLimitNs = 100000000ull;
+
+// After a time-out: waits for the last armed phase of every slot of a ring of
+// `nslots` full barriers (bar(s) for slot s), of which `armed` phases were
+// armed in total in slot order, i.e. for the TMA loads still in flight into
+// the ring.  Called by the thread that armed them.
+template <typename BarFn>
+__device__ __forceinline__ void drain_ring(BarFn bar, uint32_t nslots, uint32_t armed) {
+  for (uint32_t s = 0; s < nslots && s < armed; ++s) {
+    const uint32_t last = s + nslots * ((armed - 1 - s) / nslots);  // last arming of slot s
+    mbar_wait_for(bar(s), (last / nslots) & 1u, kDrainLimitNs);
+  }
+}
+
 // mbar_wait for roles that run whole warps: the result is made warp-uniform
 // (all lanes fail if any lane failed), so warp-collective instructions that
 // follow (tcgen05.ld/st, shuffles, votes) always see a converged warp.

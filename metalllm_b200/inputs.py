@@ -11,6 +11,9 @@ identical bf16 arrays.  Box-Muller and splitmix64 are the published methods
 """
 from __future__ import annotations
 
+import os
+from concurrent.futures import ThreadPoolExecutor
+
 import numpy as np
 
 _GOLDEN = np.uint64(0x9E3779B97F4A7C15)
@@ -41,12 +44,17 @@ def bf16_bits_to_f32(b: np.ndarray) -> np.ndarray:
 
 
 def normal_bf16(n: int, seed: int, stream: int, scale: float = 1.0, offset: int = 0,
-                chunk: int = 1 << 22) -> np.ndarray:
-    """n bf16 bit patterns of N(0, scale^2) for elements offset .. offset+n-1."""
+                chunk: int = 1 << 20, threads: int = 0) -> np.ndarray:
+    """n bf16 bit patterns of N(0, scale^2) for elements offset .. offset+n-1.
+
+    Chunks are generated on `threads` host threads (0: one per core; numpy
+    releases the GIL inside its element-wise loops); every element depends
+    only on its index, so the result does not depend on the thread count."""
     base = _splitmix64(np.array([(seed << 32) + stream], dtype=np.uint64))[0]
     out = np.empty(n, dtype=np.uint16)
     inv53 = 1.0 / float(1 << 53)
-    for s in range(0, n, chunk):
+
+    def fill(s: int) -> None:
         e = min(n, s + chunk)
         idx = np.arange(offset + s, offset + e, dtype=np.uint64) * np.uint64(2)
         with np.errstate(over="ignore"):
@@ -56,6 +64,15 @@ def normal_bf16(n: int, seed: int, stream: int, scale: float = 1.0, offset: int 
         u2 = (h2 >> np.uint64(11)).astype(np.float64) * inv53
         z = np.sqrt(-2.0 * np.log(u1)) * np.cos(2.0 * np.pi * u2) * scale
         out[s:e] = f32_to_bf16_bits(z.astype(np.float32))
+
+    starts = range(0, n, chunk)
+    nthreads = threads or (os.cpu_count() or 1)
+    if nthreads <= 1 or len(starts) <= 1:
+        for s in starts:
+            fill(s)
+    else:
+        with ThreadPoolExecutor(max_workers=min(nthreads, len(starts))) as ex:
+            list(ex.map(fill, starts))
     return out
 
 

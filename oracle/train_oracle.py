@@ -22,9 +22,13 @@ FLOAT = np.float32
 def r16(x):
     """Round float32 values to the nearest bf16 (ties to even), as float32."""
     x = np.ascontiguousarray(x, dtype=np.float32)
-    u = x.view(np.uint32).astype(np.uint64)
-    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
-    return u.astype(np.uint32).view(np.float32)
+    u = x.view(np.uint32)
+    # finite values stay below 2^32 after adding at most 0x8000
+    r = (u >> np.uint32(16)) & np.uint32(1)
+    r += np.uint32(0x7FFF)
+    r += u
+    r &= np.uint32(0xFFFF0000)
+    return r.view(np.float32)
 
 
 def layernorm(x, g, b, eps=1e-5):

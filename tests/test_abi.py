@@ -217,3 +217,14 @@ def test_model_create_validates_its_configuration():
     if not torch.cuda.is_available():
         assert create() in (4, 7), lib.ma_model_last_error()
         assert h.value is None
+
+
+def test_expire_hook_validates_without_device(cuda_lib):
+    """ma_debug_expire_next_wait (the time-out test hook) accepts only the
+    kernels that have the hook and a wait of 1 ns .. 1 s; checked on the host."""
+    from metalllm_b200 import _lib
+    assert _lib.ERROR_NAMES[cuda_lib.ma_debug_expire_next_wait(_lib.STATUS_QKV_TIMEOUT, 1000)] == "MA_ERR_RANGE"
+    assert _lib.ERROR_NAMES[cuda_lib.ma_debug_expire_next_wait(_lib.STATUS_BWD_TIMEOUT, 0)] == "MA_ERR_RANGE"
+    assert _lib.ERROR_NAMES[cuda_lib.ma_debug_expire_next_wait(_lib.STATUS_BWD_TIMEOUT, 2 * 10 ** 9)] == "MA_ERR_RANGE"
+    assert cuda_lib.ma_debug_expire_next_wait(_lib.STATUS_BWD_TIMEOUT, 1000) == 0
+    assert cuda_lib.ma_debug_expire_next_wait(0, 0) == 0  # cancels the request

@@ -9,7 +9,10 @@ Checked through the C ABI against the allocating entry points
 (ma_computeD + ma_flashAttentionBackward) on two calls in a row with different
 shapes and inputs, so that a second call which read the first call's scratch
 would show; tolerance as in the other GPU parity tests (max-abs 2e-2,
-relative-L2 1e-2).  This file is collected last on purpose."""
+relative-L2 1e-2).  Its kernels' time-out bit goes to a status word in the
+same scratch, which ma_device_status (allocating nothing) reads and clears:
+after the two calls it must read 0, and a wait made to run out through the
+time-out test hook must show there.  This file is collected last on purpose."""
 import ctypes
 
 import numpy as np
@@ -89,6 +92,26 @@ def test_noalloc_matches_allocating_entry_points_on_two_calls():
             assert np.isfinite(a32).all(), f"{name} (B={B} T={T} D={D}) not fully written"
             ok, mae, rl2 = compare(a32, b32, MAX_ABS, REL_L2)
             assert ok, f"{name} (B={B} T={T} D={D}): max_abs={mae:.3e} rel_l2={rl2:.3e}"
+    # ma_device_status also reads (and clears) the scratch's status word
+    assert A.device_status() == 0
+
+    # a backward whose bounded wait runs out (time-out test hook) is reported
+    # through the scratch's status word, and the next call is unaffected
+    B, T, H, D, q, k, v, do, out, l = prepared[0]
+    p = _params(T, H, D)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    dQ, dK, dV = (torch.empty(q.shape, dtype=torch.float32, device=q.device), torch.empty_like(q),
+                  torch.empty_like(q))
+    A.debug_expire_next_wait(_lib.STATUS_BWD_TIMEOUT, 1_000_000)
+    _lib.call("ma_flashAttentionBackward_noalloc", ptr(do), ptr(out), ptr(l), ptr(q), ptr(k),
+              ptr(v), ptr(dQ), ptr(dK), ptr(dV), ctypes.byref(p), B, stream)
+    assert A.device_status() == _lib.STATUS_BWD_TIMEOUT
+    _lib.call("ma_flashAttentionBackward_noalloc", ptr(do), ptr(out), ptr(l), ptr(q), ptr(k),
+              ptr(v), ptr(dQ), ptr(dK), ptr(dV), ctypes.byref(p), B, stream)
+    torch.cuda.synchronize()
+    for a, b in ((dQ, got[0][0]), (dK, got[0][1]), (dV, got[0][2])):
+        ok, mae, rl2 = compare(a.float().cpu().numpy(), b.float().cpu().numpy(), 1e-5, 1e-6)
+        assert ok, f"after the time-out: max_abs={mae:.3e} rel_l2={rl2:.3e}"
     assert A.device_status() == 0
 
     # a size beyond the scratch is refused on a GPU too, and changes nothing
