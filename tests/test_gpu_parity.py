@@ -4,8 +4,8 @@ ABI, against the CPU oracle (exact-interface mode) and the golden fixtures.
 Tolerances: O, dQ, dK, dV within max-abs 2e-2 and
 relative-L2 1e-2 of the oracle's fp32 values; lse within 1e-3 absolute.
 computeD is compared with the oracle's fp32 sum to 1 bf16 rounding step.
-Large configs are checked on sampled (batch, head) shards against the oracle
-and, over the whole tensor, through size-independent identities."""
+Configs 2, 3 and 4 are checked on every (batch, head) shard against the
+oracle and, over the whole tensor, through size-independent identities."""
 from pathlib import Path
 
 import numpy as np
@@ -266,12 +266,12 @@ def test_bad_call_on_gpu_raises(A):
 def test_full_config_every_shard(A, oracle_mod, cfg):
     """Every (batch, head) shard of configs 2, 3 and 4 (768, 128 and 128
     shards; attention.metal:74-76, 219-221 compute every head of every row)
-    against the oracle, in two ways:
-      - the oracle's own chain: its forward, computeD from its own bf16 O and
-        its backward from its own l and D, so no GPU intermediate feeds the
-        comparison of O, l, D, dQ, dK and dV;
-      - the oracle's backward fed the GPU's l and D, which checks the backward
-        kernel alone.
+    against the oracle: O and l against the oracle's forward, D against
+    computeD of the oracle's own bf16 O, and dQ, dK, dV twice: against the
+    oracle's backward fed the GPU's l and D (the backward kernel alone, at the
+    north_star tolerance) and against the oracle's backward fed its own l and
+    D, so that no GPU intermediate is in that chain (a convention shared by
+    the GPU's forward and backward but not the reference's would show there).
     Plus, over the whole tensor, README.md:132 (row 0 of every causal head is
     V row 0, bit for bit) and sum_keys dV = sum_queries dO per head.  These
     cover every unit of the persistent forward's alternating rounds and both
@@ -289,7 +289,7 @@ def test_full_config_every_shard(A, oracle_mod, cfg):
     g_out, g_l, g_D = bf(out), f32(l), down(Dv)
     g_dQ, g_dK, g_dV = f32(dQ), bf(dK), bf(dV)
     del out, l, Dv, dQ, dK, dV
-    # the oracle's own chain
+    # the oracle's own chain: O, l, D
     o_out, o_l, o_32 = oracle_mod.flash_forward(q, k, v, H, want_f32=True)
     check(f"{cfg} O", g_out, o_32)
     assert np.abs(g_l - o_l).max() <= LSE_ABS
@@ -297,13 +297,20 @@ def test_full_config_every_shard(A, oracle_mod, cfg):
     o_D, o_D32 = oracle_mod.compute_d(do, o_out, H, want_f32=True)
     gD = bf16_bits_to_f32(g_D)
     check(f"{cfg} D", gD, o_D32, 2 ** -6 * max(1.0, float(np.abs(o_D32).max())), REL_L2)
-    rq, _, _, rk32, rv32 = oracle_mod.flash_backward(do, o_D, o_l, q, k, v, H, want_f32=True)
-    check(f"{cfg} dQ (oracle chain)", g_dQ, rq)
-    check(f"{cfg} dK (oracle chain)", g_dK, rk32)
-    check(f"{cfg} dV (oracle chain)", g_dV, rv32)
-    del rq, rk32, rv32, o_out, o_D, o_D32
-    # the oracle's backward from the GPU's l and D
-    rq, _, _, rk32, rv32 = oracle_mod.flash_backward(do, g_D, g_l, q, k, v, H, want_f32=True)
-    check(f"{cfg} dQ", g_dQ, rq)
-    check(f"{cfg} dK", g_dK, rk32)
-    check(f"{cfg} dV", g_dV, rv32)
+    del o_out, o_D32
+    # the oracle's backward fed the GPU's l and D: the north_star tolerance
+    fq, _, _, fk, fv = oracle_mod.flash_backward(do, g_D, g_l, q, k, v, H, want_f32=True)
+    check(f"{cfg} dQ", g_dQ, fq)
+    check(f"{cfg} dK", g_dK, fk)
+    check(f"{cfg} dV", g_dV, fv)
+    # the oracle's backward from its own l and D (no GPU value in the chain).
+    # D is stored as bf16 (attention.metal:193), and where the two chains'
+    # bf16 O differ by a rounding step their D can round one step apart; a
+    # step of D moves dS = P (dP - D) / sqrt(d), hence dQ and dK, by up to
+    # |dD| |K| / sqrt(d) per key.  The allowance is that effect as the oracle
+    # itself shows it (its backward fed the GPU's D vs its own), on top of the
+    # north_star max-abs; rel-L2 keeps the north_star bound.
+    rq, _, _, rk, rv = oracle_mod.flash_backward(do, o_D, o_l, q, k, v, H, want_f32=True)
+    for name, got, own, fed in (("dQ", g_dQ, rq, fq), ("dK", g_dK, rk, fk), ("dV", g_dV, rv, fv)):
+        allowance = float(np.abs(own - fed).max())
+        check(f"{cfg} {name} (oracle chain, allowance {allowance:.2e})", got, own, MAX_ABS + allowance, REL_L2)
