@@ -70,29 +70,40 @@ using namespace sm100;
 
 constexpr int BK = 128;  // keys per unit
 constexpr int BQ = 128;  // queries per step
-constexpr int NCOMP = 256;  // compute threads (warpgroups 1 and 2)
 constexpr int SSTAGES = 8;  // statistics stages
 constexpr int PERSIST_MAX_NKT = 16;  // persistent launch when T/128 <= this (D=64)
 constexpr float LOG2E = 1.4426950408889634f;
+
+#ifndef BWD_D64_PARTS
+#define BWD_D64_PARTS 2
+#endif
 
 template <int HD, bool PERSIST>
 struct BwdCfg {
   static constexpr int KB = HD / 64;
   static constexpr bool D64 = HD == 64;
-  // D=64: a fourth warpgroup drains dQ and stores dK/dV, so the compute
-  // warpgroups only form P^T and dS^T.  Register split per thread after
-  // setmaxnreg: warpgroup 0 80, compute 184, drain 64; without
-  // it (D=128, 384 threads): warpgroup 0 120, compute 192.
-  static constexpr bool DRAIN_WG = D64;
-  static constexpr int NUM_THREADS = DRAIN_WG ? 512 : 384;
-  static constexpr int LAUNCH_REGS = DRAIN_WG ? 128 : 168;  // 65536 / threads, multiple of 8
-  static constexpr int REGS_PRODUCER = DRAIN_WG ? 80 : 120;
-  static constexpr int REGS_COMPUTE = DRAIN_WG ? 184 : 192;
+  // Compute warpgroups: each takes BQ / NPART query columns of every step.
+  // D=64 with NPART=2: a fourth warpgroup drains dQ and stores dK/dV, so the
+  // compute warpgroups only form P^T and dS^T (register split per thread
+  // after setmaxnreg: warpgroup 0 80, compute 184, drain 64).  Otherwise the
+  // compute warpgroups also drain dQ and store dK/dV, each its share of the
+  // columns: D=64 with NPART=4 (640 threads; 64 / 104), D=128 (384 threads;
+  // 120 / 192).
+  static constexpr int NPART = D64 ? BWD_D64_PARTS : 2;
+  static constexpr int CPP = BQ / NPART;       // query columns per part
+  static constexpr int NCOMP = 128 * NPART;    // compute threads
+  static constexpr bool DRAIN_WG = D64 && NPART == 2;
+  static constexpr int NUM_THREADS = 128 + NCOMP + (DRAIN_WG ? 128 : 0);
+  static constexpr int LAUNCH_REGS = (65536 / NUM_THREADS) & ~7;  // registers per thread at launch
+  static constexpr int REGS_PRODUCER = NPART == 4 ? 64 : (DRAIN_WG ? 80 : 120);
   static constexpr int REGS_DRAIN = DRAIN_WG ? 64 : 0;
+  static constexpr int REGS_COMPUTE =
+      ((NUM_THREADS * LAUNCH_REGS - 128 * REGS_PRODUCER - 128 * REGS_DRAIN) / NCOMP) & ~7;
   static constexpr int NDRAIN = DRAIN_WG ? 128 : NCOMP;  // arrivals on DQE, DSF, ACC
-  static_assert(128 * REGS_PRODUCER + 256 * REGS_COMPUTE + 128 * REGS_DRAIN ==
+  static_assert(128 * REGS_PRODUCER + NCOMP * REGS_COMPUTE + 128 * REGS_DRAIN <=
                     NUM_THREADS * LAUNCH_REGS,
-                "register split must equal the launch allocation");
+                "register split must fit the launch allocation");
+  static_assert(CPP % 16 == 0 && (HD / NPART) % 16 == 0, "column split");
   // Q_i/dO_i stages and K/V buffers: a persistent CTA double-buffers K/V to
   // prefetch the next unit; otherwise the smem goes to a deeper Q/dO ring
   static constexpr int STAGES = D64 ? (PERSIST ? 2 : 3) : 1;
@@ -208,15 +219,15 @@ __device__ __forceinline__ void advance(const BwdParams& prm, StepIter& s) {
   s.valid = next_unit(prm, s);
 }
 
-// P^T and dS^T for 64 query columns of one key row.  s[] holds S^T on entry
+// P^T and dS^T for N query columns of one key row.  s[] holds S^T on entry
 // and P^T on exit; dp[] holds dP^T on entry and dS^T on exit.  nl = -l*log2e
 // and nd = -D/sqrt(D) per query column (shared memory, broadcast reads).
-template <bool DIAG>
-__device__ __forceinline__ void p_ds_row(float (&s)[64], float (&dp)[64], const float* nl,
+template <bool DIAG, int N>
+__device__ __forceinline__ void p_ds_row(float (&s)[N], float (&dp)[N], const float* nl,
                                          const float* nd, float c, float sc, int krow, int qcol0) {
   const float2 c2 = make_float2(c, c), sc2 = make_float2(sc, sc);
 #pragma unroll
-  for (int j = 0; j < 64; j += 4) {
+  for (int j = 0; j < N; j += 4) {
     const float4 L = *reinterpret_cast<const float4*>(nl + j);
     const float4 Dn = *reinterpret_cast<const float4*>(nd + j);
     const float2 t0 = __ffma2_rn(make_float2(s[j], s[j + 1]), c2, make_float2(L.x, L.y));
@@ -244,12 +255,13 @@ __device__ __forceinline__ void p_ds_row(float (&s)[64], float (&dp)[64], const 
   }
 }
 
-// 64 bf16 values of one row as 8 swizzled 16-byte chunks of a K-major SW128
-// row (row base `rowp`, swizzle phase `row & 7`).
-__device__ __forceinline__ void store_row_sw128(uint8_t* rowp, int row, const float (&v)[64]) {
+// N bf16 values of one row as N/8 swizzled 16-byte chunks of a K-major SW128
+// row, starting at chunk ch0 (row base `rowp`, swizzle phase `row & 7`).
+template <int N>
+__device__ __forceinline__ void store_row_sw128(uint8_t* rowp, int row, const float (&v)[N], int ch0) {
 #pragma unroll
-  for (int ch = 0; ch < 8; ++ch) {
-    const int c0 = ch * 8;
+  for (int k = 0; k < N / 8; ++k) {
+    const int c0 = k * 8, ch = ch0 + k;
     uint4 w;
     w.x = pack_bf16(v[c0 + 0], v[c0 + 1]);
     w.y = pack_bf16(v[c0 + 2], v[c0 + 3]);
@@ -308,11 +320,11 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
     }
     for (int s = 0; s < SSTAGES; ++s) {
       mbar_init(BAR_TF(s), 32);
-      mbar_init(BAR_TE(s), NCOMP);
+      mbar_init(BAR_TE(s), C::NCOMP);
     }
     mbar_init(BAR_SF, 1);
-    mbar_init(BAR_SE, NCOMP);
-    mbar_init(BAR_PR, NCOMP);
+    mbar_init(BAR_SE, C::NCOMP);
+    mbar_init(BAR_PR, C::NCOMP);
     mbar_init(BAR_PE, 1);
     mbar_init(BAR_DQF, 1);
     mbar_init(BAR_DQE, C::NDRAIN);
@@ -513,36 +525,39 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
         bulk_wait<0>();
       }
     }
-  } else if (!C::DRAIN_WG || warp < 12) {
+  } else if (!C::DRAIN_WG || warp < 4 + C::NCOMP / 32) {
     reg_alloc<C::REGS_COMPUTE>();
     // ------------------------------------------------------------ compute
-    const int cw = warp - 4;                   // 0..7
+    constexpr int CPP = C::CPP;                // query columns per part
+    const int cw = warp - 4;                   // 0 .. NCOMP/32 - 1
     const int quarter = warp & 3;              // TMEM lane quarter
     const int krow = quarter * 32 + lane;      // key row (and dQ query row) within the tile
-    const int half = cw >> 2;                  // query columns half*64 .. +63
+    const int part = cw >> 2;                  // query columns part*CPP .. +CPP-1
     const uint32_t tl = tmem + ((uint32_t)(quarter * 32) << 16);
     const float c = prm.scale_log2, sc = prm.scale;
     bool ok = true;
 
     // dQ of global step t: TMEM -> fp32 staging (128-byte swizzle, 32-column
-    // boxes); the reduce issuer (warp 3) sends it to global memory
+    // boxes); the reduce issuer (warp 3) sends it to global memory.  Each
+    // part drains HD / NPART of the head dimension's columns.
     auto drain_dq = [&](uint32_t t) {
       if (ok) ok = mbar_wait_warp(BAR_DQF, t & 1, abort_p);
       if (ok && t >= 1) ok = mbar_wait_warp(BAR_DSE, (t - 1) & 1, abort_p);
       if (!ok) return;
       tc_fence_after();
-      constexpr int CPH = HD / 2;  // columns per half
+      constexpr int CPH = HD / C::NPART;  // dQ columns per part
       uint8_t* dqs = gbase + C::OFF_DQS;
 #pragma unroll
-      for (int cc = 0; cc < CPH; cc += 32) {
-        uint32_t r[32];
-        tmem_ld32(tl + C::TCOL_DQ + half * CPH + cc, r);
+      for (int cc = 0; cc < CPH; cc += 16) {
+        uint32_t r[16];
+        tmem_ld16(tl + C::TCOL_DQ + part * CPH + cc, r);
         tmem_wait_ld_dep(r);
-        const int box = (half * CPH + cc) / 32;
-        uint8_t* rowp = dqs + box * (BQ * 128) + krow * 128;
+        const int col = part * CPH + cc;  // first column (fp32) of the 16
+        uint8_t* rowp = dqs + (col / 32) * (BQ * 128) + krow * 128;
 #pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          uint4 v = make_uint4(r[ch * 4 + 0], r[ch * 4 + 1], r[ch * 4 + 2], r[ch * 4 + 3]);
+        for (int q = 0; q < 4; ++q) {
+          const int ch = (col % 32) / 4 + q;
+          uint4 v = make_uint4(r[q * 4 + 0], r[q * 4 + 1], r[q * 4 + 2], r[q * 4 + 3]);
           *reinterpret_cast<uint4*>(rowp + ((ch ^ (krow & 7)) * 16)) = v;
         }
       }
@@ -560,7 +575,7 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
       if (ok) ok = mbar_wait_warp(BAR_DONE, vuc & 1, abort_p);
       if (!ok) return;
       tc_fence_after();
-      constexpr int CPH = HD / 2;
+      constexpr int CPH = HD / C::NPART;  // dV, dK columns per part
       uint32_t acc[2][CPH];
 #pragma unroll
       for (int which = 0; which < 2; ++which) {
@@ -568,7 +583,7 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
 #pragma unroll
         for (int cc = 0; cc < CPH; cc += 16) {
           uint32_t r[16];
-          tmem_ld16(tl + tcol + half * CPH + cc, r);
+          tmem_ld16(tl + tcol + part * CPH + cc, r);
           tmem_wait_ld_dep(r);
 #pragma unroll
           for (int j = 0; j < 16; ++j) acc[which][cc + j] = r[j];
@@ -578,7 +593,7 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
       mbar_arrive(BAR_ACC);  // the next unit may overwrite dK/dV in TMEM
       const int key = v.kt * BK + krow;
       if (key < prm.T) {
-        const long long off = ((long long)v.b * prm.T + key) * prm.N + v.h * HD + half * CPH;
+        const long long off = ((long long)v.b * prm.T + key) * prm.N + v.h * HD + part * CPH;
 #pragma unroll
         for (int which = 0; which < 2; ++which) {
           uint4* dst = reinterpret_cast<uint4*>((which == 0 ? dV : dK) + off);
@@ -610,49 +625,64 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
       ok = mbar_wait_warp(BAR_SF, t & 1, abort_p);
       if (!ok) break;
       tc_fence_after();
-      float s[64], dp[64];
-      {
+      float s[CPP], dp[CPP];
+      if constexpr (CPP == 64) {
         uint32_t ra[32], rb[32];
-        tmem_ld32(tl + C::TCOL_S + half * 64, ra);
-        tmem_ld32(tl + C::TCOL_S + half * 64 + 32, rb);
+        tmem_ld32(tl + C::TCOL_S + part * 64, ra);
+        tmem_ld32(tl + C::TCOL_S + part * 64 + 32, rb);
         tmem_wait_ld_dep(ra, rb);
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           s[j] = __uint_as_float(ra[j]);
           s[32 + j] = __uint_as_float(rb[j]);
         }
-        tmem_ld32(tl + C::TCOL_DP + half * 64, ra);
-        tmem_ld32(tl + C::TCOL_DP + half * 64 + 32, rb);
+        tmem_ld32(tl + C::TCOL_DP + part * 64, ra);
+        tmem_ld32(tl + C::TCOL_DP + part * 64 + 32, rb);
         tmem_wait_ld_dep(ra, rb);
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           dp[j] = __uint_as_float(ra[j]);
           dp[32 + j] = __uint_as_float(rb[j]);
         }
+      } else {
+        static_assert(CPP == 32, "column split");
+        uint32_t ra[32], rb[32];
+        tmem_ld32(tl + C::TCOL_S + part * 32, ra);
+        tmem_ld32(tl + C::TCOL_DP + part * 32, rb);
+        tmem_wait_ld_dep(ra, rb);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          s[j] = __uint_as_float(ra[j]);
+          dp[j] = __uint_as_float(rb[j]);
+        }
       }
       tc_fence_before();
       mbar_arrive(BAR_SE);
       ok = mbar_wait_warp(BAR_TF(ss), (t / SSTAGES) & 1, abort_p);
       if (!ok) break;
-      const float* stt = stat_base + ss * (2 * BQ) + half * 64;
-      if (i == 0) p_ds_row<true>(s, dp, stt, stt + BQ, c, sc, krow, half * 64);
-      else p_ds_row<false>(s, dp, stt, stt + BQ, c, sc, krow, half * 64);
+      const float* stt = stat_base + ss * (2 * BQ) + part * CPP;
+      if (i == 0) p_ds_row<true, CPP>(s, dp, stt, stt + BQ, c, sc, krow, part * CPP);
+      else p_ds_row<false, CPP>(s, dp, stt, stt + BQ, c, sc, krow, part * CPP);
       mbar_arrive(BAR_TE(ss));
       // the previous step's UMMAs must be done with P^T/dS^T, and when the dQ
       // staging shares their smem its reduction must have read it
       if (t >= 1) ok = mbar_wait_warp(BAR_PE, (t - 1) & 1, abort_p);
       if (ok && C::DQS_ALIAS && t >= 1) ok = mbar_wait_warp(BAR_DSE, (t - 1) & 1, abort_p);
       if (!ok) break;
-      if (C::P_IN_TMEM) {
-        uint32_t pk[32];
+      // this part's columns of the key row: P^T (bf16 pairs in TMEM, or smem),
+      // dS^T (smem); chunk (part*CPP % 64) / 8 of 64-column block part*CPP / 64
+      const int blk = (part * CPP) / 64, ch0 = ((part * CPP) % 64) / 8;
+      if constexpr (C::P_IN_TMEM) {
+        uint32_t pk[CPP / 2];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) pk[j] = pack_bf16(s[2 * j], s[2 * j + 1]);
-        tmem_st32(tl + C::TCOL_PT + half * 32, pk);
+        for (int j = 0; j < CPP / 2; ++j) pk[j] = pack_bf16(s[2 * j], s[2 * j + 1]);
+        if constexpr (CPP == 64) tmem_st32(tl + C::TCOL_PT + part * 32, pk);
+        else tmem_st16(tl + C::TCOL_PT + part * 16, pk);
         tmem_wait_st();
       } else {
-        store_row_sw128(gbase + C::OFF_PT + half * (BK * 128) + krow * 128, krow, s);
+        store_row_sw128<CPP>(gbase + C::OFF_PT + blk * (BK * 128) + krow * 128, krow, s, ch0);
       }
-      store_row_sw128(gbase + C::OFF_DST + half * (BK * 128) + krow * 128, krow, dp);
+      store_row_sw128<CPP>(gbase + C::OFF_DST + blk * (BK * 128) + krow * 128, krow, dp, ch0);
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(BAR_PR);
