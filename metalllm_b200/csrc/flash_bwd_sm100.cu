@@ -36,8 +36,9 @@
 //   warpgroup 0 (120 registers per thread after setmaxnreg):
 //     warp 0   TMA producer: K/V per unit, Q_i/dO_i into a STAGES-deep ring
 //     warp 1   TMEM owner; lane 0 issues every UMMA and commit
-//     warp 2   statistics: stages -l_i*log2(e) and -D_i/sqrt(D) per query
-//              (strided in global memory) 8 tiles ahead
+//     warp 2   statistics: -l_i*log2(e) and -D_i/sqrt(D) per query (strided
+//              in global memory), loaded into registers a step ahead and
+//              staged in shared memory for the compute warps
 //     warp 3   lane 0 issues the dQ bulk reductions
 //   warpgroups 1, 2 (192 registers): compute, thread = key row = TMEM lane;
 //              warpgroup 1 takes query columns 0-63, warpgroup 2 columns
@@ -70,13 +71,9 @@ using namespace sm100;
 
 constexpr int BK = 128;  // keys per unit
 constexpr int BQ = 128;  // queries per step
-constexpr int SSTAGES = 8;  // statistics stages
 constexpr int PERSIST_MAX_NKT = 16;  // persistent launch when T/128 <= this (D=64)
 constexpr float LOG2E = 1.4426950408889634f;
 
-#ifndef BWD_D64_PARTS
-#define BWD_D64_PARTS 2
-#endif
 
 template <int HD, bool PERSIST>
 struct BwdCfg {
@@ -89,7 +86,7 @@ struct BwdCfg {
   // compute warpgroups also drain dQ and store dK/dV, each its share of the
   // columns: D=64 with NPART=4 (640 threads; 64 / 104), D=128 (384 threads;
   // 120 / 192).
-  static constexpr int NPART = D64 ? BWD_D64_PARTS : 2;
+  static constexpr int NPART = 2;
   static constexpr int CPP = BQ / NPART;       // query columns per part
   static constexpr int NCOMP = 128 * NPART;    // compute threads
   static constexpr bool DRAIN_WG = D64 && NPART == 2;
@@ -112,6 +109,13 @@ struct BwdCfg {
   static constexpr bool EARLY_S = D64;           // next S^T before dV/dK/dQ
   static constexpr bool DQ_ALIAS = !D64;         // dQ accumulator reuses the S^T columns
   static constexpr bool DQS_ALIAS = !D64;        // dQ staging reuses the P^T/dS^T smem
+  // dQ staging buffers (the code allows more than one; a second buffer was
+  // measured slower: the extra shared-memory traffic in flight slows the
+  // tensor core's operand reads more than the overlap gains).  Statistics
+  // ring stages: the statistics warp loads a step's values into registers a
+  // step ahead, so one stage suffices where the shared memory is tight.
+  static constexpr int DQSB = 1;
+  static constexpr int SSTG = (D64 && PERSIST) ? 1 : 8;
   static constexpr uint32_t KV_BYTES = BK * HD * 2;
   static constexpr uint32_t QD_BYTES = BQ * HD * 2;
   static constexpr uint32_t PT_BYTES = BK * BQ * 2;
@@ -123,14 +127,14 @@ struct BwdCfg {
   static constexpr uint32_t OFF_DO = OFF_Q + STAGES * QD_BYTES;       // [STAGES]
   static constexpr uint32_t OFF_PT = OFF_DO + STAGES * QD_BYTES;      // only without P_IN_TMEM
   static constexpr uint32_t OFF_DST = OFF_PT + (P_IN_TMEM ? 0 : PT_BYTES);
-  static constexpr uint32_t OFF_DQS = DQS_ALIAS ? OFF_PT : OFF_DST + PT_BYTES;
-  static constexpr uint32_t OFF_STAT = DQS_ALIAS ? OFF_DST + PT_BYTES : OFF_DQS + DQS_BYTES;
-  static constexpr uint32_t OFF_BAR = OFF_STAT + SSTAGES * STAT_BYTES;
+  static constexpr uint32_t OFF_DQS = DQS_ALIAS ? OFF_PT : OFF_DST + PT_BYTES;  // [DQSB]
+  static constexpr uint32_t OFF_STAT = DQS_ALIAS ? OFF_DST + PT_BYTES : OFF_DQS + DQSB * DQS_BYTES;
+  static constexpr uint32_t OFF_BAR = OFF_STAT + SSTG * STAT_BYTES;
   // kv_full/empty[KVB], qd_full/empty[S], st_full/empty[8], then s_full,
   // s_free, p_ready, p_free, dq_full, dq_free, dqs_full, dqs_free, done,
   // acc_free, never (nothing arrives: the time-out test hook), fin (the
   // UMMA issuer's wind-down)
-  static constexpr int NBAR = 2 * KVB + 2 * STAGES + 2 * SSTAGES + 12;
+  static constexpr int NBAR = 2 * KVB + 2 * STAGES + 2 * SSTG + 12 + 2 * (DQSB - 1);
   static constexpr uint32_t OFF_TSLOT = OFF_BAR + NBAR * 8;
   static constexpr uint32_t SMEM_BYTES = OFF_TSLOT + 16 + 1024;
   static constexpr uint32_t TCOL_S = 0;
@@ -292,15 +296,16 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
   auto BAR_QF = [&](int s) { return bar0 + 8u * (2 * C::KVB + s); };
   auto BAR_QE = [&](int s) { return bar0 + 8u * (2 * C::KVB + C::STAGES + s); };
   auto BAR_TF = [&](int s) { return bar0 + 8u * (2 * C::KVB + 2 * C::STAGES + s); };
-  auto BAR_TE = [&](int s) { return bar0 + 8u * (2 * C::KVB + 2 * C::STAGES + SSTAGES + s); };
-  const uint32_t BAR_SF = bar0 + 8u * (2 * C::KVB + 2 * C::STAGES + 2 * SSTAGES);
+  auto BAR_TE = [&](int s) { return bar0 + 8u * (2 * C::KVB + 2 * C::STAGES + C::SSTG + s); };
+  const uint32_t BAR_SF = bar0 + 8u * (2 * C::KVB + 2 * C::STAGES + 2 * C::SSTG);
   const uint32_t BAR_SE = BAR_SF + 8;
   const uint32_t BAR_PR = BAR_SF + 16;
   const uint32_t BAR_PE = BAR_SF + 24;
   const uint32_t BAR_DQF = BAR_SF + 32;
   const uint32_t BAR_DQE = BAR_SF + 40;
-  const uint32_t BAR_DSF = BAR_SF + 48;   // dQ staging written
-  const uint32_t BAR_DSE = BAR_SF + 56;   // dQ staging read by the reduction
+  // staging buffer b: BAR_DSF(b) written, BAR_DSE(b) read by its reduction
+  auto BAR_DSF = [&](int b) { return b == 0 ? BAR_SF + 48 : BAR_SF + 96 + 16u * (b - 1); };
+  auto BAR_DSE = [&](int b) { return b == 0 ? BAR_SF + 56 : BAR_SF + 104 + 16u * (b - 1); };
   const uint32_t BAR_DONE = BAR_SF + 64;  // a unit's last UMMA completed
   const uint32_t BAR_ACC = BAR_SF + 72;   // dK/dV TMEM read by the epilogue
   const uint32_t BAR_NEVER = BAR_SF + 80; // nothing arrives (time-out test hook)
@@ -318,7 +323,7 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
       mbar_init(BAR_QF(s), 1);
       mbar_init(BAR_QE(s), 1);
     }
-    for (int s = 0; s < SSTAGES; ++s) {
+    for (int s = 0; s < C::SSTG; ++s) {
       mbar_init(BAR_TF(s), 32);
       mbar_init(BAR_TE(s), C::NCOMP);
     }
@@ -328,8 +333,10 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
     mbar_init(BAR_PE, 1);
     mbar_init(BAR_DQF, 1);
     mbar_init(BAR_DQE, C::NDRAIN);
-    mbar_init(BAR_DSF, C::NDRAIN);
-    mbar_init(BAR_DSE, 1);
+    for (int b = 0; b < C::DQSB; ++b) {
+      mbar_init(BAR_DSF(b), C::NDRAIN);
+      mbar_init(BAR_DSE(b), 1);
+    }
     mbar_init(BAR_DONE, 1);
     mbar_init(BAR_ACC, C::NDRAIN);
     mbar_init(BAR_NEVER, 1);
@@ -489,38 +496,58 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
       }
     } else if (warp == 2) {
       // ------------------------------------------------------- statistics
-      for (StepIter s = first_step(prm); s.valid; advance(prm, s)) {
-        const int st = s.t % SSTAGES;
-        if (s.t >= SSTAGES && !mbar_wait_warp(BAR_TE(st), ((s.t / SSTAGES) - 1) & 1, abort_p)) break;
+      // A step's 128 (-l*log2e, -D/sqrt(D)) pairs, four queries per lane,
+      // are loaded into registers one step ahead, so the ring slot is filled
+      // as soon as the compute warps free it, whatever the load latency.
+      float nl[4], nd[4];
+      auto load_stats = [&](const StepIter& s) {
         const int qt = s.u.kt + s.i;
         const long long rbase = (long long)s.u.b * prm.T;
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          const int q = qt * BQ + lane * 4 + v;
+          nl[v] = 0.0f;
+          nd[v] = 0.0f;
+          if (q < prm.T) {
+            const long long si = (rbase + q) * prm.NH + s.u.h;
+            nl[v] = -__ldg(prm.lse + si) * LOG2E;
+            nd[v] = -__bfloat162float(prm.Dv[si]) * prm.scale;
+          }
+        }
+      };
+      StepIter s = first_step(prm);
+      if (s.valid) load_stats(s);
+      while (s.valid) {
+        const float cl[4] = {nl[0], nl[1], nl[2], nl[3]};
+        const float cd[4] = {nd[0], nd[1], nd[2], nd[3]};
+        StepIter nx = s;
+        advance(prm, nx);
+        if (nx.valid) load_stats(nx);  // the next step's, in flight while this one waits
+        const int st = s.t % C::SSTG;
+        if (s.t >= C::SSTG && !mbar_wait_warp(BAR_TE(st), ((s.t / C::SSTG) - 1) & 1, abort_p)) break;
         float* stt = stat_base + st * (2 * BQ);
 #pragma unroll
         for (int v = 0; v < 4; ++v) {
-          const int qi = lane * 4 + v;
-          const int q = qt * BQ + qi;
-          float nl = 0.0f, nd = 0.0f;
-          if (q < prm.T) {
-            const long long si = (rbase + q) * prm.NH + s.u.h;
-            nl = -__ldg(prm.lse + si) * LOG2E;
-            nd = -__bfloat162float(prm.Dv[si]) * prm.scale;
-          }
-          stt[qi] = nl;
-          stt[BQ + qi] = nd;
+          stt[lane * 4 + v] = cl[v];
+          stt[BQ + lane * 4 + v] = cd[v];
         }
         mbar_arrive(BAR_TF(st));
+        s = nx;
       }
     } else {
       // ------------------------------------------------- dQ reduce issuer
       if (lane == 0) {
         for (StepIter s = first_step(prm); s.valid; advance(prm, s)) {
-          if (!mbar_wait(BAR_DSF, s.t & 1, abort_p)) break;
+          const int b = s.t % C::DQSB;
+          if (!mbar_wait(BAR_DSF(b), (s.t / C::DQSB) & 1, abort_p)) break;
           for (int box = 0; box < HD / 32; ++box)
-            tma_reduce_add_3d(&tmdQ, sbase + C::OFF_DQS + box * (BQ * 128), s.u.h * HD + box * 32,
-                              (s.u.kt + s.i) * BQ, s.u.b);
+            tma_reduce_add_3d(&tmdQ, sbase + C::OFF_DQS + b * C::DQS_BYTES + box * (BQ * 128),
+                              s.u.h * HD + box * 32, (s.u.kt + s.i) * BQ, s.u.b);
           bulk_commit();
-          bulk_wait_read<0>();  // the staging buffer may be rewritten
-          mbar_arrive(BAR_DSE);
+          // the reduction DQSB-1 steps back has read its buffer, which may
+          // now be rewritten (with one buffer: this step's)
+          bulk_wait_read<C::DQSB - 1>();
+          if (s.t + 1 >= (uint32_t)C::DQSB) mbar_arrive(BAR_DSE((s.t + 1 - C::DQSB) % C::DQSB));
         }
         bulk_wait<0>();
       }
@@ -541,12 +568,13 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
     // boxes); the reduce issuer (warp 3) sends it to global memory.  Each
     // part drains HD / NPART of the head dimension's columns.
     auto drain_dq = [&](uint32_t t) {
+      const int b = t % C::DQSB;
       if (ok) ok = mbar_wait_warp(BAR_DQF, t & 1, abort_p);
-      if (ok && t >= 1) ok = mbar_wait_warp(BAR_DSE, (t - 1) & 1, abort_p);
+      if (ok && t >= (uint32_t)C::DQSB) ok = mbar_wait_warp(BAR_DSE(b), ((t / C::DQSB) - 1) & 1, abort_p);
       if (!ok) return;
       tc_fence_after();
       constexpr int CPH = HD / C::NPART;  // dQ columns per part
-      uint8_t* dqs = gbase + C::OFF_DQS;
+      uint8_t* dqs = gbase + C::OFF_DQS + b * C::DQS_BYTES;
 #pragma unroll
       for (int cc = 0; cc < CPH; cc += 16) {
         uint32_t r[16];
@@ -564,7 +592,7 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
       tc_fence_before();
       mbar_arrive(BAR_DQE);
       fence_proxy_async_smem();
-      mbar_arrive(BAR_DSF);
+      mbar_arrive(BAR_DSF(b));
     };
 
     // dK/dV of unit v (its UMMAs complete, BAR_DONE phase vuc): TMEM ->
@@ -621,7 +649,7 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
       const int i = st_it.i;
       t = st_it.t;
       uc = st_it.uc;
-      const int ss = t % SSTAGES;
+      const int ss = t % C::SSTG;
       ok = mbar_wait_warp(BAR_SF, t & 1, abort_p);
       if (!ok) break;
       tc_fence_after();
@@ -658,7 +686,7 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
       }
       tc_fence_before();
       mbar_arrive(BAR_SE);
-      ok = mbar_wait_warp(BAR_TF(ss), (t / SSTAGES) & 1, abort_p);
+      ok = mbar_wait_warp(BAR_TF(ss), (t / C::SSTG) & 1, abort_p);
       if (!ok) break;
       const float* stt = stat_base + ss * (2 * BQ) + part * CPP;
       if (i == 0) p_ds_row<true, CPP>(s, dp, stt, stt + BQ, c, sc, krow, part * CPP);
@@ -667,7 +695,7 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
       // the previous step's UMMAs must be done with P^T/dS^T, and when the dQ
       // staging shares their smem its reduction must have read it
       if (t >= 1) ok = mbar_wait_warp(BAR_PE, (t - 1) & 1, abort_p);
-      if (ok && C::DQS_ALIAS && t >= 1) ok = mbar_wait_warp(BAR_DSE, (t - 1) & 1, abort_p);
+      if (ok && C::DQS_ALIAS && t >= 1) ok = mbar_wait_warp(BAR_DSE(0), (t - 1) & 1, abort_p);
       if (!ok) break;
       // this part's columns of the key row: P^T (bf16 pairs in TMEM, or smem),
       // dS^T (smem); chunk (part*CPP % 64) / 8 of 64-column block part*CPP / 64
@@ -710,14 +738,16 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const uint32_t tl = tmem + ((uint32_t)(quarter * 32) << 16);
-    uint8_t* dqs = gbase + C::OFF_DQS;
     bool ok = true;
     for (StepIter s = first_step(prm); ok && s.valid; advance(prm, s)) {
       const uint32_t t = s.t;
-      // dQ of step t: TMEM -> fp32 staging (128-byte swizzle, 32-column
+      const int b = t % C::DQSB;
+      uint8_t* dqs = gbase + C::OFF_DQS + b * C::DQS_BYTES;
+      {
+      // dQ of step t: TMEM -> fp32 staging b (128-byte swizzle, 32-column
       // boxes); the reduce issuer (warp 3) adds it into global dQ
       ok = mbar_wait_warp(BAR_DQF, t & 1, abort_p);
-      if (ok && t >= 1) ok = mbar_wait_warp(BAR_DSE, (t - 1) & 1, abort_p);
+      if (ok && t >= (uint32_t)C::DQSB) ok = mbar_wait_warp(BAR_DSE(b), ((t / C::DQSB) - 1) & 1, abort_p);
       if (!ok) break;
       tc_fence_after();
 #pragma unroll
@@ -736,7 +766,8 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
       tc_fence_before();
       mbar_arrive(BAR_DQE);
       fence_proxy_async_smem();
-      mbar_arrive(BAR_DSF);
+      mbar_arrive(BAR_DSF(b));
+      }
       if (s.i + 1 == s.u.nq) {
         // the unit's dK/dV (all its UMMAs complete): TMEM -> bf16 -> this
         // key row's slices in global memory (rows past T are not stored),
