@@ -400,9 +400,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int nt = x == 0 ? un.nA : un.nB;
       if (nt == 0) continue;
       const int qtile = 2 * un.pair + x;
-      // the previous unit's O store must have read the P buffer (its staging)
-      if (sc >= 1 && wg_leader) bulk_wait_read<0>();
-      bar_sync_named(wg_bar, 128);
+      // the previous unit's O store must have read the staging before it is
+      // written again: at D=128 it holds P from this unit's first tile on, so
+      // wait here; at D=64 (P in TMEM) it is next written by this unit's dO
+      // load or epilogue, which wait there instead, so this unit's first
+      // tiles overlap the store
+      if constexpr (!C::P_TMEM) {
+        if (sc >= 1 && wg_leader) bulk_wait_read<0>();
+        bar_sync_named(wg_bar, 128);
+      }
       float m_used = -INFINITY, l_sum = 0.0f;
       // one key tile; DIAG: the diagonal tile (keys after the query masked).
       // Instantiated twice so that the other tiles carry no masking code.
@@ -413,6 +419,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           // staging (idle until the epilogue; rows past T read as zero); the
           // epilogue reads each chunk back before writing O over it
           if (prm.dO && wg_leader) {
+            bulk_wait_read<0>();  // the previous unit's O store has read the staging
             mbar_arrive_expect_tx(BAR_DO(x), BM * HD * 2);
             ++nd_armed;
             for (int kb = 0; kb < C::KB; ++kb)
@@ -531,6 +538,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         ok = (j == qtile) ? tile(std::true_type{}, j) : tile(std::false_type{}, j);
       // --------------------------------------------- epilogue of tile X
       const bool epi = ok && mbar_wait_warp(BAR_PV(x), (sc - 1) & 1, abort_p);
+      if constexpr (C::P_TMEM) {
+        // without dO the epilogue is the staging's first writer in this unit
+        // (with dO the warpgroup waits for the dO load, issued after the wait)
+        if (!prm.dO) {
+          if (wg_leader) bulk_wait_read<0>();
+          bar_sync_named(wg_bar, 128);
+        }
+      }
       if (epi) {
         tc_fence_after();
         const float inv = 1.0f / l_sum;
