@@ -42,8 +42,11 @@
 //     warp 3   lane 0 issues the dQ bulk reductions
 //   warpgroups 1, 2 (192 registers): compute, thread = key row = TMEM lane;
 //              warpgroup 1 takes query columns 0-63, warpgroup 2 columns
-//              64-127; dQ drain into the staging buffer and dK/dV epilogue
-//              (each thread stores its key row's slice).
+//              64-127; the dK/dV epilogue (each thread stores its key row's
+//              slice of its part's columns) and, at D=128, the dQ drain into
+//              the staging buffer.
+// At D=64 a fourth warpgroup (warps 12-15, 64 registers) drains dQ, and the
+// CTA has 512 threads (warpgroup 0 80 registers, compute 184).
 // D=64 schedule ("early S"): S^T/dP^T of the next query tile are issued as
 // soon as the compute warps have read the current one, so they run on the
 // tensor core while the compute warps form P^T/dS^T; dV, dK and dQ follow, and
@@ -80,12 +83,11 @@ struct BwdCfg {
   static constexpr int KB = HD / 64;
   static constexpr bool D64 = HD == 64;
   // Compute warpgroups: each takes BQ / NPART query columns of every step.
-  // D=64 with NPART=2: a fourth warpgroup drains dQ and stores dK/dV, so the
-  // compute warpgroups only form P^T and dS^T (register split per thread
-  // after setmaxnreg: warpgroup 0 80, compute 184, drain 64).  Otherwise the
-  // compute warpgroups also drain dQ and store dK/dV, each its share of the
-  // columns: D=64 with NPART=4 (640 threads; 64 / 104), D=128 (384 threads;
-  // 120 / 192).
+  // D=64 with NPART=2: a fourth warpgroup drains dQ (register split per
+  // thread after setmaxnreg: warpgroup 0 80, compute 184, drain 64).
+  // Otherwise the compute warpgroups also drain dQ, each its share of the
+  // columns: D=64 with NPART=4 (640 threads; 64 / 104; measured slower and
+  // not used), D=128 (384 threads; 120 / 192).
   static constexpr int NPART = 2;
   static constexpr int CPP = BQ / NPART;       // query columns per part
   static constexpr int NCOMP = 128 * NPART;    // compute threads
@@ -96,7 +98,15 @@ struct BwdCfg {
   static constexpr int REGS_DRAIN = DRAIN_WG ? 64 : 0;
   static constexpr int REGS_COMPUTE =
       ((NUM_THREADS * LAUNCH_REGS - 128 * REGS_PRODUCER - 128 * REGS_DRAIN) / NCOMP) & ~7;
-  static constexpr int NDRAIN = DRAIN_WG ? 128 : NCOMP;  // arrivals on DQE, DSF, ACC
+  static constexpr int NDRAIN = DRAIN_WG ? 128 : NCOMP;  // arrivals on DQE, DSF
+  // The unit's dK/dV epilogue (TMEM -> bf16 -> global memory) is run by the
+  // compute warps, each part its columns, once they have handed the next
+  // unit's first step to the tensor core: they would otherwise wait there for
+  // the step's products, and with all of them the accumulators are released
+  // sooner than by the drain warpgroup alone.
+  static constexpr bool EPI_COMPUTE = true;
+  static_assert(EPI_COMPUTE, "the drain warpgroup drains dQ only");
+  static constexpr int NACC = EPI_COMPUTE ? NCOMP : NDRAIN;  // arrivals on ACC
   static_assert(128 * REGS_PRODUCER + NCOMP * REGS_COMPUTE + 128 * REGS_DRAIN <=
                     NUM_THREADS * LAUNCH_REGS,
                 "register split must fit the launch allocation");
@@ -338,7 +348,7 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
       mbar_init(BAR_DSE(b), 1);
     }
     mbar_init(BAR_DONE, 1);
-    mbar_init(BAR_ACC, C::NDRAIN);
+    mbar_init(BAR_ACC, C::NACC);
     mbar_init(BAR_NEVER, 1);
     mbar_init(BAR_FIN, 1);
     fence_mbar_init();
@@ -720,21 +730,21 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
         } else {
           drain_dq(t);
         }
+      }
+      if constexpr (C::EPI_COMPUTE) {
         if (i == 0 && have_prev) epilogue(prev, uc - 1);
         prev = u;
         have_prev = true;
       }
     }
-    if constexpr (!C::DRAIN_WG) {
-      if (ok && have_prev) {  // the last unit of this CTA
-        if (C::EARLY_S) drain_dq(t);
-        epilogue(prev, uc);
-      }
+    if (ok && have_prev) {  // the last unit of this CTA
+      if constexpr (!C::DRAIN_WG && C::EARLY_S) drain_dq(t);
+      if constexpr (C::EPI_COMPUTE) epilogue(prev, uc);
     }
   } else {
     reg_dealloc<C::REGS_DRAIN>();
-    // ------------------------------------------- dQ drain, dK/dV epilogue
-    // (D=64, warps 12-15): thread = TMEM lane = dQ query row = key row
+    // ---------------------------------------------------------- dQ drain
+    // (D=64, warps 12-15): thread = TMEM lane = dQ query row
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const uint32_t tl = tmem + ((uint32_t)(quarter * 32) << 16);
@@ -743,7 +753,6 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
       const uint32_t t = s.t;
       const int b = t % C::DQSB;
       uint8_t* dqs = gbase + C::OFF_DQS + b * C::DQS_BYTES;
-      {
       // dQ of step t: TMEM -> fp32 staging b (128-byte swizzle, 32-column
       // boxes); the reduce issuer (warp 3) adds it into global dQ
       ok = mbar_wait_warp(BAR_DQF, t & 1, abort_p);
@@ -767,43 +776,6 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
       mbar_arrive(BAR_DQE);
       fence_proxy_async_smem();
       mbar_arrive(BAR_DSF(b));
-      }
-      if (s.i + 1 == s.u.nq) {
-        // the unit's dK/dV (all its UMMAs complete): TMEM -> bf16 -> this
-        // key row's slices in global memory (rows past T are not stored),
-        // then the accumulators are released to the next unit
-        ok = mbar_wait_warp(BAR_DONE, s.uc & 1, abort_p);
-        if (!ok) break;
-        tc_fence_after();
-        const int key = s.u.kt * BK + row;
-        const long long off = ((long long)s.u.b * prm.T + key) * prm.N + s.u.h * HD;
-#pragma unroll
-        for (int which = 0; which < 2; ++which) {
-          uint4* dst = reinterpret_cast<uint4*>((which == 0 ? dV : dK) + off);
-          const uint32_t tcol = which == 0 ? C::TCOL_DV : C::TCOL_DK;
-#pragma unroll
-          for (int cc = 0; cc < HD; cc += 16) {
-            uint32_t r[16];
-            tmem_ld16(tl + tcol + cc, r);
-            tmem_wait_ld_dep(r);
-            if (key < prm.T) {
-              uint4 w0, w1;
-              w0.x = pack_bf16(__uint_as_float(r[0]), __uint_as_float(r[1]));
-              w0.y = pack_bf16(__uint_as_float(r[2]), __uint_as_float(r[3]));
-              w0.z = pack_bf16(__uint_as_float(r[4]), __uint_as_float(r[5]));
-              w0.w = pack_bf16(__uint_as_float(r[6]), __uint_as_float(r[7]));
-              w1.x = pack_bf16(__uint_as_float(r[8]), __uint_as_float(r[9]));
-              w1.y = pack_bf16(__uint_as_float(r[10]), __uint_as_float(r[11]));
-              w1.z = pack_bf16(__uint_as_float(r[12]), __uint_as_float(r[13]));
-              w1.w = pack_bf16(__uint_as_float(r[14]), __uint_as_float(r[15]));
-              dst[cc / 8] = w0;
-              dst[cc / 8 + 1] = w1;
-            }
-          }
-        }
-        tc_fence_before();
-        mbar_arrive(BAR_ACC);
-      }
     }
   }
 
