@@ -207,10 +207,12 @@ def time_split(ctx, A, cfg, steps, warmup, seed, peak):
     def step(ev=None):
         if ev is not None:
             ev[0].record(st)
-        A.flashAttentionForwardComputeD(q, k, v, do, p, Bl, out=out, l=l, D=Dv, shard=shard, stream=st)
+        A.flashAttentionForwardComputeD(q, k, v, do, p, Bl, out=out, l=l, D=Dv, shard=shard, stream=st,
+                                        zero_dQ=dQ)
         if ev is not None:
             ev[1].record(st)
-        A.flashAttentionBackward(do, Dv, l, q, k, v, p, Bl, dQ=dQ, dK=dK, dV=dV, shard=shard, stream=st)
+        A.flashAttentionBackward(do, Dv, l, q, k, v, p, Bl, dQ=dQ, dK=dK, dV=dV, shard=shard, stream=st,
+                                 accumulate_dQ=True)
         if ev is not None:
             ev[2].record(st)
 
@@ -357,16 +359,21 @@ def run_gpu(args):
 
     # dO is an input of this attention-only step, so computeD rides in the
     # forward's epilogue (ma_flashAttentionForwardComputeD; at d=128 it is
-    # the separate kernel right after the forward)
+    # the separate kernel right after the forward), and the forward also
+    # writes the zeros the backward then adds dQ into (the reference's dQ
+    # contract; ma_flashAttentionForwardComputeDZeroDQ +
+    # ma_flashAttentionBackwardAccumulate), instead of a separate zeroing
+    # pass over dQ before the backward
     def step(ev=None):
         if ev is not None:
             ev[0].record(stream)
-        A.flashAttentionForwardComputeD(q, k, v, do, p, Bl, out=out, l=l, D=Dv, shard=shard, stream=stream)
+        A.flashAttentionForwardComputeD(q, k, v, do, p, Bl, out=out, l=l, D=Dv, shard=shard, stream=stream,
+                                        zero_dQ=dQ)
         if ev is not None:
             ev[1].record(stream)
             ev[2].record(stream)
         A.flashAttentionBackward(do, Dv, l, q, k, v, p, Bl, dQ=dQ, dK=dK, dV=dV, shard=shard,
-                                 stream=stream)
+                                 stream=stream, accumulate_dQ=True)
         if ev is not None:
             ev[3].record(stream)
 

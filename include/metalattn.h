@@ -234,6 +234,44 @@ MA_API int ma_model_status(ma_model* model, uint32_t* status);
 /* Text for the last error of a ma_model_* call on the calling thread. */
 MA_API const char* ma_model_last_error(void);
 
+/* The pair ma_flashAttentionForwardComputeDZeroDQ + ma_flashAttentionBackwardAccumulate
+ * is ma_flashAttentionForwardComputeD + ma_flashAttentionBackward with dQ
+ * handled as the reference handles it: its backward adds each key tile's
+ * contribution into dQ (attention.metal:292-296), which its host zeroes
+ * first (model.h:549-551).  ma_flashAttentionBackward zeroes dQ itself, a
+ * separate pass over the whole fp32 tensor (201 MB at config 2) before the
+ * kernel; here the forward writes those zeros instead, each thread for the
+ * query row it computes, overlapped with its work.  Results equal the
+ * separate calls (dQ to fp32 rounding, as between any two runs).
+ *
+ * ForwardComputeDZeroDQ: as ma_flashAttentionForwardComputeD, and it also
+ * writes zeros to dQ (fp32 [B][M][N], 16-byte aligned) for every (row, head)
+ * it computes (the shard's, for _shard).  No counterpart in the reference
+ * (the reference zeroes dQ on the host, model.h:549-551). */
+MA_API int ma_flashAttentionForwardComputeDZeroDQ(const ma_bf16* q, const ma_bf16* k, const ma_bf16* v,
+                                                  const ma_bf16* dO, ma_bf16* out, float* l, ma_bf16* D,
+                                                  float* dQ, const AttentionParams* p, uint32_t B,
+                                                  ma_stream_t stream);
+MA_API int ma_flashAttentionForwardComputeDZeroDQ_shard(const ma_bf16* q, const ma_bf16* k,
+                                                        const ma_bf16* v, const ma_bf16* dO, ma_bf16* out,
+                                                        float* l, ma_bf16* D, float* dQ,
+                                                        const AttentionParams* p, uint32_t B,
+                                                        uint32_t bh_begin, uint32_t bh_end,
+                                                        ma_stream_t stream);
+/* flashAttentionBackward with the reference's dQ contract
+ * (attention.metal:198-211, 292-296): dQ += the backward's dQ, so dQ must
+ * hold zeros (or earlier partial sums) on entry; dK and dV are written as by
+ * ma_flashAttentionBackward.  Same arguments and limits. */
+MA_API int ma_flashAttentionBackwardAccumulate(const ma_bf16* dZ, const ma_bf16* d, const float* l,
+                                               const ma_bf16* q, const ma_bf16* k, const ma_bf16* v,
+                                               float* dQ, ma_bf16* dK, ma_bf16* dV,
+                                               const AttentionParams* p, uint32_t B, ma_stream_t stream);
+MA_API int ma_flashAttentionBackwardAccumulate_shard(const ma_bf16* dZ, const ma_bf16* d, const float* l,
+                                                     const ma_bf16* q, const ma_bf16* k, const ma_bf16* v,
+                                                     float* dQ, ma_bf16* dK, ma_bf16* dV,
+                                                     const AttentionParams* p, uint32_t B,
+                                                     uint32_t bh_begin, uint32_t bh_end, ma_stream_t stream);
+
 /* Allocation-free backward pass: computeD followed by flashAttentionBackward,
  * for callers that cannot let a library allocate device memory (hosts whose
  * own arena or caching allocator owns all of the GPU's memory, processes under

@@ -53,6 +53,10 @@ SIGNATURES = {
     "ma_flashAttentionForwardComputeD": [_P, _P, _P, _P, _P, _P, _P, _PP, _U32, _P],
     "ma_flashAttentionForwardComputeD_shard": [_P, _P, _P, _P, _P, _P, _P, _PP, _U32, _U32, _U32, _P],
     "ma_flashAttentionBackward": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _PP, _U32, _P],
+    "ma_flashAttentionBackwardAccumulate": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _PP, _U32, _P],
+    "ma_flashAttentionBackwardAccumulate_shard": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _PP, _U32, _U32, _U32, _P],
+    "ma_flashAttentionForwardComputeDZeroDQ": [_P, _P, _P, _P, _P, _P, _P, _P, _PP, _U32, _P],
+    "ma_flashAttentionForwardComputeDZeroDQ_shard": [_P, _P, _P, _P, _P, _P, _P, _P, _PP, _U32, _U32, _U32, _P],
     "ma_flashAttentionForward_shard": [_P, _P, _P, _P, _P, _PP, _U32, _U32, _U32, _P],
     "ma_computeD_shard": [_P, _P, _P, _PP, _U32, _U32, _U32, _P],
     "ma_flashAttentionBackward_shard": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _PP, _U32, _U32, _U32, _P],

@@ -204,17 +204,30 @@ def flashAttentionForward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, p: 
 def flashAttentionForwardComputeD(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, dO: torch.Tensor,
                                   p: AttentionParams, B: int, out: Optional[torch.Tensor] = None,
                                   l: Optional[torch.Tensor] = None, D: Optional[torch.Tensor] = None,
-                                  shard: Optional[tuple] = None, stream: Optional[torch.cuda.Stream] = None):
+                                  shard: Optional[tuple] = None, stream: Optional[torch.cuda.Stream] = None,
+                                  zero_dQ: Optional[torch.Tensor] = None):
     """out, l, D = flashAttentionForward then computeD(dO, out), for callers
     that know dO before the forward (ma_flashAttentionForwardComputeD; at
-    head size 64 D is formed in the forward's epilogue)."""
+    head size 64 D is formed in the forward's epilogue).  With zero_dQ (fp32
+    [B, T, N]) the forward also writes zeros to it for every (row, head) it
+    computes (ma_flashAttentionForwardComputeDZeroDQ), for a following
+    flashAttentionBackward(..., accumulate_dQ=True)."""
     act = (B, p.M, p.N)
     for t, n in ((q, "q"), (k, "k"), (v, "v"), (dO, "dO")):
         _check(t, n, torch.bfloat16, act)
     out = _out(out, q, act, torch.bfloat16, "out")
     l = _out(l, q, (B, p.M, p.NH), torch.float32, "l")
     D = _out(D, q, (B, p.M, p.NH), torch.bfloat16, "D")
-    if shard is None:
+    if zero_dQ is not None:
+        _check(zero_dQ, "zero_dQ", torch.float32, act)
+        name = "ma_flashAttentionForwardComputeDZeroDQ"
+        args = (_ptr(q), _ptr(k), _ptr(v), _ptr(dO), _ptr(out), _ptr(l), _ptr(D), _ptr(zero_dQ),
+                ctypes.byref(p), B)
+        if shard is None:
+            _lib.call(name, *args, _stream(stream))
+        else:
+            _lib.call(name + "_shard", *args, shard[0], shard[1], _stream(stream))
+    elif shard is None:
         _lib.call("ma_flashAttentionForwardComputeD", _ptr(q), _ptr(k), _ptr(v), _ptr(dO), _ptr(out), _ptr(l),
                   _ptr(D), ctypes.byref(p), B, _stream(stream))
     else:
@@ -243,22 +256,28 @@ def flashAttentionBackward(dZ: torch.Tensor, d: torch.Tensor, l: torch.Tensor, q
                            k: torch.Tensor, v: torch.Tensor, p: AttentionParams, B: int,
                            dQ: Optional[torch.Tensor] = None, dK: Optional[torch.Tensor] = None,
                            dV: Optional[torch.Tensor] = None, shard: Optional[tuple] = None,
-                           stream: Optional[torch.cuda.Stream] = None):
-    """dQ (fp32), dK, dV (bf16) of causal attention (attention.metal:198-299)."""
+                           stream: Optional[torch.cuda.Stream] = None, accumulate_dQ: bool = False):
+    """dQ (fp32), dK, dV (bf16) of causal attention (attention.metal:198-299).
+    With accumulate_dQ, dQ (given) is added to, as the reference's kernel
+    adds into a dQ its host zeroed (ma_flashAttentionBackwardAccumulate);
+    otherwise dQ is written."""
     act = (B, p.M, p.N)
     for t, n in ((dZ, "dZ"), (q, "q"), (k, "k"), (v, "v")):
         _check(t, n, torch.bfloat16, act)
     _check(d, "d", torch.bfloat16, (B, p.M, p.NH))
     _check(l, "l", torch.float32, (B, p.M, p.NH))
+    if accumulate_dQ and dQ is None:
+        raise ValueError("accumulate_dQ needs the dQ tensor to add into")
     dQ = _out(dQ, q, act, torch.float32, "dQ")
     dK = _out(dK, q, act, torch.bfloat16, "dK")
     dV = _out(dV, q, act, torch.bfloat16, "dV")
     args = (_ptr(dZ), _ptr(d), _ptr(l), _ptr(q), _ptr(k), _ptr(v), _ptr(dQ), _ptr(dK), _ptr(dV),
             ctypes.byref(p), B)
+    name = "ma_flashAttentionBackwardAccumulate" if accumulate_dQ else "ma_flashAttentionBackward"
     if shard is None:
-        _lib.call("ma_flashAttentionBackward", *args, _stream(stream))
+        _lib.call(name, *args, _stream(stream))
     else:
-        _lib.call("ma_flashAttentionBackward_shard", *args, shard[0], shard[1], _stream(stream))
+        _lib.call(name + "_shard", *args, shard[0], shard[1], _stream(stream))
     return dQ, dK, dV
 
 

@@ -135,7 +135,8 @@ using bf16m = __nv_bfloat16*;
 
 int forward_impl(const ma_bf16* q, const ma_bf16* k, const ma_bf16* v, ma_bf16* out, float* l,
                  const AttentionParams* p, uint32_t B, uint32_t b0, uint32_t b1, bool range,
-                 ma_stream_t stream, const ma_bf16* dO = nullptr, ma_bf16* D = nullptr) {
+                 ma_stream_t stream, const ma_bf16* dO = nullptr, ma_bf16* D = nullptr,
+                 float* dQ = nullptr, bool want_dqz = false) {
   ma::AttnShape s;
   int rc = check_shape(p, B, b0, b1, range, &s);
   if (rc) return rc;
@@ -150,6 +151,7 @@ int forward_impl(const ma_bf16* q, const ma_bf16* k, const ma_bf16* v, ma_bf16* 
     if (!D) return fail(MA_ERR_NULL, "pointer 'D' is NULL");
     if (reinterpret_cast<uintptr_t>(D) & 1u) return fail(MA_ERR_ALIGN, "pointer 'D' is not 2-byte aligned");
   }
+  if (want_dqz) MA_REQUIRE_PTR(dQ);  // the forward writes zeros to it
   uint32_t* status = nullptr;
   rc = device_status_word(&status);
   if (rc) return rc;
@@ -160,7 +162,7 @@ int forward_impl(const ma_bf16* q, const ma_bf16* k, const ma_bf16* v, ma_bf16* 
   cudaError_t e = ma::launch_flash_fwd(reinterpret_cast<bf16p>(q), reinterpret_cast<bf16p>(k),
                                        reinterpret_cast<bf16p>(v), reinterpret_cast<bf16m>(out), l, s,
                                        status, st, fused ? reinterpret_cast<bf16p>(dO) : nullptr,
-                                       fused ? reinterpret_cast<bf16m>(D) : nullptr);
+                                       fused ? reinterpret_cast<bf16m>(D) : nullptr, want_dqz ? dQ : nullptr);
   if (e != cudaSuccess) return cuda_fail(e, "flashAttentionForward launch");
   if (with_d && !fused) {
     e = ma::launch_compute_d(reinterpret_cast<bf16p>(dO), reinterpret_cast<bf16p>(out), reinterpret_cast<bf16m>(D),
@@ -193,7 +195,7 @@ int compute_d_impl(const ma_bf16* dO, const ma_bf16* O, ma_bf16* D, const Attent
 int backward_impl(const ma_bf16* dZ, const ma_bf16* d, const float* l, const ma_bf16* q,
                   const ma_bf16* k, const ma_bf16* v, float* dQ, ma_bf16* dK, ma_bf16* dV,
                   const AttentionParams* p, uint32_t B, uint32_t b0, uint32_t b1, bool range,
-                  ma_stream_t stream) {
+                  ma_stream_t stream, bool accumulate_dq = false) {
   ma::AttnShape s;
   int rc = check_shape(p, B, b0, b1, range, &s);
   if (rc) return rc;
@@ -214,7 +216,7 @@ int backward_impl(const ma_bf16* dZ, const ma_bf16* d, const float* l, const ma_
   cudaError_t e = ma::launch_flash_bwd(
       reinterpret_cast<bf16p>(dZ), reinterpret_cast<bf16p>(d), l, reinterpret_cast<bf16p>(q),
       reinterpret_cast<bf16p>(k), reinterpret_cast<bf16p>(v), dQ, reinterpret_cast<bf16m>(dK),
-      reinterpret_cast<bf16m>(dV), s, status, reinterpret_cast<cudaStream_t>(stream));
+      reinterpret_cast<bf16m>(dV), s, status, reinterpret_cast<cudaStream_t>(stream), accumulate_dq);
   if (e != cudaSuccess) return cuda_fail(e, "flashAttentionBackward launch");
   return ok();
 }
@@ -274,6 +276,19 @@ int ma_flashAttentionForwardComputeD_shard(const ma_bf16* q, const ma_bf16* k, c
   return forward_impl(q, k, v, out, l, p, B, bh_begin, bh_end, true, stream, dO, D);
 }
 
+int ma_flashAttentionForwardComputeDZeroDQ(const ma_bf16* q, const ma_bf16* k, const ma_bf16* v,
+                                           const ma_bf16* dO, ma_bf16* out, float* l, ma_bf16* D, float* dQ,
+                                           const AttentionParams* p, uint32_t B, ma_stream_t stream) {
+  return forward_impl(q, k, v, out, l, p, B, 0, 0, false, stream, dO, D, dQ, true);
+}
+
+int ma_flashAttentionForwardComputeDZeroDQ_shard(const ma_bf16* q, const ma_bf16* k, const ma_bf16* v,
+                                                 const ma_bf16* dO, ma_bf16* out, float* l, ma_bf16* D,
+                                                 float* dQ, const AttentionParams* p, uint32_t B,
+                                                 uint32_t bh_begin, uint32_t bh_end, ma_stream_t stream) {
+  return forward_impl(q, k, v, out, l, p, B, bh_begin, bh_end, true, stream, dO, D, dQ, true);
+}
+
 int ma_computeD(const ma_bf16* dO, const ma_bf16* O, ma_bf16* D, const AttentionParams* p,
                 uint32_t B, ma_stream_t stream) {
   return compute_d_impl(dO, O, D, p, B, 0, 0, false, stream);
@@ -297,6 +312,21 @@ int ma_flashAttentionBackward_shard(const ma_bf16* dZ, const ma_bf16* d, const f
                                     const AttentionParams* p, uint32_t B, uint32_t bh_begin,
                                     uint32_t bh_end, ma_stream_t stream) {
   return backward_impl(dZ, d, l, q, k, v, dQ, dK, dV, p, B, bh_begin, bh_end, true, stream);
+}
+
+int ma_flashAttentionBackwardAccumulate(const ma_bf16* dZ, const ma_bf16* d, const float* l,
+                                        const ma_bf16* q, const ma_bf16* k, const ma_bf16* v, float* dQ,
+                                        ma_bf16* dK, ma_bf16* dV, const AttentionParams* p, uint32_t B,
+                                        ma_stream_t stream) {
+  return backward_impl(dZ, d, l, q, k, v, dQ, dK, dV, p, B, 0, 0, false, stream, true);
+}
+
+int ma_flashAttentionBackwardAccumulate_shard(const ma_bf16* dZ, const ma_bf16* d, const float* l,
+                                              const ma_bf16* q, const ma_bf16* k, const ma_bf16* v,
+                                              float* dQ, ma_bf16* dK, ma_bf16* dV, const AttentionParams* p,
+                                              uint32_t B, uint32_t bh_begin, uint32_t bh_end,
+                                              ma_stream_t stream) {
+  return backward_impl(dZ, d, l, q, k, v, dQ, dK, dV, p, B, bh_begin, bh_end, true, stream, true);
 }
 
 // ---------------------------------------------------------------- GEMMs
@@ -674,13 +704,16 @@ int pipeline_chunk(ma_host_pipeline* pl, int c, uint32_t b0, uint32_t bc, bool b
   // with the backward, dO is already here: computeD rides in the forward's
   // epilogue at D = 64
   const bool fuse_d = backward && sh.D == 64;
+  // with the backward, the forward also writes the zeros the backward adds
+  // dQ into (no separate zeroing pass over dQ)
   e = ma::launch_flash_fwd(s.q, s.k, s.v, s.out, s.l, sh, status, pl->comp, fuse_d ? s.dO : nullptr,
-                           fuse_d ? s.D : nullptr);
+                           fuse_d ? s.D : nullptr, backward ? s.dQ : nullptr);
   if (e != cudaSuccess) return cuda_fail(e, "host pipeline: flashAttentionForward launch");
   if (backward) {
     if (!fuse_d) e = ma::launch_compute_d(s.dO, s.out, s.D, sh, pl->comp);
     if (e != cudaSuccess) return cuda_fail(e, "host pipeline: computeD launch");
-    e = ma::launch_flash_bwd(s.dO, s.D, s.l, s.q, s.k, s.v, s.dQ, s.dK, s.dV, sh, status, pl->comp);
+    e = ma::launch_flash_bwd(s.dO, s.D, s.l, s.q, s.k, s.v, s.dQ, s.dK, s.dV, sh, status, pl->comp,
+                             /*accumulate_dq=*/true);
     if (e != cudaSuccess) return cuda_fail(e, "host pipeline: flashAttentionBackward launch");
   }
   e = cudaEventRecord(s.comp_done, pl->comp);

@@ -75,15 +75,23 @@ void count_launches(unsigned n);
 cudaError_t launch_compute_d(const __nv_bfloat16* dO, const __nv_bfloat16* O,
                              __nv_bfloat16* Dv, const AttnShape& s, cudaStream_t st);
 // dO, Dv (D = 64 only, both or neither): computeD fused into the epilogue.
+// dQz (optional): the forward also writes zeros to the dQ columns of the
+// shard's rows, for a following backward that accumulates into dQ.
 cudaError_t launch_flash_fwd(const __nv_bfloat16* q, const __nv_bfloat16* k,
                              const __nv_bfloat16* v, __nv_bfloat16* out, float* lse,
                              const AttnShape& s, uint32_t* status, cudaStream_t st,
-                             const __nv_bfloat16* dO = nullptr, __nv_bfloat16* Dv = nullptr);
+                             const __nv_bfloat16* dO = nullptr, __nv_bfloat16* Dv = nullptr,
+                             float* dQz = nullptr);
+// Zeroes the dQ columns of the shard's (batch, head) slabs (a memset for the
+// whole batch).
+cudaError_t launch_zero_dq(float* dQ, const AttnShape& s, cudaStream_t st);
+// accumulate_dq: dQ += the backward's dQ (dQ holds zeros or earlier partial
+// sums on entry); otherwise the launcher zeroes the shard's dQ first.
 cudaError_t launch_flash_bwd(const __nv_bfloat16* dO, const __nv_bfloat16* Dv,
                              const float* lse, const __nv_bfloat16* q,
                              const __nv_bfloat16* k, const __nv_bfloat16* v, float* dQ,
                              __nv_bfloat16* dK, __nv_bfloat16* dV, const AttnShape& s,
-                             uint32_t* status, cudaStream_t st);
+                             uint32_t* status, cudaStream_t st, bool accumulate_dq = false);
 cudaError_t launch_qkv(const __nv_bfloat16* X, __nv_bfloat16* q, __nv_bfloat16* k,
                        __nv_bfloat16* v, const __nv_bfloat16* qw, const __nv_bfloat16* kw,
                        const __nv_bfloat16* vw, int rows, int N, uint32_t* status,

@@ -841,19 +841,14 @@ template <int HD>
 cudaError_t launch_bwd(const __nv_bfloat16* dO, const __nv_bfloat16* Dv, const float* lse,
                        const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* v,
                        float* dQ, __nv_bfloat16* dK, __nv_bfloat16* dV, const AttnShape& s,
-                       uint32_t* status, cudaStream_t st) {
-  // dQ is accumulated by bulk reductions: zero the shard's columns first
+                       uint32_t* status, cudaStream_t st, bool accumulate_dq) {
+  // dQ is accumulated by bulk reductions: zero the shard's columns first,
+  // unless the caller asks for dQ += (it holds zeros or partial sums)
   const int nbh = s.bh_end - s.bh_begin;
-  cudaError_t e;
-  if (s.bh_begin == 0 && s.bh_end == s.B * s.NH) {
-    e = cudaMemsetAsync(dQ, 0, (size_t)s.B * s.T * s.N * sizeof(float), st);
-  } else {
-    launch_pdl(zero_dq_shard_kernel, 1184, 256, 0, st, reinterpret_cast<float4*>(dQ), s.T, s.N, s.D, s.NH,
-                                              s.bh_begin, s.bh_end);
-    count_launches(1);
-    e = cudaGetLastError();
+  if (!accumulate_dq) {
+    const cudaError_t e = launch_zero_dq(dQ, s, st);
+    if (e != cudaSuccess) return e;
   }
-  if (e != cudaSuccess) return e;
   BwdParams prm;
   prm.T = s.T;
   prm.N = s.N;
@@ -881,14 +876,23 @@ cudaError_t launch_bwd(const __nv_bfloat16* dO, const __nv_bfloat16* Dv, const f
 
 }  // namespace
 
+cudaError_t launch_zero_dq(float* dQ, const AttnShape& s, cudaStream_t st) {
+  if (s.bh_begin == 0 && s.bh_end == s.B * s.NH)
+    return cudaMemsetAsync(dQ, 0, (size_t)s.B * s.T * s.N * sizeof(float), st);
+  launch_pdl(zero_dq_shard_kernel, 1184, 256, 0, st, reinterpret_cast<float4*>(dQ), s.T, s.N, s.D, s.NH,
+             s.bh_begin, s.bh_end);
+  count_launches(1);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_flash_bwd(const __nv_bfloat16* dO, const __nv_bfloat16* Dv,
                              const float* lse, const __nv_bfloat16* q,
                              const __nv_bfloat16* k, const __nv_bfloat16* v, float* dQ,
                              __nv_bfloat16* dK, __nv_bfloat16* dV, const AttnShape& s,
-                             uint32_t* status, cudaStream_t st) {
+                             uint32_t* status, cudaStream_t st, bool accumulate_dq) {
   if (s.bh_end <= s.bh_begin) return cudaSuccess;
-  return s.D == 64 ? launch_bwd<64>(dO, Dv, lse, q, k, v, dQ, dK, dV, s, status, st)
-                   : launch_bwd<128>(dO, Dv, lse, q, k, v, dQ, dK, dV, s, status, st);
+  return s.D == 64 ? launch_bwd<64>(dO, Dv, lse, q, k, v, dQ, dK, dV, s, status, st, accumulate_dq)
+                   : launch_bwd<128>(dO, Dv, lse, q, k, v, dQ, dK, dV, s, status, st, accumulate_dq);
 }
 
 }  // namespace ma

@@ -81,7 +81,11 @@ struct FwdCfg {
   static constexpr uint32_t OFF_K = OFF_Q + QST * 2 * QT_BYTES;  // [KST]
   static constexpr uint32_t OFF_V = OFF_K + KST * KV_BYTES;      // [VST]
   static constexpr uint32_t OFF_P = OFF_V + VST * KV_BYTES;      // [2 tiles] P / O staging
-  static constexpr uint32_t OFF_BAR = OFF_P + 2 * STG_BYTES;
+  // D=64: an all-zero fp32 tile (128 rows x 32 columns) that TMA stores copy
+  // into dQ when the forward zeroes it for an accumulating backward
+  static constexpr uint32_t ZT_BYTES = P_TMEM ? BM * 32 * 4 : 0;
+  static constexpr uint32_t OFF_ZT = OFF_P + 2 * STG_BYTES;
+  static constexpr uint32_t OFF_BAR = OFF_ZT + ZT_BYTES;
   // q_full/empty[QST], k_full/empty[KST], v_full/empty[VST], per tile X:
   // s_full, s_free, p_full, pv_done, o_free, do_full; then never (nothing
   // arrives: the time-out test hook) and fin (the UMMA issuer's wind-down)
@@ -105,6 +109,10 @@ struct FwdParams {
   // bf16(sum_c O[row][h*64+c] * dO[row][h*64+c]) from the bf16-rounded O
   const __nv_bfloat16* dO;
   __nv_bfloat16* D;
+  // optional (D=64): zeros are written to dQ's slab of every query tile the
+  // kernel computes (by TMA stores, tensor map tmdQz), for a backward that
+  // then accumulates into dQ
+  float* dQz;
   uint32_t expire_ns;  // time-out test hook (ma_debug_expire_next_wait), 0 = off
 };
 
@@ -157,7 +165,7 @@ template <int HD>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
-                     const __grid_constant__ CUtensorMap tmdO,
+                     const __grid_constant__ CUtensorMap tmdO, const __grid_constant__ CUtensorMap tmdQz,
                      const FwdParams prm) {
   pdl_wait_and_release();
   using C = FwdCfg<HD>;
@@ -216,6 +224,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 1) {
     tmem_alloc(tslot, 512);
     tmem_relinquish();
+  }
+  if (C::ZT_BYTES && prm.dQz) {  // the zero tile the dQ stores copy from
+    for (uint32_t i = threadIdx.x; i < C::ZT_BYTES / 16; i += NUM_THREADS)
+      reinterpret_cast<uint4*>(gbase + C::OFF_ZT)[i] = make_uint4(0u, 0u, 0u, 0u);
+    fence_proxy_async_smem();
   }
   tc_fence_before();
   __syncthreads();
@@ -400,6 +413,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int nt = x == 0 ? un.nA : un.nB;
       if (nt == 0) continue;
       const int qtile = 2 * un.pair + x;
+      if (C::ZT_BYTES && prm.dQz && wg_leader) {
+        // this query tile's dQ slab (128 rows x HD fp32; rows past T are
+        // clipped) from the zero tile, by TMA stores that need no waiting for
+        for (int box = 0; box < HD / 32; ++box)
+          tma_store_3d(&tmdQz, sbase + C::OFF_ZT, un.h * HD + box * 32, qtile * BM, un.b);
+        bulk_commit();
+      }
       // the previous unit's O store must have read the staging before it is
       // written again: at D=128 it holds P from this unit's first tile on, so
       // wait here; at D=64 (P in TMEM) it is next written by this unit's dO
@@ -616,7 +636,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 template <int HD>
 cudaError_t launch_fwd(const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* v,
                        __nv_bfloat16* out, float* lse, const AttnShape& s, uint32_t* status,
-                       cudaStream_t st, const __nv_bfloat16* dO, __nv_bfloat16* Dv) {
+                       cudaStream_t st, const __nv_bfloat16* dO, __nv_bfloat16* Dv, float* dQz) {
   using C = FwdCfg<HD>;
   // The setmaxnreg split assumes the kernel was compiled to exactly
   // LAUNCH_REGS registers per thread; refuse to launch otherwise.
@@ -627,7 +647,7 @@ cudaError_t launch_fwd(const __nv_bfloat16* q, const __nv_bfloat16* k, const __n
     return a.numRegs == LAUNCH_REGS ? cudaSuccess : cudaErrorInvalidKernelImage;
   }();
   if (reg_check != cudaSuccess) return reg_check;
-  CUtensorMap tq, tk, tv, to, tdo;
+  CUtensorMap tq, tk, tv, to, tdo, tdqz;
   const CUtensorMapDataType bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B;
   if (!make_tmap_3d(&tq, q, bf, 2, s.N, s.T, s.B, 64, BM, sw) ||
@@ -639,6 +659,13 @@ cudaError_t launch_fwd(const __nv_bfloat16* q, const __nv_bfloat16* k, const __n
     if (!make_tmap_3d(&tdo, dO, bf, 2, s.N, s.T, s.B, 64, BM, sw)) return cudaErrorInvalidValue;
   } else {
     tdo = tq;  // not read without dO
+  }
+  if (dQz && C::ZT_BYTES) {
+    if (!make_tmap_3d(&tdqz, dQz, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, s.N, s.T, s.B, 32, BM,
+                      CU_TENSOR_MAP_SWIZZLE_128B))
+      return cudaErrorInvalidValue;
+  } else {
+    tdqz = tq;  // not written without dQz
   }
   FwdParams prm;
   prm.T = s.T;
@@ -653,6 +680,7 @@ cudaError_t launch_fwd(const __nv_bfloat16* q, const __nv_bfloat16* k, const __n
   prm.status = status;
   prm.dO = dO;
   prm.D = Dv;
+  prm.dQz = C::ZT_BYTES ? dQz : nullptr;
   prm.expire_ns = take_expire_request(STATUS_FWD_TIMEOUT);
   cudaError_t e = cudaFuncSetAttribute(flash_fwd_kernel<HD>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
@@ -661,7 +689,7 @@ cudaError_t launch_fwd(const __nv_bfloat16* q, const __nv_bfloat16* k, const __n
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int grid = prm.nunits < sms ? prm.nunits : sms;
-  launch_pdl(flash_fwd_kernel<HD>, grid, NUM_THREADS, C::SMEM_BYTES, st, tq, tk, tv, to, tdo, prm);
+  launch_pdl(flash_fwd_kernel<HD>, grid, NUM_THREADS, C::SMEM_BYTES, st, tq, tk, tv, to, tdo, tdqz, prm);
   count_launches(1);
   return cudaGetLastError();
 }
@@ -671,11 +699,17 @@ cudaError_t launch_fwd(const __nv_bfloat16* q, const __nv_bfloat16* k, const __n
 cudaError_t launch_flash_fwd(const __nv_bfloat16* q, const __nv_bfloat16* k,
                              const __nv_bfloat16* v, __nv_bfloat16* out, float* lse,
                              const AttnShape& s, uint32_t* status, cudaStream_t st,
-                             const __nv_bfloat16* dO, __nv_bfloat16* Dv) {
+                             const __nv_bfloat16* dO, __nv_bfloat16* Dv, float* dQz) {
   if (s.bh_end <= s.bh_begin) return cudaSuccess;
   if ((dO == nullptr) != (Dv == nullptr) || (dO && s.D != 64)) return cudaErrorInvalidValue;
-  return s.D == 64 ? launch_fwd<64>(q, k, v, out, lse, s, status, st, dO, Dv)
-                   : launch_fwd<128>(q, k, v, out, lse, s, status, st, nullptr, nullptr);
+  if (s.D == 64) return launch_fwd<64>(q, k, v, out, lse, s, status, st, dO, Dv, dQz);
+  // D=128: no shared memory left for the zero tile; dQ is zeroed by the
+  // separate pass, before the forward
+  if (dQz) {
+    const cudaError_t e = launch_zero_dq(dQz, s, st);
+    if (e != cudaSuccess) return e;
+  }
+  return launch_fwd<128>(q, k, v, out, lse, s, status, st, nullptr, nullptr, nullptr);
 }
 
 }  // namespace ma

@@ -228,3 +228,21 @@ def test_expire_hook_validates_without_device(cuda_lib):
     assert _lib.ERROR_NAMES[cuda_lib.ma_debug_expire_next_wait(_lib.STATUS_BWD_TIMEOUT, 2 * 10 ** 9)] == "MA_ERR_RANGE"
     assert cuda_lib.ma_debug_expire_next_wait(_lib.STATUS_BWD_TIMEOUT, 1000) == 0
     assert cuda_lib.ma_debug_expire_next_wait(0, 0) == 0  # cancels the request
+
+
+def test_zero_dq_and_accumulate_validate_without_device(cuda_lib):
+    """The forward that zeroes dQ refuses a NULL or misaligned dQ, and the
+    accumulating backward validates like ma_flashAttentionBackward, before
+    any device work."""
+    from metalllm_b200 import _lib
+    p = _lib.AttentionParams(256, 128, 64, 2)
+    fake = ctypes.c_void_p(1 << 20)
+    odd = ctypes.c_void_p((1 << 20) + 4)
+    rc = cuda_lib.ma_flashAttentionForwardComputeDZeroDQ(*([fake] * 7), None, ctypes.byref(p), 1, None)
+    assert _lib.ERROR_NAMES[rc] == "MA_ERR_NULL" and b"'dQ'" in cuda_lib.ma_last_error_string()
+    rc = cuda_lib.ma_flashAttentionForwardComputeDZeroDQ(*([fake] * 7), odd, ctypes.byref(p), 1, None)
+    assert _lib.ERROR_NAMES[rc] == "MA_ERR_ALIGN"
+    rc = cuda_lib.ma_flashAttentionBackwardAccumulate(*([fake] * 9), ctypes.byref(_lib.AttentionParams(256, 96, 32, 3)), 1, None)
+    assert _lib.ERROR_NAMES[rc] == "MA_ERR_SHAPE"
+    rc = cuda_lib.ma_flashAttentionBackwardAccumulate_shard(*([fake] * 9), ctypes.byref(p), 1, 0, 3, None)
+    assert _lib.ERROR_NAMES[rc] == "MA_ERR_RANGE"

@@ -314,3 +314,62 @@ def test_full_config_every_shard(A, oracle_mod, cfg):
     for name, got, own, fed in (("dQ", g_dQ, rq, fq), ("dK", g_dK, rk, fk), ("dV", g_dV, rv, fv)):
         allowance = float(np.abs(own - fed).max())
         check(f"{cfg} {name} (oracle chain, allowance {allowance:.2e})", got, own, MAX_ABS + allowance, REL_L2)
+
+
+@pytest.mark.parametrize("B,T,H,D,shard", [(2, 512, 3, 64, None), (3, 200, 2, 64, (1, 5)),
+                                         (2, 130, 3, 128, None), (2, 256, 2, 128, (1, 3))])
+def test_forward_zero_dq_and_accumulating_backward(A, B, T, H, D, shard):
+    """ma_flashAttentionForwardComputeDZeroDQ writes out, l, D bit-identical
+    to ma_flashAttentionForwardComputeD and exact zeros to dQ on the
+    (batch, head) slabs it computes (rows < T), nothing elsewhere;
+    ma_flashAttentionBackwardAccumulate then adds the backward's dQ into
+    dQ (the reference's contract, attention.metal:292-296 with the host
+    zeroing of model.h:549-551) and writes dK, dV bit-identical to
+    ma_flashAttentionBackward."""
+    q, k, v, do = inputs(B, T, H, D, seed=33)
+    p = A.make_params(T, H, D)
+    tq, tk, tv, tdo = up(q), up(k), up(v), up(do)
+    act = (B, T, H * D)
+    nan = lambda shp, dt: torch.full(shp, float("nan"), dtype=dt, device="cuda")
+    r_out, r_l, r_D = nan(act, torch.bfloat16), nan((B, T, H), torch.float32), nan((B, T, H), torch.bfloat16)
+    A.flashAttentionForwardComputeD(tq, tk, tv, tdo, p, B, out=r_out, l=r_l, D=r_D, shard=shard)
+    r_dQ, r_dK, r_dV = nan(act, torch.float32), nan(act, torch.bfloat16), nan(act, torch.bfloat16)
+    A.flashAttentionBackward(tdo, r_D, r_l, tq, tk, tv, p, B, dQ=r_dQ, dK=r_dK, dV=r_dV, shard=shard)
+    out, l, Dv = nan(act, torch.bfloat16), nan((B, T, H), torch.float32), nan((B, T, H), torch.bfloat16)
+    dQ = nan(act, torch.float32)
+    A.flashAttentionForwardComputeD(tq, tk, tv, tdo, p, B, out=out, l=l, D=Dv, shard=shard, zero_dQ=dQ)
+    torch.cuda.synchronize()
+    assert A.device_status() == 0
+    same = lambda a, b: torch.equal(torch.nan_to_num(a.float(), nan=7.0), torch.nan_to_num(b.float(), nan=7.0))
+    assert same(out, r_out) and same(l, r_l) and same(Dv, r_D)
+    lo, hi = shard if shard is not None else (0, B * H)
+    for bh in range(B * H):
+        b, h = divmod(bh, H)
+        slab = dQ[b, :, h * D:(h + 1) * D]
+        if lo <= bh < hi:
+            assert torch.equal(slab, torch.zeros_like(slab))
+        else:
+            assert torch.isnan(slab).all()
+    # the accumulating backward on the zeros: dQ as the writing backward's
+    dK, dV = nan(act, torch.bfloat16), nan(act, torch.bfloat16)
+    A.flashAttentionBackward(tdo, Dv, l, tq, tk, tv, p, B, dQ=dQ, dK=dK, dV=dV, shard=shard,
+                             accumulate_dQ=True)
+    torch.cuda.synchronize()
+    assert same(dK, r_dK) and same(dV, r_dV)
+    for bh in range(lo, hi):
+        b, h = divmod(bh, H)
+        cols = slice(h * D, (h + 1) * D)
+        check(f"dQ[{bh}]", f32(dQ[b, :, cols]), f32(r_dQ[b, :, cols]), 1e-5, 1e-6)
+    # and onto earlier partial sums: dQ = X + the backward's dQ
+    X = torch.randn(act, device="cuda")
+    dQ2 = X.clone()
+    A.flashAttentionBackward(tdo, Dv, l, tq, tk, tv, p, B, dQ=dQ2, shard=shard, accumulate_dQ=True)
+    torch.cuda.synchronize()
+    for bh in range(B * H):
+        b, h = divmod(bh, H)
+        cols = slice(h * D, (h + 1) * D)
+        if lo <= bh < hi:
+            check(f"X+dQ[{bh}]", f32(dQ2[b, :, cols]), f32(X[b, :, cols] + r_dQ[b, :, cols]), 1e-5, 1e-6)
+        else:
+            assert torch.equal(dQ2[b, :, cols], X[b, :, cols])
+    assert A.device_status() == 0
