@@ -574,28 +574,35 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         bool dok = true;
         if (fuse_d) dok = mbar_wait_warp(BAR_DO(x), nd & 1, abort_p);
         float dsum = 0.0f;
-        // stage O (bf16) in this tile's P buffer (free: its last PV is done)
+        // stage O (bf16) in this tile's P buffer (free: its last PV is done);
+        // O is read from TMEM 64 columns (two loads, one wait) at a time
 #pragma unroll
-        for (int cc = 0; cc < HD; cc += 16) {
-          uint32_t r[16];
-          tmem_ld16(trow + tcol_o + cc, r);
-          tmem_wait_ld_dep(r);
-          uint4 v0, v1;
-          v0.x = pack_bf16(__uint_as_float(r[0]) * inv, __uint_as_float(r[1]) * inv);
-          v0.y = pack_bf16(__uint_as_float(r[2]) * inv, __uint_as_float(r[3]) * inv);
-          v0.z = pack_bf16(__uint_as_float(r[4]) * inv, __uint_as_float(r[5]) * inv);
-          v0.w = pack_bf16(__uint_as_float(r[6]) * inv, __uint_as_float(r[7]) * inv);
-          v1.x = pack_bf16(__uint_as_float(r[8]) * inv, __uint_as_float(r[9]) * inv);
-          v1.y = pack_bf16(__uint_as_float(r[10]) * inv, __uint_as_float(r[11]) * inv);
-          v1.z = pack_bf16(__uint_as_float(r[12]) * inv, __uint_as_float(r[13]) * inv);
-          v1.w = pack_bf16(__uint_as_float(r[14]) * inv, __uint_as_float(r[15]) * inv);
-          const int kb = cc / 64, ch = (cc % 64) / 8;
-          uint8_t* blk = pbuf + kb * (BM * 128) + row * 128;
-          uint4* p0 = reinterpret_cast<uint4*>(blk + ((ch ^ (row & 7)) * 16));
-          uint4* p1 = reinterpret_cast<uint4*>(blk + (((ch + 1) ^ (row & 7)) * 16));
-          if (fuse_d) dsum += dot_bf16x8(v0, *p0) + dot_bf16x8(v1, *p1);  // dO, then O over it
-          *p0 = v0;
-          *p1 = v1;
+        for (int c64 = 0; c64 < HD; c64 += 64) {
+          uint32_t ra[32], rb[32];
+          tmem_ld32(trow + tcol_o + c64, ra);
+          tmem_ld32(trow + tcol_o + c64 + 32, rb);
+          tmem_wait_ld_dep(ra, rb);
+#pragma unroll
+          for (int c16 = 0; c16 < 64; c16 += 16) {
+            const uint32_t* r = c16 < 32 ? ra + c16 : rb + (c16 - 32);
+            const int cc = c64 + c16;
+            uint4 v0, v1;
+            v0.x = pack_bf16(__uint_as_float(r[0]) * inv, __uint_as_float(r[1]) * inv);
+            v0.y = pack_bf16(__uint_as_float(r[2]) * inv, __uint_as_float(r[3]) * inv);
+            v0.z = pack_bf16(__uint_as_float(r[4]) * inv, __uint_as_float(r[5]) * inv);
+            v0.w = pack_bf16(__uint_as_float(r[6]) * inv, __uint_as_float(r[7]) * inv);
+            v1.x = pack_bf16(__uint_as_float(r[8]) * inv, __uint_as_float(r[9]) * inv);
+            v1.y = pack_bf16(__uint_as_float(r[10]) * inv, __uint_as_float(r[11]) * inv);
+            v1.z = pack_bf16(__uint_as_float(r[12]) * inv, __uint_as_float(r[13]) * inv);
+            v1.w = pack_bf16(__uint_as_float(r[14]) * inv, __uint_as_float(r[15]) * inv);
+            const int kb = cc / 64, ch = (cc % 64) / 8;
+            uint8_t* blk = pbuf + kb * (BM * 128) + row * 128;
+            uint4* p0 = reinterpret_cast<uint4*>(blk + ((ch ^ (row & 7)) * 16));
+            uint4* p1 = reinterpret_cast<uint4*>(blk + (((ch + 1) ^ (row & 7)) * 16));
+            if (fuse_d) dsum += dot_bf16x8(v0, *p0) + dot_bf16x8(v1, *p1);  // dO, then O over it
+            *p0 = v0;
+            *p1 = v1;
+          }
         }
         tc_fence_before();
         mbar_arrive(BAR_OE(x));  // O_X may be overwritten by the next unit
