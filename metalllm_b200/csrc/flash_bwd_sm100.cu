@@ -21,16 +21,20 @@
 // accumulated in fp32 by the bulk reductions of every key tile, so the
 // launcher zeroes it first (the reference's host zeroes it, model.h:549).
 //
-// Scheduling: units are ordered (batch, head)-major, key tiles in order
-// (heaviest first), and dealt in rounds of gridDim.x, alternating direction
-// (CTA c takes position c in even rounds and gridDim.x-1-c in odd ones), so
-// the units in flight share a few (batch, head) Q/dO sets in L2.  For short
-// sequences at D=64 the kernel is persistent (one CTA per SM walks many
-// units): the next unit's K/V (double-buffered), Q/dO tiles and first S^T/dP^T
-// are fetched and computed while the current unit finishes, and a unit's
-// dK/dV epilogue runs after the next unit's first step has been handed to the
-// tensor core; otherwise every CTA takes one unit and the smem goes to a
-// deeper Q/dO ring.
+// Scheduling: units are ordered in blocks of hb (batch, head) pairs, within
+// a block by key tile (heaviest first), then head; hb = 1 is (batch,
+// head)-major.  Short sequences at D=64 (PERSIST): one CTA per SM, hb = 1,
+// units dealt in rounds of gridDim.x in alternating direction (CTA c takes
+// position c in even rounds and gridDim.x-1-c in odd ones), so the units of
+// a head start together and walk different query tiles, and the units in
+// flight share a few heads' Q/dO in L2.  Longer sequences, whose units differ
+// more in size: one CTA per unit; a running CTA takes its own unit and then,
+// by cluster launch control, the units of CTAs that have not started yet, in
+// launch order, so units go greedily to whichever SM is free.  Either way the
+// next unit's K/V, Q/dO tiles and first S^T/dP^T are fetched and computed
+// while the current unit finishes, and a unit's dK/dV epilogue runs after the
+// next unit's first step has been handed to the tensor core.  PERSIST
+// double-buffers K/V; otherwise the smem goes to a deeper Q/dO ring.
 //
 // Roles (384 threads, three warpgroups):
 //   warpgroup 0 (120 registers per thread after setmaxnreg):
@@ -74,7 +78,7 @@ using namespace sm100;
 
 constexpr int BK = 128;  // keys per unit
 constexpr int BQ = 128;  // queries per step
-constexpr int PERSIST_MAX_NKT = 16;  // persistent launch when T/128 <= this (D=64)
+constexpr int PERSIST_MAX_NKT = 16;  // static schedule, double-buffered K/V when T/128 <= this (D=64)
 constexpr float LOG2E = 1.4426950408889634f;
 
 
@@ -139,12 +143,22 @@ struct BwdCfg {
   static constexpr uint32_t OFF_DST = OFF_PT + (P_IN_TMEM ? 0 : PT_BYTES);
   static constexpr uint32_t OFF_DQS = DQS_ALIAS ? OFF_PT : OFF_DST + PT_BYTES;  // [DQSB]
   static constexpr uint32_t OFF_STAT = DQS_ALIAS ? OFF_DST + PT_BYTES : OFF_DQS + DQSB * DQS_BYTES;
-  static constexpr uint32_t OFF_BAR = OFF_STAT + SSTG * STAT_BYTES;
+  // the unit schedule: NSCHED 16-byte launch-control responses, read by the
+  // producer, the UMMA issuer (twice: its look-ahead and current steps), the
+  // statistics and reduce warps, and every compute and drain warp
+  static constexpr bool DYN = !PERSIST;  // units taken by launch control
+  // (batch, head) pairs per block of the unit order (measured: D=128 gains
+  // from 16, D=64 at long sequences is fastest (batch, head)-major)
+  static constexpr int HB = (DYN && !D64) ? 16 : 1;
+  static constexpr int NSCHED = DYN ? (int)kSchedSlots : 0;
+  static constexpr uint32_t SCHED_READERS = 5 + NCOMP / 32 + (DRAIN_WG ? 4 : 0);
+  static constexpr uint32_t OFF_SCHED = OFF_STAT + SSTG * STAT_BYTES;
+  static constexpr uint32_t OFF_BAR = OFF_SCHED + NSCHED * 16;
   // kv_full/empty[KVB], qd_full/empty[S], st_full/empty[8], then s_full,
   // s_free, p_ready, p_free, dq_full, dq_free, dqs_full, dqs_free, done,
   // acc_free, never (nothing arrives: the time-out test hook), fin (the
-  // UMMA issuer's wind-down)
-  static constexpr int NBAR = 2 * KVB + 2 * STAGES + 2 * SSTG + 12 + 2 * (DQSB - 1);
+  // UMMA issuer's wind-down), sched_full/empty[NSCHED]
+  static constexpr int NBAR = 2 * KVB + 2 * STAGES + 2 * SSTG + 12 + 2 * (DQSB - 1) + 2 * NSCHED;
   static constexpr uint32_t OFF_TSLOT = OFF_BAR + NBAR * 8;
   static constexpr uint32_t SMEM_BYTES = OFF_TSLOT + 16 + 1024;
   static constexpr uint32_t TCOL_S = 0;
@@ -164,23 +178,35 @@ struct BwdParams {
   uint32_t expire_ns;  // time-out test hook (ma_debug_expire_next_wait), 0 = off
 };
 
-// Unit k -> (batch, head, key tile); its query tiles are kt .. nkt-1.
+// Unit k -> (batch, head, key tile); its query tiles are kt .. nkt-1.  Block
+// k / (HB * nkt) holds the units of HB (batch, head) pairs (fewer in the last
+// block), key tile-major; HB = 1 is (batch, head)-major.
 struct BUnit {
   int b, h, kt, nq;
 };
 
+template <int HB>
 __device__ __forceinline__ BUnit bwd_unit(const BwdParams& prm, int k) {
   BUnit u;
-  const int bh = prm.bh_begin + k / prm.nkt;
-  u.kt = k % prm.nkt;
+  int bh;
+  if constexpr (HB > 1) {
+    const int per = HB * prm.nkt;
+    const int blk = k / per, r = k % per;
+    const int hb = min(HB, prm.nbh - blk * HB);
+    bh = prm.bh_begin + blk * HB + r % hb;
+    u.kt = r / hb;
+  } else {
+    bh = prm.bh_begin + k / prm.nkt;
+    u.kt = k % prm.nkt;
+  }
   u.b = bh / prm.NH;
   u.h = bh % prm.NH;
   u.nq = prm.nkt - u.kt;
   return u;
 }
 
-// The unit of this CTA in round g: -1 when rounds are exhausted, -2 when this
-// CTA has none in round g (last, partial round).
+// Static schedule: the unit of this CTA in round g, -1 when rounds are
+// exhausted, -2 when this CTA has none in round g (last, partial round).
 __device__ __forceinline__ int bwd_unit_of_round(const BwdParams& prm, int g) {
   const int G = gridDim.x;
   if ((long long)g * G >= prm.nunits) return -1;
@@ -192,7 +218,7 @@ __device__ __forceinline__ int bwd_unit_of_round(const BwdParams& prm, int g) {
 // Walks this CTA's (unit, query tile) steps in order.  t counts steps over
 // all units, uc counts units.
 struct StepIter {
-  int g;        // next round to look at
+  int g;        // dynamic: units fetched; static: next round to look at
   BUnit u;
   int i;        // query tile index within the unit
   uint32_t t;   // global step
@@ -200,29 +226,39 @@ struct StepIter {
   bool valid;
 };
 
-__device__ __forceinline__ bool next_unit(const BwdParams& prm, StepIter& s) {
-  for (;;) {
-    const int k = bwd_unit_of_round(prm, s.g);
-    if (k == -1) return false;
-    ++s.g;
-    if (k >= 0) {
-      s.u = bwd_unit(prm, k);
-      return true;
+template <bool DYN, int HB, bool WARP>
+__device__ __forceinline__ bool next_unit(const BwdParams& prm, StepIter& s, const Sched& sc) {
+  if constexpr (DYN) {
+    const int k = sched_unit<WARP>(sc, (uint32_t)s.g++);
+    if (k < 0 || k >= prm.nunits) return false;
+    s.u = bwd_unit<HB>(prm, k);
+    return true;
+  } else {
+    for (;;) {
+      const int k = bwd_unit_of_round(prm, s.g);
+      if (k == -1) return false;
+      ++s.g;
+      if (k >= 0) {
+        s.u = bwd_unit<HB>(prm, k);
+        return true;
+      }
     }
   }
 }
 
-__device__ __forceinline__ StepIter first_step(const BwdParams& prm) {
+template <bool DYN, int HB, bool WARP>
+__device__ __forceinline__ StepIter first_step(const BwdParams& prm, const Sched& sc) {
   StepIter s;
   s.g = 0;
   s.i = 0;
   s.t = 0;
   s.uc = 0;
-  s.valid = next_unit(prm, s);
+  s.valid = next_unit<DYN, HB, WARP>(prm, s, sc);
   return s;
 }
 
-__device__ __forceinline__ void advance(const BwdParams& prm, StepIter& s) {
+template <bool DYN, int HB, bool WARP>
+__device__ __forceinline__ void advance(const BwdParams& prm, StepIter& s, const Sched& sc) {
   ++s.t;
   if (s.i + 1 < s.u.nq) {
     ++s.i;
@@ -230,7 +266,7 @@ __device__ __forceinline__ void advance(const BwdParams& prm, StepIter& s) {
   }
   s.i = 0;
   ++s.uc;
-  s.valid = next_unit(prm, s);
+  s.valid = next_unit<DYN, HB, WARP>(prm, s, sc);
 }
 
 // P^T and dS^T for N query columns of one key row.  s[] holds S^T on entry
@@ -320,6 +356,8 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
   const uint32_t BAR_ACC = BAR_SF + 72;   // dK/dV TMEM read by the epilogue
   const uint32_t BAR_NEVER = BAR_SF + 80; // nothing arrives (time-out test hook)
   const uint32_t BAR_FIN = BAR_SF + 88;   // the UMMA issuer's last commit (wind-down)
+  const uint32_t BAR_UF = BAR_SF + 96 + 16u * (C::DQSB - 1);  // sched_full[NSCHED], then sched_empty
+  const uint32_t BAR_UE = BAR_UF + 8u * C::NSCHED;
   const uint32_t tslot = sbase + C::OFF_TSLOT;
   float* stat_base = reinterpret_cast<float*>(gbase + C::OFF_STAT);
 
@@ -351,6 +389,10 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
     mbar_init(BAR_ACC, C::NACC);
     mbar_init(BAR_NEVER, 1);
     mbar_init(BAR_FIN, 1);
+    for (int u = 0; u < C::NSCHED; ++u) {
+      mbar_init(BAR_UF + 8u * u, 1);
+      mbar_init(BAR_UE + 8u * u, C::SCHED_READERS);
+    }
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -362,6 +404,7 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(gbase + C::OFF_TSLOT);
   volatile int* abort_p = &abort_flag;
+  const Sched sch{sbase + C::OFF_SCHED, BAR_UF, BAR_UE, abort_p};  // the unit schedule
 
   if (warp < 4) {
     reg_dealloc<C::REGS_PRODUCER>();
@@ -371,7 +414,8 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
         tma_prefetch_desc(&tmQ);
         tma_prefetch_desc(&tmdO);
         uint32_t kv_armed = 0, q_armed = 0;  // loads issued into each ring
-        for (StepIter s = first_step(prm); s.valid; advance(prm, s)) {
+        uint32_t nreq = 0;                   // launch-control requests issued
+        for (StepIter s = first_step<C::DYN, C::HB, false>(prm, sch); s.valid; advance<C::DYN, C::HB, false>(prm, s, sch)) {
           const int col0 = s.u.h * HD;
           if (s.i == 0) {  // K/V of a new unit
             const int kvs = s.uc % C::KVB;
@@ -396,8 +440,15 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
             tma_load_3d(sbase + C::OFF_DO + st * C::QD_BYTES + kb * BQ * 128, &tmdO, BAR_QF(st),
                         col0 + kb * 64, qt * BQ, s.u.b);
           }
+          // three steps before the unit's end (or at its start), ask for the
+          // next unit, so that every reader finds the answer when it gets there
+          if (C::DYN && s.i == max(0, s.u.nq - 3)) {
+            if (!sched_request(sch, nreq)) break;
+            ++nreq;
+          }
         }
-        if (*abort_p) {  // wind-down: let the loads still in flight land
+        if (*abort_p) {  // wind-down: let the loads and the request still in flight land
+          if (C::DYN) sched_drain(sch, nreq);
           drain_ring(BAR_KF, C::KVB, kv_armed);
           drain_ring(BAR_QF, C::STAGES, q_armed);
         }
@@ -437,20 +488,24 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
           umma_commit(BAR_SF);
           return true;
         };
-        StepIter cur = first_step(prm);
+        StepIter cur = first_step<C::DYN, C::HB, false>(prm, sch);
         StepIter la = cur;  // next step whose S^T/dP^T is to be issued
         bool ok = true;
         if (la.valid) {
           ok = issue_s(la);
-          advance(prm, la);
+          advance<C::DYN, C::HB, false>(prm, la, sch);
         }
         // time-out test hook: with the first products in flight, wait on a
         // barrier nothing arrives at until the hook's limit runs out
         if (ok && prm.expire_ns) ok = mbar_wait(BAR_NEVER, 0, abort_p, prm.expire_ns);
-        for (; ok && cur.valid; advance(prm, cur)) {
-          if (C::EARLY_S && la.valid) {
+        for (; ok && cur.valid; advance<C::DYN, C::HB, false>(prm, cur, sch)) {
+          // the next step's S^T/dP^T ahead of this step's products, except
+          // where it starts a unit whose K/V can only be loaded into the
+          // single K/V buffer once this step's products are done with it
+          const bool early = C::EARLY_S && la.valid && (C::KVB > 1 || la.uc == cur.uc);
+          if (early) {
             if (!issue_s(la)) break;
-            advance(prm, la);
+            advance<C::DYN, C::HB, false>(prm, la, sch);
           }
           const int st = cur.t % C::STAGES;
           const int kvs = cur.uc % C::KVB;
@@ -494,9 +549,10 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
             umma_commit(BAR_KE(kvs));
             umma_commit(BAR_DONE);
           }
-          if (!C::EARLY_S && la.valid) {
+          // (after them: D=128, or a unit start with a single K/V buffer)
+          if ((!C::EARLY_S || C::KVB == 1) && !early && la.valid) {
             if (!issue_s(la)) break;
-            advance(prm, la);
+            advance<C::DYN, C::HB, false>(prm, la, sch);
           }
         }
         if (*abort_p) {  // wind-down: every UMMA issued must complete before TMEM is freed
@@ -525,13 +581,13 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
           }
         }
       };
-      StepIter s = first_step(prm);
+      StepIter s = first_step<C::DYN, C::HB, true>(prm, sch);
       if (s.valid) load_stats(s);
       while (s.valid) {
         const float cl[4] = {nl[0], nl[1], nl[2], nl[3]};
         const float cd[4] = {nd[0], nd[1], nd[2], nd[3]};
         StepIter nx = s;
-        advance(prm, nx);
+        advance<C::DYN, C::HB, true>(prm, nx, sch);
         if (nx.valid) load_stats(nx);  // the next step's, in flight while this one waits
         const int st = s.t % C::SSTG;
         if (s.t >= C::SSTG && !mbar_wait_warp(BAR_TE(st), ((s.t / C::SSTG) - 1) & 1, abort_p)) break;
@@ -547,7 +603,7 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
     } else {
       // ------------------------------------------------- dQ reduce issuer
       if (lane == 0) {
-        for (StepIter s = first_step(prm); s.valid; advance(prm, s)) {
+        for (StepIter s = first_step<C::DYN, C::HB, false>(prm, sch); s.valid; advance<C::DYN, C::HB, false>(prm, s, sch)) {
           const int b = s.t % C::DQSB;
           if (!mbar_wait(BAR_DSF(b), (s.t / C::DQSB) & 1, abort_p)) break;
           for (int box = 0; box < HD / 32; ++box)
@@ -654,7 +710,7 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
     BUnit prev{};
     uint32_t t = 0, uc = 0;
     bool have_prev = false;
-    for (StepIter st_it = first_step(prm); ok && st_it.valid; advance(prm, st_it)) {
+    for (StepIter st_it = first_step<C::DYN, C::HB, true>(prm, sch); ok && st_it.valid; advance<C::DYN, C::HB, true>(prm, st_it, sch)) {
       const BUnit& u = st_it.u;
       const int i = st_it.i;
       t = st_it.t;
@@ -724,17 +780,20 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(BAR_PR);
+      // on a unit's first step the previous unit's dK/dV epilogue comes
+      // first: the UMMA issuer waits for it before this step's products,
+      // the dQ product that drain_dq(t) waits for among them
+      if constexpr (C::EPI_COMPUTE) {
+        if (i == 0 && have_prev) epilogue(prev, uc - 1);
+        prev = u;
+        have_prev = true;
+      }
       if constexpr (!C::DRAIN_WG) {
         if (C::EARLY_S) {
           if (t >= 1) drain_dq(t - 1);
         } else {
           drain_dq(t);
         }
-      }
-      if constexpr (C::EPI_COMPUTE) {
-        if (i == 0 && have_prev) epilogue(prev, uc - 1);
-        prev = u;
-        have_prev = true;
       }
     }
     if (ok && have_prev) {  // the last unit of this CTA
@@ -749,7 +808,7 @@ __global__ void __launch_bounds__(BwdCfg<HD, PERSIST>::NUM_THREADS, 1)
     const int row = quarter * 32 + lane;
     const uint32_t tl = tmem + ((uint32_t)(quarter * 32) << 16);
     bool ok = true;
-    for (StepIter s = first_step(prm); ok && s.valid; advance(prm, s)) {
+    for (StepIter s = first_step<C::DYN, C::HB, true>(prm, sch); ok && s.valid; advance<C::DYN, C::HB, true>(prm, s, sch)) {
       const uint32_t t = s.t;
       const int b = t % C::DQSB;
       uint8_t* dqs = gbase + C::OFF_DQS + b * C::DQS_BYTES;
@@ -863,7 +922,9 @@ cudaError_t launch_bwd(const __nv_bfloat16* dO, const __nv_bfloat16* Dv, const f
   prm.Dv = Dv;
   prm.status = status;
   prm.expire_ns = take_expire_request(STATUS_BWD_TIMEOUT);
-  // persistent (one CTA per SM) for short sequences at D=64, else one unit per CTA
+  // short sequences at D=64: static rounds over one CTA per SM, (batch,
+  // head)-major; otherwise one CTA per unit, the running CTAs taking over the
+  // rest (see bwd_unit)
   if (HD == 64 && prm.nkt <= PERSIST_MAX_NKT) {
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);

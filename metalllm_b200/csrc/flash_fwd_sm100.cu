@@ -4,8 +4,8 @@
 // roles in a persistent kernel.
 //
 // Work unit: one (batch*head, 256-row query pair) = two 128-row query tiles
-// A (rows 256p..256p+127) and B (the next 128 rows), dealt to one CTA per SM
-// (see unit_of_round).  Per key tile j (128 keys) of a unit:
+// A (rows 256p..256p+127) and B (the next 128 rows), heaviest first (see
+// decode_unit).  Per key tile j (128 keys) of a unit:
 //   S_X  = Q_X K_j^T          UMMA 128x128xD, fp32 in TMEM      (X = A, B)
 //   P_X  = exp2(S_X c - m_X)  softmax warpgroup X, c = log2(e)/sqrt(D), bf16
 //   O_X += P_X V_j            UMMA 128xDx128, fp32 in TMEM
@@ -57,7 +57,7 @@ constexpr float LOG2E = 1.4426950408889634f;
 constexpr float LN2 = 0.6931471805599453f;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
 
-template <int HD>
+template <int HD, bool DYN = false>
 struct FwdCfg {
   static constexpr int KB = HD / 64;  // 64-column blocks per row
   static constexpr int QST = HD == 64 ? 2 : 1;  // Q-pair stages
@@ -85,11 +85,15 @@ struct FwdCfg {
   // into dQ when the forward zeroes it for an accumulating backward
   static constexpr uint32_t ZT_BYTES = P_TMEM ? BM * 32 * 4 : 0;
   static constexpr uint32_t OFF_ZT = OFF_P + 2 * STG_BYTES;
-  static constexpr uint32_t OFF_BAR = OFF_ZT + ZT_BYTES;
+  // the unit schedule: NSCHED 16-byte launch-control responses
+  static constexpr int NSCHED = DYN ? (int)kSchedSlots : 0;  // dynamic schedule only
+  static constexpr uint32_t OFF_SCHED = OFF_ZT + ZT_BYTES;
+  static constexpr uint32_t OFF_BAR = OFF_SCHED + NSCHED * 16;
   // q_full/empty[QST], k_full/empty[KST], v_full/empty[VST], per tile X:
   // s_full, s_free, p_full, pv_done, o_free, do_full; then never (nothing
-  // arrives: the time-out test hook) and fin (the UMMA issuer's wind-down)
-  static constexpr int NBAR = 2 * QST + 2 * KST + 2 * VST + 2 * 6 + 2;
+  // arrives: the time-out test hook), fin (the UMMA issuer's wind-down) and
+  // sched_full/empty[NSCHED]
+  static constexpr int NBAR = 2 * QST + 2 * KST + 2 * VST + 2 * 6 + 2 + 2 * NSCHED;
   static constexpr uint32_t OFF_TSLOT = OFF_BAR + NBAR * 8;
   static constexpr uint32_t SMEM_BYTES = OFF_TSLOT + 16 + 1024;  // + alignment slack
   static constexpr uint32_t TCOL_S = 0;     // S_A, S_B at columns 0, 128
@@ -132,11 +136,14 @@ __device__ __forceinline__ float dot_bf16x8(uint4 a, uint4 b) {
 }
 
 // Work units, heaviest first (causal work grows with the pair index):
-// k -> (pair = npairs-1 - k / nbh, bh = bh_begin + k % nbh), dealt in rounds
-// of G = gridDim.x in alternating direction: in round g CTA c takes
-// k = g*G + c for even g and g*G + G-1-c for odd g, which balances the
-// decreasing unit sizes across CTAs (a CTA with a large unit in one round
-// gets a small one in the next).
+// k -> (pair = npairs-1 - k / nbh, bh = bh_begin + k % nbh), dealt in one of
+// two ways.  Static (up to 16 query tiles): one CTA per SM, units in rounds of
+// G = gridDim.x in alternating direction (round g gives CTA c unit g*G + c
+// for even g and g*G + G-1-c for odd g), which balances the decreasing unit
+// sizes across CTAs.  Dynamic (longer sequences, whose units differ more in
+// size): one CTA per unit; a running CTA takes its own unit (k = blockIdx.x)
+// and then, by cluster launch control, the units of CTAs that have not
+// started yet, in launch order, so units go greedily to whichever SM is free.
 struct Unit {
   int pair, b, h, nA, nB, nkv;
 };
@@ -153,7 +160,7 @@ __device__ __forceinline__ Unit decode_unit(const FwdParams& prm, int k) {
   return x;
 }
 
-// The g-th unit of this CTA, or -1 when it has none left.
+// Static schedule: the g-th unit of this CTA, or -1 when it has none left.
 __device__ __forceinline__ int unit_of_round(const FwdParams& prm, int g) {
   const int G = gridDim.x;
   const long long k = (long long)g * G + ((g & 1) ? G - 1 - (int)blockIdx.x : (int)blockIdx.x);
@@ -161,14 +168,14 @@ __device__ __forceinline__ int unit_of_round(const FwdParams& prm, int g) {
   return k < prm.nunits ? (int)k : -1;
 }
 
-template <int HD>
+template <int HD, bool DYN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
                      const __grid_constant__ CUtensorMap tmdO, const __grid_constant__ CUtensorMap tmdQz,
                      const FwdParams prm) {
   pdl_wait_and_release();
-  using C = FwdCfg<HD>;
+  using C = FwdCfg<HD, DYN>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ int abort_flag;
   const uint32_t raw = smem_u32(smem_raw);
@@ -193,6 +200,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   auto BAR_DO = [&](int x) { return barX + 8u * (5 * 2 + x); };  // dO tile of X landed (fused computeD)
   const uint32_t BAR_NEVER = barX + 8u * 12;  // nothing arrives (time-out test hook)
   const uint32_t BAR_FIN = barX + 8u * 13;    // the UMMA issuer's last commit (wind-down)
+  auto BAR_UF = [&](int s) { return barX + 8u * (14 + s); };              // response s landed
+  auto BAR_UE = [&](int s) { return barX + 8u * (14 + C::NSCHED + s); };  // response s read by all
+  // dynamic schedule: unit g >= 1 of this CTA is the one launch-control
+  // response g-1 names (requested by the TMA producer when it starts unit
+  // g-1); readers: the producer, the UMMA issuer and the 8 softmax warps
+  constexpr uint32_t SCHED_READERS = 10;
   const uint32_t tslot = sbase + C::OFF_TSLOT;
 
   if (threadIdx.x == 0) {
@@ -219,6 +232,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     mbar_init(BAR_NEVER, 1);
     mbar_init(BAR_FIN, 1);
+    for (int u = 0; u < C::NSCHED; ++u) {
+      mbar_init(BAR_UF(u), 1);
+      mbar_init(BAR_UE(u), SCHED_READERS);
+    }
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -235,6 +252,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(gbase + C::OFF_TSLOT);
   volatile int* abort_p = &abort_flag;
+  const Sched sch{sbase + C::OFF_SCHED, BAR_UF(0), BAR_UE(0), abort_p};
 
   if (warp < 4) {
     reg_dealloc<REGS_PRODUCER>();
@@ -244,10 +262,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
       uint32_t qc = 0, kc = 0, vc = 0;
+      uint32_t nreq = 0;  // launch-control requests issued (request r names unit r+1)
       bool ok = true;
       for (int g = 0; ok; ++g) {
-        const int k = unit_of_round(prm, g);
+        int k;
+        if constexpr (DYN) k = sched_unit<false>(sch, g);
+        else k = unit_of_round(prm, g);
         if (k < 0) break;
+        // dynamic: request unit g+1 now, a unit ahead of every reader
+        if constexpr (DYN) {
+          if (!sched_request(sch, nreq)) break;
+          ++nreq;
+        }
         const Unit un = decode_unit(prm, k);
         const int col0 = un.h * HD;
         const int qs = qc % C::QST;
@@ -276,7 +302,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           ++vc;
         }
       }
-      if (*abort_p) {  // wind-down: let the loads still in flight land
+      if (*abort_p) {  // wind-down: let the loads and the request still in flight land
+        if (DYN) sched_drain(sch, nreq);
         drain_ring(BAR_QF, C::QST, qc);
         drain_ring(BAR_KF, C::KST, kc);
         drain_ring(BAR_VF, C::VST, vc);
@@ -291,7 +318,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t uc[2] = {0, 0};   // units in which tile X was active
       bool ok = true;
       for (int g = 0; ok; ++g) {
-        const int k = unit_of_round(prm, g);
+        int k;
+        if constexpr (DYN) k = sched_unit<false>(sch, g);
+        else k = unit_of_round(prm, g);
         if (k < 0) break;
         const Unit un = decode_unit(prm, k);
         const int n[2] = {un.nA, un.nB};
@@ -407,7 +436,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint32_t nd_armed = 0;  // dO tile loads issued (leader)
     bool ok = true;
     for (int g = 0; ok; ++g) {
-      const int k = unit_of_round(prm, g);
+      int k;
+      if constexpr (DYN) k = sched_unit<true>(sch, g);
+      else k = unit_of_round(prm, g);
       if (k < 0) break;
       const Unit un = decode_unit(prm, k);
       const int nt = x == 0 ? un.nA : un.nB;
@@ -640,20 +671,42 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (threadIdx.x == 0 && abort_flag) atomicOr(prm.status, STATUS_FWD_TIMEOUT);
 }
 
+// Launches the instantiation DYN (dynamic schedule: one CTA per unit, else
+// one per SM).
+template <int HD, bool DYN>
+cudaError_t launch_fwd_kernel(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                              const CUtensorMap& to, const CUtensorMap& tdo, const CUtensorMap& tdqz,
+                              const FwdParams& prm, cudaStream_t st) {
+  using C = FwdCfg<HD, DYN>;
+  // The setmaxnreg split assumes the kernel was compiled to exactly
+  // LAUNCH_REGS registers per thread; refuse to launch otherwise.
+  static const cudaError_t reg_check = [] {
+    cudaFuncAttributes a;
+    cudaError_t e = cudaFuncGetAttributes(&a, flash_fwd_kernel<HD, DYN>);
+    if (e != cudaSuccess) return e;
+    return a.numRegs == LAUNCH_REGS ? cudaSuccess : cudaErrorInvalidKernelImage;
+  }();
+  if (reg_check != cudaSuccess) return reg_check;
+  cudaError_t e = cudaFuncSetAttribute(flash_fwd_kernel<HD, DYN>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+  if (e != cudaSuccess) return e;
+  int grid = prm.nunits;  // dynamic: one CTA per unit (see decode_unit)
+  if (!DYN) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    grid = prm.nunits < sms ? prm.nunits : sms;
+  }
+  launch_pdl(flash_fwd_kernel<HD, DYN>, grid, NUM_THREADS, C::SMEM_BYTES, st, tq, tk, tv, to, tdo, tdqz, prm);
+  count_launches(1);
+  return cudaGetLastError();
+}
+
 template <int HD>
 cudaError_t launch_fwd(const __nv_bfloat16* q, const __nv_bfloat16* k, const __nv_bfloat16* v,
                        __nv_bfloat16* out, float* lse, const AttnShape& s, uint32_t* status,
                        cudaStream_t st, const __nv_bfloat16* dO, __nv_bfloat16* Dv, float* dQz) {
   using C = FwdCfg<HD>;
-  // The setmaxnreg split assumes the kernel was compiled to exactly
-  // LAUNCH_REGS registers per thread; refuse to launch otherwise.
-  static const cudaError_t reg_check = [] {
-    cudaFuncAttributes a;
-    cudaError_t e = cudaFuncGetAttributes(&a, flash_fwd_kernel<HD>);
-    if (e != cudaSuccess) return e;
-    return a.numRegs == LAUNCH_REGS ? cudaSuccess : cudaErrorInvalidKernelImage;
-  }();
-  if (reg_check != cudaSuccess) return reg_check;
   CUtensorMap tq, tk, tv, to, tdo, tdqz;
   const CUtensorMapDataType bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B;
@@ -689,16 +742,9 @@ cudaError_t launch_fwd(const __nv_bfloat16* q, const __nv_bfloat16* k, const __n
   prm.D = Dv;
   prm.dQz = C::ZT_BYTES ? dQz : nullptr;
   prm.expire_ns = take_expire_request(STATUS_FWD_TIMEOUT);
-  cudaError_t e = cudaFuncSetAttribute(flash_fwd_kernel<HD>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
-  if (e != cudaSuccess) return e;
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int grid = prm.nunits < sms ? prm.nunits : sms;
-  launch_pdl(flash_fwd_kernel<HD>, grid, NUM_THREADS, C::SMEM_BYTES, st, tq, tk, tv, to, tdo, tdqz, prm);
-  count_launches(1);
-  return cudaGetLastError();
+  // static rounds up to 16 query tiles, the dynamic schedule beyond
+  if (prm.nqt > 16) return launch_fwd_kernel<HD, true>(tq, tk, tv, to, tdo, tdqz, prm, st);
+  return launch_fwd_kernel<HD, false>(tq, tk, tv, to, tdo, tdqz, prm, st);
 }
 
 }  // namespace

@@ -151,6 +151,90 @@ __device__ __forceinline__ void bar_sync_named(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// ------------------------------------------------- cluster launch control
+// A persistent-style kernel launched with one CTA per work unit: a running
+// CTA asks the hardware to cancel the launch of a CTA that has not started
+// yet and takes over its unit, so fast SMs take more units and the grid ends
+// when the work does.  The 16-byte response lands in shared memory at `resp`
+// (16-byte aligned) and completes `bar`, which the caller armed for 16 bytes.
+__device__ __forceinline__ void clc_try_cancel(uint32_t resp, uint32_t bar) {
+  asm volatile(
+      "clusterlaunchcontrol.try_cancel.async.shared::cta.mbarrier::complete_tx::bytes.b128 [%0], [%1];" ::"r"(resp),
+      "r"(bar)
+      : "memory");
+}
+
+// The x index of the CTA a completed response cancelled, or -1 when it
+// cancelled none (no CTA was left to launch: the grid's work is all taken).
+__device__ __forceinline__ int clc_cancelled_x(uint32_t resp) {
+  uint64_t lo, hi;
+  asm volatile("ld.shared.v2.u64 {%0, %1}, [%2];" : "=l"(lo), "=l"(hi) : "r"(resp) : "memory");
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .b128 rr;\n\t.reg .pred p;\n\t"
+      "mov.b128 rr, {%1, %2};\n\t"
+      "clusterlaunchcontrol.query_cancel.is_canceled.pred.b128 p, rr;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "l"(lo), "l"(hi));
+  if (!ok) return -1;
+  uint32_t x;
+  asm volatile(
+      "{\n\t.reg .b128 rr;\n\t"
+      "mov.b128 rr, {%1, %2};\n\t"
+      "clusterlaunchcontrol.query_cancel.get_first_ctaid::x.b32.b128 %0, rr;\n\t}"
+      : "=r"(x)
+      : "l"(lo), "l"(hi));
+  return (int)x;
+}
+
+// The unit sequence of a CTA scheduled by launch control: unit 0 is its own
+// (blockIdx.x); unit g >= 1 is the one response g-1 names, in slot
+// (g-1) % kSchedSlots of a ring of 16-byte responses with a full barrier (the
+// requester's) and an empty barrier (one arrival per reader) per slot.
+constexpr uint32_t kSchedSlots = 4;
+
+struct Sched {
+  uint32_t resp;         // slot 0's response; slot u at resp + 16u
+  uint32_t full, empty;  // slot 0's barriers; slot u at + 8u
+  volatile int* abort;
+};
+
+// Unit g of the sequence, or -1 when there is none (or a wait timed out:
+// the abort flag is then set).  Every reader calls it once per g, in order;
+// WARP: a whole warp reads (lane 0 releases the slot), else one thread.
+template <bool WARP>
+__device__ __forceinline__ int sched_unit(const Sched& sc, uint32_t g) {
+  if (g == 0) return (int)blockIdx.x;
+  const uint32_t u = (g - 1) % kSchedSlots, ph = ((g - 1) / kSchedSlots) & 1u;
+  if (!(WARP ? mbar_wait_warp(sc.full + 8u * u, ph, sc.abort) : mbar_wait(sc.full + 8u * u, ph, sc.abort)))
+    return -1;
+  const int k = clc_cancelled_x(sc.resp + 16u * u);
+  if (WARP) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(sc.empty + 8u * u);
+  } else {
+    mbar_arrive(sc.empty + 8u * u);
+  }
+  return k;
+}
+
+// The requester's side: request r (naming unit r+1) into slot r % kSchedSlots,
+// once every reader has released the slot's previous response.
+__device__ __forceinline__ bool sched_request(const Sched& sc, uint32_t r) {
+  const uint32_t u = r % kSchedSlots;
+  if (r >= kSchedSlots && !mbar_wait(sc.empty + 8u * u, ((r / kSchedSlots) - 1) & 1u, sc.abort)) return false;
+  mbar_arrive_expect_tx(sc.full + 8u * u, 16);
+  clc_try_cancel(sc.resp + 16u * u, sc.full + 8u * u);
+  return true;
+}
+
+// After a time-out: lets the last request still in flight land.
+__device__ __forceinline__ void sched_drain(const Sched& sc, uint32_t nreq) {
+  if (nreq > 0)
+    mbar_wait_for(sc.full + 8u * ((nreq - 1) % kSchedSlots), ((nreq - 1) / kSchedSlots) & 1u, kDrainLimitNs);
+}
+
 // ------------------------------------------------------------------ TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
