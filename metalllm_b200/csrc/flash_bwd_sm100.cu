@@ -18,23 +18,27 @@
 // TMEM (bf16 pairs) and dV's UMMA takes it from there; at D=128 TMEM is full
 // and P^T goes to shared memory like dS^T.  dK/dV are owned by the unit and
 // stored once (bf16, straight from registers to global memory); dQ is
-// accumulated in fp32 by the bulk reductions of every key tile, so the
-// launcher zeroes it first (the reference's host zeroes it, model.h:549).
+// accumulated in fp32 by the bulk reductions of every key tile into zeros:
+// the launcher writes them first, unless the caller passes a dQ that already
+// holds them (the accumulating entry point; the reference's host zeroes dQ,
+// model.h:549).
 //
-// Scheduling: units are ordered in blocks of hb (batch, head) pairs, within
-// a block by key tile (heaviest first), then head; hb = 1 is (batch,
-// head)-major.  Short sequences at D=64 (PERSIST): one CTA per SM, hb = 1,
+// Scheduling: units are ordered in blocks of HB (batch, head) pairs, within
+// a block by key tile (heaviest first), then head; HB = 1 is (batch,
+// head)-major.  Short sequences at D=64 (PERSIST): one CTA per SM, HB = 1,
 // units dealt in rounds of gridDim.x in alternating direction (CTA c takes
 // position c in even rounds and gridDim.x-1-c in odd ones), so the units of
 // a head start together and walk different query tiles, and the units in
 // flight share a few heads' Q/dO in L2.  Longer sequences, whose units differ
 // more in size: one CTA per unit; a running CTA takes its own unit and then,
 // by cluster launch control, the units of CTAs that have not started yet, in
-// launch order, so units go greedily to whichever SM is free.  Either way the
-// next unit's K/V, Q/dO tiles and first S^T/dP^T are fetched and computed
-// while the current unit finishes, and a unit's dK/dV epilogue runs after the
-// next unit's first step has been handed to the tensor core.  PERSIST
-// double-buffers K/V; otherwise the smem goes to a deeper Q/dO ring.
+// launch order, so units go greedily to whichever SM is free.  Either way a
+// unit's dK/dV epilogue runs after the next unit's first step has been handed
+// to the tensor core.  PERSIST double-buffers K/V, so the next unit's K/V,
+// Q/dO tiles and first S^T/dP^T are fetched and computed while the current
+// unit finishes; otherwise the smem goes to a deeper Q/dO ring and the next
+// unit's K/V load and first S^T/dP^T wait for the current unit's last
+// products.
 //
 // Roles (384 threads, three warpgroups):
 //   warpgroup 0 (120 registers per thread after setmaxnreg):

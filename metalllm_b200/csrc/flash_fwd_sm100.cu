@@ -1,7 +1,8 @@
 // flash_fwd_sm100.cu -- flashAttentionForward (attention.metal:56-164) on
 // sm_100a: tcgen05 UMMA with TMEM accumulators, TMA-staged Q/K/V tiles in
 // 128-byte-swizzled shared memory, an mbarrier pipeline and warp-specialised
-// roles in a persistent kernel.
+// roles; each CTA walks many work units (static rounds, or launch control for
+// long sequences: see decode_unit).
 //
 // Work unit: one (batch*head, 256-row query pair) = two 128-row query tiles
 // A (rows 256p..256p+127) and B (the next 128 rows), heaviest first (see
