@@ -103,6 +103,9 @@ SHAPES = [
     # on load and clipped on store, per batch row)
     (1, 1, 1, 64), (2, 100, 2, 64), (3, 200, 3, 64), (2, 130, 2, 128), (1, 257, 2, 128),
     (2, 1000, 1, 64),
+    # more than 16 tiles: both kernels deal their units by cluster launch
+    # control (one CTA per unit) instead of static rounds
+    (1, 2200, 2, 64), (1, 2113, 1, 128),
 ]
 
 
@@ -317,7 +320,8 @@ def test_full_config_every_shard(A, oracle_mod, cfg):
 
 
 @pytest.mark.parametrize("B,T,H,D,shard", [(2, 512, 3, 64, None), (3, 200, 2, 64, (1, 5)),
-                                         (2, 130, 3, 128, None), (2, 256, 2, 128, (1, 3))])
+                                         (2, 130, 3, 128, None), (2, 256, 2, 128, (1, 3)),
+                                         (2, 2200, 2, 64, (1, 3))])
 def test_forward_zero_dq_and_accumulating_backward(A, B, T, H, D, shard):
     """ma_flashAttentionForwardComputeDZeroDQ writes out, l, D bit-identical
     to ma_flashAttentionForwardComputeD and exact zeros to dQ on the

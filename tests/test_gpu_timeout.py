@@ -56,12 +56,15 @@ def _same(a, b):
     assert torch.allclose(a[3], b[3], rtol=1e-5, atol=1e-5)
 
 
-# (which kernel, head size, sequence length): the persistent d=64 backward,
-# the one-unit-per-CTA d=128 backward, both forwards, and the forward with
-# computeD fused at T=256, where the unit's diagonal tile is its first, so
-# the dO tile load is in flight when the wait runs out
-CASES = [("bwd", 64, 512), ("bwd", 128, 512), ("fwd", 64, 512), ("fwd", 128, 512),
-         ("fwd_d", 64, 256)]
+# (which kernel, head size, sequence length): the d=64 backward and forward
+# of both schedules (static rounds up to 16 tiles, one CTA per unit under
+# cluster launch control beyond, with a launch-control request in flight
+# when the wait runs out), the d=128 backward (always launch control) and
+# forward, and the forward with computeD fused at T=256, where the unit's
+# diagonal tile is its first, so the dO tile load is in flight when the wait
+# runs out
+CASES = [("bwd", 64, 512), ("bwd", 64, 2304), ("bwd", 128, 512), ("fwd", 64, 512),
+         ("fwd", 64, 2304), ("fwd", 128, 512), ("fwd_d", 64, 256)]
 
 
 @pytest.mark.parametrize("kernel,D,T", CASES, ids=[f"{k}-d{d}-T{t}" for k, d, t in CASES])
