@@ -88,6 +88,10 @@ struct FwdCfg {
   static constexpr uint32_t OFF_ZT = OFF_P + 2 * STG_BYTES;
   // the unit schedule: NSCHED 16-byte launch-control responses
   static constexpr int NSCHED = DYN ? (int)kSchedSlots : 0;  // dynamic schedule only
+  // dynamic schedule's unit order: blocks of HB (batch, head) pairs at D=128
+  // (their query pairs share K/V in L2: C3 forward -4.6 %), one block at D=64
+  // (C4: blocks of 8-32 heads measured 1-2 % slower)
+  static constexpr int HB = (DYN && HD == 128) ? 16 : 0;
   static constexpr uint32_t OFF_SCHED = OFF_ZT + ZT_BYTES;
   static constexpr uint32_t OFF_BAR = OFF_SCHED + NSCHED * 16;
   // q_full/empty[QST], k_full/empty[KST], v_full/empty[VST], per tile X:
@@ -145,14 +149,28 @@ __device__ __forceinline__ float dot_bf16x8(uint4 a, uint4 b) {
 // size): one CTA per unit; a running CTA takes its own unit (k = blockIdx.x)
 // and then, by cluster launch control, the units of CTAs that have not
 // started yet, in launch order, so units go greedily to whichever SM is free.
+// With HB > 0 (the dynamic schedule at D=128) the order is blocked instead:
+// block k / (HB*npairs) holds HB (batch, head) pairs (fewer in the last
+// block), heaviest pair first within it, so the units in flight share their
+// heads' K/V tiles in L2 and the grid still ends on light units.
 struct Unit {
   int pair, b, h, nA, nB, nkv;
 };
 
+template <int HB>
 __device__ __forceinline__ Unit decode_unit(const FwdParams& prm, int k) {
   Unit x;
-  x.pair = prm.npairs - 1 - k / prm.nbh;
-  const int bh = prm.bh_begin + k % prm.nbh;
+  int bh;
+  if constexpr (HB > 0) {  // blocks of HB (batch, head) pairs, heaviest pair first in each
+    const int per = HB * prm.npairs;
+    const int blk = k / per, r = k % per;
+    const int hb = min(HB, prm.nbh - blk * HB);
+    x.pair = prm.npairs - 1 - r / hb;
+    bh = prm.bh_begin + blk * HB + r % hb;
+  } else {
+    x.pair = prm.npairs - 1 - k / prm.nbh;
+    bh = prm.bh_begin + k % prm.nbh;
+  }
   x.b = bh / prm.NH;
   x.h = bh % prm.NH;
   x.nA = 2 * x.pair + 1;                                   // key tiles 0..2p
@@ -275,7 +293,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (!sched_request(sch, nreq)) break;
           ++nreq;
         }
-        const Unit un = decode_unit(prm, k);
+        const Unit un = decode_unit<C::HB>(prm, k);
         const int col0 = un.h * HD;
         const int qs = qc % C::QST;
         if (qc >= C::QST && !mbar_wait(BAR_QE(qs), ((qc / C::QST) - 1) & 1, abort_p)) break;
@@ -323,7 +341,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if constexpr (DYN) k = sched_unit<false>(sch, g);
         else k = unit_of_round(prm, g);
         if (k < 0) break;
-        const Unit un = decode_unit(prm, k);
+        const Unit un = decode_unit<C::HB>(prm, k);
         const int n[2] = {un.nA, un.nB};
         const int qs = qc % C::QST;
         if (!mbar_wait(BAR_QF(qs), (qc / C::QST) & 1, abort_p)) break;
@@ -441,7 +459,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if constexpr (DYN) k = sched_unit<true>(sch, g);
       else k = unit_of_round(prm, g);
       if (k < 0) break;
-      const Unit un = decode_unit(prm, k);
+      const Unit un = decode_unit<C::HB>(prm, k);
       const int nt = x == 0 ? un.nA : un.nB;
       if (nt == 0) continue;
       const int qtile = 2 * un.pair + x;
