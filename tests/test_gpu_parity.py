@@ -222,6 +222,62 @@ def test_determinism(A):
     check("dQ rerun", f32(r1[3]), f32(r2[3]), 1e-5, 1e-6)
 
 
+@pytest.mark.parametrize("B,T,H,D", [(2, 512, 2, 64), (1, 2304, 2, 64), (1, 1024, 2, 128)])
+def test_replay_from_a_cuda_graph(A, B, T, H, D):
+    """The attention step captured once into a CUDA graph and replayed twice
+    gives the eager results: the plain chain (forward, computeD, backward) and
+    the bench's two launches (forward with computeD and dQ's zeros, backward
+    accumulating into dQ), under both schedules (static rounds at T=512;
+    cluster launch control for both kernels at T=2304 and for the d=128
+    backward)."""
+    q, k, v, do = inputs(B, T, H, D, seed=41)
+    ref = gpu_chain(A, q, k, v, do, B, T, H, D)
+    p = A.make_params(T, H, D)
+    tq, tk, tv, tdo = up(q), up(k), up(v), up(do)
+    act, rows = (B, T, H * D), (B, T, H)
+    new = lambda shp, dt: torch.full(shp, float("nan"), dtype=dt, device="cuda")
+    bufs = [new(act, torch.bfloat16), new(rows, torch.float32), new(rows, torch.bfloat16),
+            new(act, torch.float32), new(act, torch.bfloat16), new(act, torch.bfloat16)]
+    fused = [new(act, torch.bfloat16), new(rows, torch.float32), new(rows, torch.bfloat16),
+             new(act, torch.float32), new(act, torch.bfloat16), new(act, torch.bfloat16)]
+
+    def step():
+        out, l, Dv, dQ, dK, dV = bufs
+        A.flashAttentionForward(tq, tk, tv, p, B, out=out, l=l)
+        A.computeD(tdo, out, p, B, D=Dv)
+        A.flashAttentionBackward(tdo, Dv, l, tq, tk, tv, p, B, dQ=dQ, dK=dK, dV=dV)
+        out, l, Dv, dQ, dK, dV = fused
+        A.flashAttentionForwardComputeD(tq, tk, tv, tdo, p, B, out=out, l=l, D=Dv, zero_dQ=dQ)
+        A.flashAttentionBackward(tdo, Dv, l, tq, tk, tv, p, B, dQ=dQ, dK=dK, dV=dV, accumulate_dQ=True)
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):  # eager warm-up outside the capture
+        step()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    # the eager results: the plain chain is the one gpu_chain runs (dQ to
+    # fp32 rounding: its partial sums arrive in no fixed order); the fused
+    # chain's D may differ from computeD's by one bf16 step, and dK, dQ with it
+    for i in (0, 1, 2, 4, 5):
+        assert torch.equal(bufs[i], ref[i]), i
+    check("dQ plain", f32(bufs[3]), f32(ref[3]), 1e-4, 1e-5)
+    eager = [[t.clone() for t in bufs], [t.clone() for t in fused]]
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+    for _ in range(2):
+        for b in bufs + fused:
+            b.fill_(float("nan"))
+        g.replay()
+        torch.cuda.synchronize()
+        assert A.device_status() == 0
+        for got, want in zip((bufs, fused), eager):
+            for i in (0, 1, 2, 4, 5):
+                assert torch.equal(got[i], want[i]), i
+            check("dQ replay", f32(got[3]), f32(want[3]), 1e-4, 1e-5)
+
+
 @pytest.mark.parametrize("B,M,H,D", [
     (2, 256, 6, 64),     # N = 384 (128-column tiles)
     (1, 64, 3, 64),      # N = 192 (64-column tiles), one partial row tile
